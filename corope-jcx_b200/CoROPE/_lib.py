@@ -1,0 +1,218 @@
+"""ctypes binding of libcorope_b200.so (the C ABI declared in include/corope.h).
+
+The shared library is looked up next to this file (built in-tree by
+``corope-jcx_b200/build.py``).  There is no fallback: if the library or a
+CUDA device is missing, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import threading
+from typing import Optional
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libcorope_b200.so")
+
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+ALGO_AUTO, ALGO_EXACT, ALGO_TENSOR = 0, 1, 2
+_ALGOS = {"auto": ALGO_AUTO, "exact": ALGO_EXACT, "tensor": ALGO_TENSOR}
+
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_DEVICE = range(6)
+
+_I64x3 = ctypes.c_int64 * 3
+
+
+class FwdParams(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p),
+        ("m", ctypes.c_void_p), ("l", ctypes.c_void_p), ("a", ctypes.c_void_p),
+        ("lse", ctypes.c_void_p),
+        ("thetas", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p), ("bias_row_stride", ctypes.c_int64),
+        ("q_stride", _I64x3), ("k_stride", _I64x3), ("v_stride", _I64x3),
+        ("o_stride", _I64x3),
+        ("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+        ("sm_scale", ctypes.c_float), ("theta", ctypes.c_float),
+        ("causal", ctypes.c_int32), ("dtype", ctypes.c_int32), ("algo", ctypes.c_int32),
+    ]
+
+
+class BwdParams(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p), ("dout", ctypes.c_void_p),
+        ("m", ctypes.c_void_p), ("l", ctypes.c_void_p), ("a", ctypes.c_void_p),
+        ("thetas", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p), ("bias_row_stride", ctypes.c_int64),
+        ("dq", ctypes.c_void_p), ("dk", ctypes.c_void_p), ("dv", ctypes.c_void_p),
+        ("q_stride", _I64x3), ("k_stride", _I64x3), ("v_stride", _I64x3),
+        ("o_stride", _I64x3), ("do_stride", _I64x3),
+        ("dq_stride", _I64x3), ("dk_stride", _I64x3), ("dv_stride", _I64x3),
+        ("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+        ("sm_scale", ctypes.c_float), ("theta", ctypes.c_float),
+        ("causal", ctypes.c_int32), ("dtype", ctypes.c_int32), ("algo", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load_library():
+    """Load (once) and return the ctypes handle; raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"CoROPE CUDA library not found at {LIB_PATH}; build it with "
+                    "`python corope-jcx_b200/build.py` (no CPU fallback exists)")
+            lib = ctypes.CDLL(LIB_PATH)
+            lib.corope_fwd.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_void_p]
+            lib.corope_fwd.restype = ctypes.c_int
+            lib.corope_mqa_fwd.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_void_p]
+            lib.corope_mqa_fwd.restype = ctypes.c_int
+            lib.corope_bwd.argtypes = [ctypes.POINTER(BwdParams), ctypes.c_void_p]
+            lib.corope_bwd.restype = ctypes.c_int
+            lib.corope_bwd_workspace_bytes.argtypes = [ctypes.POINTER(BwdParams)]
+            lib.corope_bwd_workspace_bytes.restype = ctypes.c_size_t
+            lib.corope_last_error.argtypes = []
+            lib.corope_last_error.restype = ctypes.c_char_p
+            lib.corope_params_size.argtypes = [ctypes.c_int]
+            lib.corope_params_size.restype = ctypes.c_size_t
+            lib.corope_abi_version.argtypes = []
+            lib.corope_abi_version.restype = ctypes.c_int
+            _lib = lib
+    return _lib
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return DTYPE_F32
+    if t.dtype == torch.float16:
+        return DTYPE_F16
+    if t.dtype == torch.bfloat16:
+        return DTYPE_BF16
+    raise TypeError(f"CoRoPE kernels support float32/float16/bfloat16, got {t.dtype}")
+
+
+def _rowmajor(t: torch.Tensor) -> torch.Tensor:
+    """Last dim contiguous with even strides (pairs are loaded together)."""
+    if t.stride(-1) != 1 or any(s % 2 for s in t.stride()[:3]):
+        t = t.contiguous()
+    return t
+
+
+def _strides(t: torch.Tensor):
+    return _I64x3(t.stride(0), t.stride(1), t.stride(2))
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _check(rc: int, what: str):
+    if rc == OK:
+        return
+    msg = load_library().corope_last_error().decode(errors="replace")
+    if rc == ERR_UNSUPPORTED:
+        raise NotImplementedError(f"{what}: {msg}")
+    if rc == ERR_INVALID:
+        raise ValueError(f"{what}: {msg}")
+    raise RuntimeError(f"{what}: {msg} (status {rc})")
+
+
+def algo_code(algo) -> int:
+    if isinstance(algo, int):
+        return algo
+    try:
+        return _ALGOS[algo]
+    except KeyError:
+        raise ValueError(f"algo must be one of {sorted(_ALGOS)}, got {algo!r}") from None
+
+
+_theta_cache = {}
+
+
+def theta_table(head_dim: int, theta: float, device) -> torch.Tensor:
+    """[D/2] fp32 table ``1 / theta ** (arange(0, D, 2) / D)`` computed with the
+    same torch expression as the reference (CoROPE/forward.py:130-132), on
+    the device, cached per (D, theta, device)."""
+    key = (head_dim, float(theta), str(device))
+    t = _theta_cache.get(key)
+    if t is None:
+        t = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device=device).float() / head_dim))
+        t = t.contiguous()
+        _theta_cache[key] = t
+    return t
+
+
+def default_scale(head_dim: int, sm_scale) -> float:
+    return 1.0 / math.sqrt(head_dim) if sm_scale is None else float(sm_scale)
+
+
+def fwd(q, k, v, o, m, l, a, lse, sm_scale, theta, bias=None, algo="auto", thetas=None,
+        mqa=False):
+    """Launch corope_fwd / corope_mqa_fwd on the current stream of q."""
+    lib = load_library()
+    B, H, S, D = q.shape
+    p = FwdParams()
+    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+    p.m, p.l, p.a, p.lse = _ptr(m), _ptr(l), _ptr(a), _ptr(lse)
+    th = thetas if thetas is not None else theta_table(D, theta, q.device)
+    p.thetas = th.data_ptr()
+    if bias is not None:
+        p.bias = bias.data_ptr()
+        p.bias_row_stride = bias.stride(0)
+    p.q_stride, p.k_stride, p.v_stride, p.o_stride = (_strides(q), _strides(k), _strides(v),
+                                                      _strides(o))
+    p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, k.shape[1], S, D
+    p.sm_scale, p.theta = float(sm_scale), float(theta)
+    p.causal, p.dtype, p.algo = 1, _dtype_code(q), algo_code(algo)
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    fn = lib.corope_mqa_fwd if mqa else lib.corope_fwd
+    with torch.cuda.device(q.device):
+        rc = fn(ctypes.byref(p), ctypes.c_void_p(stream))
+    _check(rc, "corope_mqa_fwd" if mqa else "corope_fwd")
+
+
+def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="auto",
+        thetas=None):
+    """Launch corope_bwd on the current stream of q with a torch-allocated
+    workspace."""
+    lib = load_library()
+    B, H, S, D = q.shape
+    p = BwdParams()
+    p.q, p.k, p.v, p.o, p.dout = (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                  do.data_ptr())
+    p.m, p.l, p.a = m.data_ptr(), l.data_ptr(), a.data_ptr()
+    th = thetas if thetas is not None else theta_table(D, theta, q.device)
+    p.thetas = th.data_ptr()
+    if bias is not None:
+        p.bias = bias.data_ptr()
+        p.bias_row_stride = bias.stride(0)
+    p.dq, p.dk, p.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    p.q_stride, p.k_stride, p.v_stride = _strides(q), _strides(k), _strides(v)
+    p.o_stride, p.do_stride = _strides(o), _strides(do)
+    p.dq_stride, p.dk_stride, p.dv_stride = _strides(dq), _strides(dk), _strides(dv)
+    p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, k.shape[1], S, D
+    p.sm_scale, p.theta = float(sm_scale), float(theta)
+    p.causal, p.dtype, p.algo = 1, _dtype_code(q), algo_code(algo)
+    nbytes = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    with torch.cuda.device(q.device):
+        rc = lib.corope_bwd(ctypes.byref(p), ctypes.c_void_p(stream))
+    _check(rc, "corope_bwd")
+    return ws

@@ -1,0 +1,82 @@
+"""CoRoPE attention backward -- drop-in for the reference's
+``CoROPE/co_rope_backward.py:co_rope_backward``.
+
+Two calling conventions exist in the reference and both are accepted:
+
+* ``co_rope_backward(saved, do, sm_scale=None, theta=10000.0) -> (dq, dk, dv)``
+  (co_rope_backward.py:116-211, used by check.py:134);
+* ``co_rope_backward(q, k, v, o, m, l, a, do, thetas, causal, sm_scale)
+  -> (dq, dk, dv, dthetas)`` (co_rope_attn.py:45-47, benchmark.py:46-48) where
+  ``thetas`` is the repeat-interleaved [H, D] or [D] frequency table and
+  ``dthetas`` is always None (the reference never produces it).
+
+The gradients are those of the reference definition (autograd through
+check.py:44-103); the reference's own Triton backward does not compute them
+(its loop skips the diagonal, uses a block-local cumsum and rotates in the
+opposite direction), so parity is with the definition, not with that kernel.
+K/V with fewer heads than Q (MQA/GQA, from ``co_rope_mqa_forward``) are
+accepted: their gradients are summed over each head group.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .forward import _check_causal
+
+__all__ = ["co_rope_backward"]
+
+
+def _run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo):
+    B, H, S, D = q.shape
+    assert q.is_cuda and k.is_cuda and v.is_cuda, "Inputs must be CUDA tensors"
+    assert k.shape[0] == B and k.shape[2:] == q.shape[2:] and v.shape == k.shape
+    assert do.shape == q.shape and o.shape == q.shape
+    sm_scale = _lib.default_scale(D, sm_scale)
+    q, k, v, o = (_lib._rowmajor(x) for x in (q, k, v, o))
+    do = _lib._rowmajor(do.to(q.dtype))
+    m, l, a = (x.contiguous().float() for x in (m, l, a))
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    for t in (dq, dk, dv):
+        assert t.stride(-1) == 1
+    _lib.bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=bias, algo=algo,
+             thetas=thetas)
+    return dq, dk, dv
+
+
+def co_rope_backward(*args, sm_scale=None, theta=10000.0, thetas=None, causal=True,
+                     contextual_bias=None, algo="auto", **kwargs):
+    if args and isinstance(args[0], (tuple, list)):
+        # (saved, do, sm_scale=None, theta=10000.0)
+        saved, do = args[0], args[1] if len(args) > 1 else kwargs.pop("do")
+        if len(args) > 2:
+            sm_scale = args[2]
+        if len(args) > 3:
+            theta = args[3]
+        q, k, v, o, m, l, a = saved
+        _check_causal(causal)
+        return _run(q, k, v, o, m, l, a, do, sm_scale, theta, None, contextual_bias, algo)
+    # (q, k, v, o, m, l, a, do, thetas, causal, sm_scale)
+    names = ["q", "k", "v", "o", "m", "l", "a", "do", "thetas", "causal", "sm_scale"]
+    vals = dict(zip(names, args))
+    for n in names:
+        if n not in vals and n in kwargs:
+            vals[n] = kwargs.pop(n)
+    if "thetas" not in vals:
+        vals["thetas"] = thetas
+    if "causal" not in vals:
+        vals["causal"] = causal
+    if "sm_scale" not in vals:
+        vals["sm_scale"] = sm_scale
+    _check_causal(vals["causal"])
+    th = vals["thetas"]
+    table = None
+    if th is not None:
+        th = th.reshape(-1, th.shape[-1])[0] if th.dim() > 1 else th
+        # repeat-interleaved [D] -> one entry per pair
+        table = th[0::2].float().contiguous() if th.numel() == vals["q"].shape[-1] else th.float().contiguous()
+    dq, dk, dv = _run(vals["q"], vals["k"], vals["v"], vals["o"], vals["m"], vals["l"], vals["a"],
+                      vals["do"], vals["sm_scale"], theta, table, contextual_bias, algo)
+    return dq, dk, dv, None

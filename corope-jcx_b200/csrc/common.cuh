@@ -1,0 +1,86 @@
+// Shared device helpers for the CoRoPE kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/corope.h"
+
+namespace corope {
+
+// ---- element conversion -------------------------------------------------
+template <typename T> __device__ __forceinline__ float to_f32(T x);
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+// ---- angles ---------------------------------------------------------------
+// sin/cos of x = a * theta (radians, |x| up to ~1e5).  The product is
+// rounded once to fp32, as the reference's `freq = a * thetas` is
+// (check.py:68-72), then reduced to [-pi, pi] with a two-constant
+// Cody-Waite split of 2*pi (the hi part has 8 significant bits, so k*hi is
+// exact in fp32 for |k| < 2^16, i.e. |x| < 4e5; lo carries the rest), and
+// evaluated with the hardware approximation, which is accurate on [-pi, pi].
+__device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
+  const float kInv2Pi = 0.15915494309189535f;
+  const float k2PiHi = 6.28125f;                 // 2*pi rounded to 8 bits
+  const float k2PiLo = 1.9353071795864769e-3f;   // 2*pi - k2PiHi
+  float k = rintf(x * kInv2Pi);
+  float r = fmaf(-k, k2PiHi, x);
+  r = fmaf(-k, k2PiLo, r);
+  __sincosf(r, s, c);
+}
+
+__device__ __forceinline__ float sigmoidf_fast(float x) {
+  return 1.0f / (1.0f + __expf(-x));
+}
+
+// theta_p = 1 / theta^(2p/D) in fp32, the reference's table
+// (CoROPE/forward.py:130-133, without the repeat_interleave), or the
+// caller's table when one is given.
+__device__ __forceinline__ float theta_at(const float* table, float theta, int p, int D) {
+  return table ? table[p] : 1.0f / powf(theta, (float)(2 * p) / (float)D);
+}
+
+// Arguments shared by the forward kernels (element strides; D stride 1).
+struct FwdArgs {
+  const void *q, *k, *v;
+  void* o;
+  float *m, *l, *a, *lse;
+  const float* thetas;  // [D/2] or NULL: theta^(-2p/D) from `theta`
+  const float* bias;
+  int64_t bias_rs;
+  int64_t qs[3], ks[3], vs[3], os[3];
+  int B, H, Hkv, S, D;
+  float sm_scale, theta;
+};
+
+struct BwdArgs {
+  const void *q, *k, *v, *o, *dout;
+  const float *m, *l, *a;
+  const float* thetas;
+  const float* bias;
+  int64_t bias_rs;
+  void *dq, *dk, *dv;
+  int64_t qs[3], ks[3], vs[3], os[3], dos[3], dqs[3], dks[3], dvs[3];
+  int B, H, Hkv, S, D;
+  float sm_scale, theta;
+  // workspace views
+  float* delta;  // [B,H,S]  rowsum(dO * O)
+  float* lse;    // [B,H,S]  m + log(l)
+  float* dk32;   // [B,Hkv,S,D] fp32 accumulators
+  float* dv32;   // [B,Hkv,S,D]
+};
+
+}  // namespace corope

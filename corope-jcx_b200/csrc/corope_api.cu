@@ -1,0 +1,215 @@
+// C ABI of libcorope_b200.so: argument checks, workspace carving and kernel
+// dispatch.  No device memory is allocated here; errors are reported as
+// status codes plus a thread-local message (nothing throws across the ABI).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace corope {
+cudaError_t exact_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st);
+cudaError_t exact_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st);
+bool exact_supports_head_dim(int D);
+// tensor-core path (tc_fwd.cu); returns cudaErrorNotSupported when the
+// shape is outside its coverage
+bool tc_fwd_supported(const FwdArgs& a, int dtype);
+cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st);
+}  // namespace corope
+
+using namespace corope;
+
+static thread_local char g_err[512] = "";
+
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static int cuda_fail(cudaError_t e, const char* what) {
+  return fail(COROPE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+static bool aligned(const void* p, size_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+static size_t dtype_size(int dt) {
+  switch (dt) {
+    case COROPE_DTYPE_F32: return 4;
+    case COROPE_DTYPE_F16: return 2;
+    case COROPE_DTYPE_BF16: return 2;
+    default: return 0;
+  }
+}
+
+// Device must be compute capability 10.0 (B200) for the sm_100a image.
+static int check_device() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0)
+    return fail(COROPE_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                major, minor);
+  return COROPE_OK;
+}
+
+static int check_common(int B, int H, int Hkv, int S, int D, int causal, int dtype, float sm,
+                        float theta) {
+  if (B <= 0 || H <= 0 || Hkv <= 0 || S <= 0 || D <= 0)
+    return fail(COROPE_ERR_INVALID, "sizes must be positive (B=%d H=%d Hkv=%d S=%d D=%d)", B, H,
+                Hkv, S, D);
+  if (H % Hkv != 0)
+    return fail(COROPE_ERR_INVALID, "kv_heads (%d) must divide heads (%d)", Hkv, H);
+  if (D % 2 != 0) return fail(COROPE_ERR_INVALID, "head_dim must be even (got %d)", D);
+  if (!exact_supports_head_dim(D))
+    return fail(COROPE_ERR_UNSUPPORTED, "head_dim %d not supported (4, 8, 16, 32, 64, 128)", D);
+  if (!causal)
+    return fail(COROPE_ERR_UNSUPPORTED,
+                "causal=False is not implemented (the reference kernels are causal only)");
+  if (dtype_size(dtype) == 0) return fail(COROPE_ERR_INVALID, "unknown dtype %d", dtype);
+  if (!(sm > 0.f) || !(theta > 0.f))
+    return fail(COROPE_ERR_INVALID, "sm_scale and theta must be positive");
+  return COROPE_OK;
+}
+
+static int check_tensor(const void* p, const int64_t* st, const char* name, int dtype) {
+  if (!p) return fail(COROPE_ERR_INVALID, "%s is NULL", name);
+  if (!aligned(p, dtype_size(dtype)))
+    return fail(COROPE_ERR_INVALID, "%s is not aligned to its element size", name);
+  for (int i = 0; i < 3; ++i)
+    if (st[i] < 0) return fail(COROPE_ERR_INVALID, "%s has a negative stride", name);
+  if (st[0] % 2 || st[1] % 2 || st[2] % 2 || !aligned(p, 2 * dtype_size(dtype)))
+    return fail(COROPE_ERR_INVALID, "%s strides must be even (rows start on a pair)", name);
+  return COROPE_OK;
+}
+
+static void copy3(int64_t* d, const int64_t* s) { d[0] = s[0]; d[1] = s[1]; d[2] = s[2]; }
+
+static int fwd_common(const corope_fwd_params_t* p, corope_stream_t stream, bool mqa) {
+  if (!p) return fail(COROPE_ERR_INVALID, "params is NULL");
+  int rc = check_common(p->batch, p->heads, p->kv_heads, p->seq_len, p->head_dim, p->causal,
+                        p->dtype, p->sm_scale, p->theta);
+  if (rc) return rc;
+  if (!mqa && p->kv_heads != p->heads)
+    return fail(COROPE_ERR_INVALID, "corope_fwd needs kv_heads == heads; use corope_mqa_fwd");
+  if ((rc = check_tensor(p->q, p->q_stride, "q", p->dtype))) return rc;
+  if ((rc = check_tensor(p->k, p->k_stride, "k", p->dtype))) return rc;
+  if ((rc = check_tensor(p->v, p->v_stride, "v", p->dtype))) return rc;
+  if ((rc = check_tensor(p->o, p->o_stride, "o", p->dtype))) return rc;
+  if (p->bias && p->bias_row_stride < p->seq_len)
+    return fail(COROPE_ERR_INVALID, "bias_row_stride must be >= seq_len");
+  if ((rc = check_device())) return rc;
+
+  FwdArgs a{};
+  a.q = p->q; a.k = p->k; a.v = p->v; a.o = p->o;
+  a.m = p->m; a.l = p->l; a.a = p->a; a.lse = p->lse;
+  a.thetas = p->thetas; a.bias = p->bias; a.bias_rs = p->bias_row_stride;
+  copy3(a.qs, p->q_stride); copy3(a.ks, p->k_stride); copy3(a.vs, p->v_stride);
+  copy3(a.os, p->o_stride);
+  a.B = p->batch; a.H = p->heads; a.Hkv = p->kv_heads; a.S = p->seq_len; a.D = p->head_dim;
+  a.sm_scale = p->sm_scale; a.theta = p->theta;
+
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool tc_ok = tc_fwd_supported(a, p->dtype);
+  if (p->algo == COROPE_ALGO_TENSOR && !tc_ok)
+    return fail(COROPE_ERR_UNSUPPORTED,
+                "tensor-core forward needs bf16/f16, head_dim 64 or 128 and 16-byte aligned rows");
+  if (p->algo != COROPE_ALGO_EXACT && p->algo != COROPE_ALGO_AUTO && p->algo != COROPE_ALGO_TENSOR)
+    return fail(COROPE_ERR_INVALID, "unknown algo %d", p->algo);
+  cudaError_t e = (p->algo != COROPE_ALGO_EXACT && tc_ok) ? tc_fwd_launch(a, p->dtype, st)
+                                                          : exact_fwd_launch(a, p->dtype, st);
+  if (e != cudaSuccess) return cuda_fail(e, "forward launch");
+  return COROPE_OK;
+}
+
+static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+static size_t bwd_ws(const corope_bwd_params_t* p) {
+  const size_t rows = (size_t)p->batch * p->heads * p->seq_len;
+  const size_t kv = (size_t)p->batch * p->kv_heads * p->seq_len * p->head_dim;
+  return 2 * align256(rows * 4) + 2 * align256(kv * 4);
+}
+
+extern "C" {
+
+int corope_fwd(const corope_fwd_params_t* p, corope_stream_t stream) {
+  return fwd_common(p, stream, false);
+}
+
+int corope_mqa_fwd(const corope_fwd_params_t* p, corope_stream_t stream) {
+  return fwd_common(p, stream, true);
+}
+
+size_t corope_bwd_workspace_bytes(const corope_bwd_params_t* p) {
+  if (!p || p->batch <= 0 || p->heads <= 0 || p->kv_heads <= 0 || p->seq_len <= 0 ||
+      p->head_dim <= 0)
+    return 0;
+  return bwd_ws(p);
+}
+
+int corope_bwd(const corope_bwd_params_t* p, corope_stream_t stream) {
+  if (!p) return fail(COROPE_ERR_INVALID, "params is NULL");
+  int rc = check_common(p->batch, p->heads, p->kv_heads, p->seq_len, p->head_dim, p->causal,
+                        p->dtype, p->sm_scale, p->theta);
+  if (rc) return rc;
+  if ((rc = check_tensor(p->q, p->q_stride, "q", p->dtype))) return rc;
+  if ((rc = check_tensor(p->k, p->k_stride, "k", p->dtype))) return rc;
+  if ((rc = check_tensor(p->v, p->v_stride, "v", p->dtype))) return rc;
+  if ((rc = check_tensor(p->o, p->o_stride, "o", p->dtype))) return rc;
+  if ((rc = check_tensor(p->dout, p->do_stride, "dout", p->dtype))) return rc;
+  if ((rc = check_tensor(p->dq, p->dq_stride, "dq", p->dtype))) return rc;
+  if ((rc = check_tensor(p->dk, p->dk_stride, "dk", p->dtype))) return rc;
+  if ((rc = check_tensor(p->dv, p->dv_stride, "dv", p->dtype))) return rc;
+  if (!p->m || !p->l || !p->a) return fail(COROPE_ERR_INVALID, "m, l and a are required");
+  if (p->bias && p->bias_row_stride < p->seq_len)
+    return fail(COROPE_ERR_INVALID, "bias_row_stride must be >= seq_len");
+  if (p->algo == COROPE_ALGO_TENSOR)
+    return fail(COROPE_ERR_UNSUPPORTED, "tensor-core backward is not available in this build");
+  const size_t need = bwd_ws(p);
+  if (!p->workspace || p->workspace_bytes < need)
+    return fail(COROPE_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need,
+                p->workspace ? p->workspace_bytes : (size_t)0);
+  if (!aligned(p->workspace, 256)) return fail(COROPE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  if ((rc = check_device())) return rc;
+
+  BwdArgs a{};
+  a.q = p->q; a.k = p->k; a.v = p->v; a.o = p->o; a.dout = p->dout;
+  a.m = p->m; a.l = p->l; a.a = p->a;
+  a.thetas = p->thetas; a.bias = p->bias; a.bias_rs = p->bias_row_stride;
+  a.dq = p->dq; a.dk = p->dk; a.dv = p->dv;
+  copy3(a.qs, p->q_stride); copy3(a.ks, p->k_stride); copy3(a.vs, p->v_stride);
+  copy3(a.os, p->o_stride); copy3(a.dos, p->do_stride); copy3(a.dqs, p->dq_stride);
+  copy3(a.dks, p->dk_stride); copy3(a.dvs, p->dv_stride);
+  a.B = p->batch; a.H = p->heads; a.Hkv = p->kv_heads; a.S = p->seq_len; a.D = p->head_dim;
+  a.sm_scale = p->sm_scale; a.theta = p->theta;
+
+  const size_t rows = (size_t)p->batch * p->heads * p->seq_len;
+  const size_t kv = (size_t)p->batch * p->kv_heads * p->seq_len * p->head_dim;
+  char* ws = static_cast<char*>(p->workspace);
+  a.delta = reinterpret_cast<float*>(ws);
+  a.lse = reinterpret_cast<float*>(ws + align256(rows * 4));
+  a.dk32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4));
+  a.dv32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4) + align256(kv * 4));
+
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(a.dk32, 0, 2 * align256(kv * 4), st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+  e = exact_bwd_launch(a, p->dtype, st);
+  if (e != cudaSuccess) return cuda_fail(e, "backward launch");
+  return COROPE_OK;
+}
+
+const char* corope_last_error(void) { return g_err; }
+
+size_t corope_params_size(int which) {
+  return which == 0 ? sizeof(corope_fwd_params_t) : which == 1 ? sizeof(corope_bwd_params_t) : 0;
+}
+
+int corope_abi_version(void) { return COROPE_ABI_VERSION; }
+
+}  // extern "C"

@@ -1,0 +1,491 @@
+// Exact-math CoRoPE kernels on CUDA cores (sm_100a).
+//
+// Every (query t, key j, pair p) angle a_tj * theta_p gets its own sine and
+// cosine, as in the reference definition (check.py:65-95).  These kernels are
+// the precision anchor of the library (COROPE_ALGO_EXACT) and cover every
+// shape; the tensor-core kernels in tc_fwd.cu are the fast path.
+//
+// Work split: one CTA owns BM = 64 query rows of one (b, h); each row is
+// owned by TPR consecutive threads, each holding an interleaved subset of the
+// D/2 rotation pairs (pair p belongs to thread p % TPR, which keeps the
+// shared-memory reads of a key row bank-conflict free).  Keys are staged in
+// shared memory as fp32 tiles of BN = 32.
+#include "common.cuh"
+
+namespace corope {
+
+constexpr int kBM = 64;
+constexpr int kBN = 32;
+
+template <typename T>
+__device__ __forceinline__ float2 load_pair(const T* base, int64_t off) {
+  return make_float2(to_f32<T>(base[off]), to_f32<T>(base[off + 1]));
+}
+
+// Load keys [j0, j0 + kBN) of one head into shared memory as fp32 pairs
+// (rows past the sequence end are zero).
+template <typename T, int D>
+__device__ __forceinline__ void stage_rows(float2* dst, const T* src, int64_t seq_stride,
+                                           int j0, int S, int nthreads) {
+  constexpr int P = D / 2;
+  for (int idx = threadIdx.x; idx < kBN * P; idx += nthreads) {
+    int r = idx / P, p = idx % P;
+    int j = j0 + r;
+    dst[idx] = (j < S) ? load_pair<T>(src, (int64_t)j * seq_stride + 2 * p) : make_float2(0.f, 0.f);
+  }
+}
+
+template <int TPR>
+__device__ __forceinline__ float group_sum(float x) {
+#pragma unroll
+  for (int off = 1; off < TPR; off <<= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+  return x;
+}
+
+// ---------------------------------------------------------------------------
+// Forward.  Keys are walked from the diagonal down to 0 (as the reference
+// kernel does, CoROPE/forward.py:57-78) so the contextual position
+// a_tj = sum_{i=j+1..t} z_ti is a running suffix sum per row.
+// ---------------------------------------------------------------------------
+template <typename T, int D, int TPR, bool HAS_BIAS>
+__global__ void __launch_bounds__(kBM * TPR)
+exact_fwd_kernel(FwdArgs args) {
+  constexpr int P = D / 2;
+  constexpr int NP = P / TPR;       // pairs per thread
+  constexpr int NT = kBM * TPR;
+  constexpr int CH = 8;             // keys per online-softmax update
+  __shared__ float2 Ks[kBN * P];
+  __shared__ float2 Vs[kBN * P];
+  __shared__ float th_s[P];
+
+  const int qtile = gridDim.x - 1 - blockIdx.x;   // longest rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (args.H / args.Hkv);
+  const int rl = threadIdx.x / TPR, sub = threadIdx.x % TPR;
+  const int t = qtile * kBM + rl;
+  const int S = args.S;
+
+  const T* qb = (const T*)args.q + b * args.qs[0] + h * args.qs[1];
+  const T* kb = (const T*)args.k + b * args.ks[0] + hk * args.ks[1];
+  const T* vb = (const T*)args.v + b * args.vs[0] + hk * args.vs[1];
+
+  for (int p = threadIdx.x; p < P; p += NT) th_s[p] = theta_at(args.thetas, args.theta, p, D);
+
+  float2 qp[NP], op[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    int p = i * TPR + sub;
+    qp[i] = (t < S) ? load_pair<T>(qb, (int64_t)t * args.qs[2] + 2 * p) : make_float2(0.f, 0.f);
+    op[i] = make_float2(0.f, 0.f);
+  }
+  float m_run = -1e30f, l_run = 0.f, a_run = 0.f;
+  float lg[CH];
+  const float sm = args.sm_scale;
+
+  const int last_row = min(S - 1, qtile * kBM + kBM - 1);
+  for (int j0 = (last_row / kBN) * kBN; j0 >= 0; j0 -= kBN) {
+    __syncthreads();
+    stage_rows<T, D>(Ks, kb, args.ks[2], j0, S, NT);
+    stage_rows<T, D>(Vs, vb, args.vs[2], j0, S, NT);
+    __syncthreads();
+#pragma unroll 1
+    for (int c0 = kBN - CH; c0 >= 0; c0 -= CH) {
+#pragma unroll
+      for (int u = CH - 1; u >= 0; --u) {
+        const int jj = c0 + u;
+        const int j = j0 + jj;
+        const bool valid = (j <= t) && (t < S);
+        const float2* kr = Ks + jj * P;
+        float g = 0.f;
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          float2 kk = kr[i * TPR + sub];
+          g = fmaf(qp[i].x, kk.x, fmaf(qp[i].y, kk.y, g));
+        }
+        g = group_sum<TPR>(g);
+        const float z = valid ? sigmoidf_fast(g) : 0.f;
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          float2 kk = kr[i * TPR + sub];
+          float s, c;
+          sincos_reduced(a_run * th_s[i * TPR + sub], &s, &c);
+          float Cp = fmaf(qp[i].x, kk.x, qp[i].y * kk.y);
+          float Sp = fmaf(qp[i].x, kk.y, -qp[i].y * kk.x);
+          acc = fmaf(c, Cp, fmaf(s, Sp, acc));
+        }
+        acc = group_sum<TPR>(acc);
+        float logit = acc * sm;
+        if (HAS_BIAS && valid) logit += args.bias[(int64_t)t * args.bias_rs + j];
+        lg[u] = valid ? logit : -INFINITY;
+        a_run += z;
+      }
+      // online softmax over the CH keys just scored
+      float mx = m_run;
+#pragma unroll
+      for (int u = 0; u < CH; ++u) mx = fmaxf(mx, lg[u]);
+      const float alpha = __expf(m_run - mx);
+      l_run *= alpha;
+#pragma unroll
+      for (int i = 0; i < NP; ++i) { op[i].x *= alpha; op[i].y *= alpha; }
+#pragma unroll
+      for (int u = 0; u < CH; ++u) {
+        const float pr = __expf(lg[u] - mx);
+        l_run += pr;
+        const float2* vr = Vs + (c0 + u) * P;
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+          float2 vv = vr[i * TPR + sub];
+          op[i].x = fmaf(pr, vv.x, op[i].x);
+          op[i].y = fmaf(pr, vv.y, op[i].y);
+        }
+      }
+      m_run = mx;
+    }
+  }
+
+  if (t < S) {
+    T* ob = (T*)args.o + b * args.os[0] + h * args.os[1] + (int64_t)t * args.os[2];
+    const float inv = 1.0f / l_run;
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      int p = i * TPR + sub;
+      ob[2 * p] = from_f32<T>(op[i].x * inv);
+      ob[2 * p + 1] = from_f32<T>(op[i].y * inv);
+    }
+    if (sub == 0) {
+      const int64_t r = ((int64_t)b * args.H + h) * S + t;
+      if (args.m) args.m[r] = m_run;
+      if (args.l) args.l[r] = l_run;
+      if (args.a) args.a[r] = a_run;
+      if (args.lse) args.lse[r] = m_run + logf(l_run);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward
+// ---------------------------------------------------------------------------
+// delta_t = sum_d dO_td * O_td and lse_t = m_t + log(l_t); one warp per row.
+template <typename T>
+__global__ void exact_bwd_pre_kernel(BwdArgs args) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)args.B * args.H * args.S;
+  if (warp >= rows) return;
+  const int t = warp % args.S;
+  const int bh = warp / args.S;
+  const int h = bh % args.H, b = bh / args.H;
+  const T* ob = (const T*)args.o + b * args.os[0] + h * args.os[1] + (int64_t)t * args.os[2];
+  const T* db = (const T*)args.dout + b * args.dos[0] + h * args.dos[1] + (int64_t)t * args.dos[2];
+  float s = 0.f;
+  for (int d = lane; d < args.D; d += 32) s = fmaf(to_f32<T>(ob[d]), to_f32<T>(db[d]), s);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) {
+    args.delta[warp] = s;
+    args.lse[warp] = args.m[warp] + logf(args.l[warp]);
+  }
+}
+
+// Query-stationary backward.  For each key tile (ascending) the row owners
+// recompute gates, positions a_tj = A_t - sum_{i<=j} z_ti, logits, P, dP and
+// the position/gate chain (exclusive prefix sum of da along keys), update dq,
+// and leave the per-pair scalars (P, dlogit*sm, dgate, a) in shared memory;
+// then the same threads re-partition by key and reduce dk, dv over the
+// tile's 64 rows, adding the partial sums to fp32 accumulators in global
+// memory.
+template <typename T, int D, int TPR, bool HAS_BIAS>
+__global__ void __launch_bounds__(kBM * TPR)
+exact_bwd_kernel(BwdArgs args) {
+  constexpr int P = D / 2;
+  constexpr int NP = P / TPR;
+  constexpr int NT = kBM * TPR;
+  constexpr int TPK = NT / kBN;                    // threads per key in phase 2
+  constexpr int NP2 = (P + TPK - 1) / TPK;
+  constexpr int PB = kBN + 1;                      // padded pair-buffer row
+  extern __shared__ float4 smem_f4[];
+  float2* Ks = reinterpret_cast<float2*>(smem_f4);
+  float2* Vs = Ks + kBN * P;
+  float2* Qs = Vs + kBN * P;
+  float2* Ds = Qs + kBM * P;
+  float* bufP = reinterpret_cast<float*>(Ds + kBM * P);
+  float* bufW = bufP + kBM * PB;
+  float* bufG = bufW + kBM * PB;
+  float* bufA = bufG + kBM * PB;
+  float* th_s = bufA + kBM * PB;
+
+  const int qtile = gridDim.x - 1 - blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (args.H / args.Hkv);
+  const int rl = threadIdx.x / TPR, sub = threadIdx.x % TPR;
+  const int q0 = qtile * kBM;
+  const int t = q0 + rl;
+  const int S = args.S;
+  const float sm = args.sm_scale;
+
+  const T* qb = (const T*)args.q + b * args.qs[0] + h * args.qs[1];
+  const T* kb = (const T*)args.k + b * args.ks[0] + hk * args.ks[1];
+  const T* vb = (const T*)args.v + b * args.vs[0] + hk * args.vs[1];
+  const T* db = (const T*)args.dout + b * args.dos[0] + h * args.dos[1];
+
+  for (int p = threadIdx.x; p < P; p += NT) th_s[p] = theta_at(args.thetas, args.theta, p, D);
+  for (int idx = threadIdx.x; idx < kBM * P; idx += NT) {
+    int r = idx / P, p = idx % P;
+    int tt = q0 + r;
+    Qs[idx] = (tt < S) ? load_pair<T>(qb, (int64_t)tt * args.qs[2] + 2 * p) : make_float2(0.f, 0.f);
+    Ds[idx] = (tt < S) ? load_pair<T>(db, (int64_t)tt * args.dos[2] + 2 * p) : make_float2(0.f, 0.f);
+  }
+  __syncthreads();
+
+  float2 qp[NP], dop[NP], dqp[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    qp[i] = Qs[rl * P + i * TPR + sub];
+    dop[i] = Ds[rl * P + i * TPR + sub];
+    dqp[i] = make_float2(0.f, 0.f);
+  }
+  const int64_t rix = ((int64_t)b * args.H + h) * S + t;
+  const float A_t = (t < S) ? args.a[rix] : 0.f;
+  const float lse_t = (t < S) ? args.lse[rix] : 0.f;
+  const float dlt_t = (t < S) ? args.delta[rix] : 0.f;
+  float c_run = 0.f, da_run = 0.f;
+
+  // phase-2 mapping
+  const int kj = threadIdx.x / TPK, sub2 = threadIdx.x % TPK;
+  float* dk32 = args.dk32 + ((int64_t)b * args.Hkv + hk) * S * D;
+  float* dv32 = args.dv32 + ((int64_t)b * args.Hkv + hk) * S * D;
+
+  const int last_row = min(S - 1, q0 + kBM - 1);
+  for (int j0 = 0; j0 <= last_row; j0 += kBN) {
+    __syncthreads();
+    stage_rows<T, D>(Ks, kb, args.ks[2], j0, S, NT);
+    stage_rows<T, D>(Vs, vb, args.vs[2], j0, S, NT);
+    __syncthreads();
+    // ---- phase 1: row owners --------------------------------------------
+#pragma unroll 1
+    for (int jj = 0; jj < kBN; ++jj) {
+      const int j = j0 + jj;
+      const bool valid = (j <= t) && (t < S);
+      const float2* kr = Ks + jj * P;
+      const float2* vr = Vs + jj * P;
+      float g = 0.f;
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        float2 kk = kr[i * TPR + sub];
+        g = fmaf(qp[i].x, kk.x, fmaf(qp[i].y, kk.y, g));
+      }
+      g = group_sum<TPR>(g);
+      const float z = valid ? sigmoidf_fast(g) : 0.f;
+      c_run += z;
+      const float a = valid ? (A_t - c_run) : 0.f;
+      float cs[NP], sn[NP];
+      float acc = 0.f, dacc = 0.f, dpp = 0.f;
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        const int p = i * TPR + sub;
+        float2 kk = kr[p];
+        float2 vv = vr[p];
+        sincos_reduced(a * th_s[p], &sn[i], &cs[i]);
+        float Cp = fmaf(qp[i].x, kk.x, qp[i].y * kk.y);
+        float Sp = fmaf(qp[i].x, kk.y, -qp[i].y * kk.x);
+        acc = fmaf(cs[i], Cp, fmaf(sn[i], Sp, acc));
+        dacc = fmaf(th_s[p], fmaf(cs[i], Sp, -sn[i] * Cp), dacc);
+        dpp = fmaf(dop[i].x, vv.x, fmaf(dop[i].y, vv.y, dpp));
+      }
+      acc = group_sum<TPR>(acc);
+      dacc = group_sum<TPR>(dacc);
+      dpp = group_sum<TPR>(dpp);
+      float logit = acc * sm;
+      if (HAS_BIAS && valid) logit += args.bias[(int64_t)t * args.bias_rs + j];
+      const float pr = valid ? __expf(logit - lse_t) : 0.f;
+      const float w = pr * (dpp - dlt_t) * sm;      // d logit * sm_scale
+      const float da = w * dacc;
+      const float ds = valid ? da_run * z * (1.f - z) : 0.f;   // exclusive prefix
+      da_run += valid ? da : 0.f;
+#pragma unroll
+      for (int i = 0; i < NP; ++i) {
+        float2 kk = kr[i * TPR + sub];
+        // w * R(-phi) k + ds * k
+        dqp[i].x += w * fmaf(kk.x, cs[i], kk.y * sn[i]) + ds * kk.x;
+        dqp[i].y += w * fmaf(kk.y, cs[i], -kk.x * sn[i]) + ds * kk.y;
+      }
+      if (sub == 0) {
+        bufP[rl * PB + jj] = pr;
+        bufW[rl * PB + jj] = valid ? w : 0.f;
+        bufG[rl * PB + jj] = ds;
+        bufA[rl * PB + jj] = a;
+      }
+    }
+    __syncthreads();
+    // ---- phase 2: key owners --------------------------------------------
+    {
+      const int j = j0 + kj;
+      float2 dkp[NP2], dvp[NP2];
+#pragma unroll
+      for (int i = 0; i < NP2; ++i) { dkp[i] = make_float2(0.f, 0.f); dvp[i] = dkp[i]; }
+#pragma unroll 1
+      for (int r = 0; r < kBM; ++r) {
+        const float pr = bufP[r * PB + kj];
+        const float w = bufW[r * PB + kj];
+        const float ds = bufG[r * PB + kj];
+        const float a = bufA[r * PB + kj];
+#pragma unroll
+        for (int i = 0; i < NP2; ++i) {
+          const int p = i * TPK + sub2;
+          if (p < P) {
+            float s, c;
+            sincos_reduced(a * th_s[p], &s, &c);
+            float2 qq = Qs[r * P + p];
+            float2 dd = Ds[r * P + p];
+            // w * R(phi) q + ds * q
+            dkp[i].x += w * fmaf(qq.x, c, -qq.y * s) + ds * qq.x;
+            dkp[i].y += w * fmaf(qq.x, s, qq.y * c) + ds * qq.y;
+            dvp[i].x = fmaf(pr, dd.x, dvp[i].x);
+            dvp[i].y = fmaf(pr, dd.y, dvp[i].y);
+          }
+        }
+      }
+      if (j < S) {
+#pragma unroll
+        for (int i = 0; i < NP2; ++i) {
+          const int p = i * TPK + sub2;
+          if (p < P) {
+            atomicAdd(dk32 + (int64_t)j * D + 2 * p, dkp[i].x);
+            atomicAdd(dk32 + (int64_t)j * D + 2 * p + 1, dkp[i].y);
+            atomicAdd(dv32 + (int64_t)j * D + 2 * p, dvp[i].x);
+            atomicAdd(dv32 + (int64_t)j * D + 2 * p + 1, dvp[i].y);
+          }
+        }
+      }
+    }
+  }
+
+  if (t < S) {
+    T* dqb = (T*)args.dq + b * args.dqs[0] + h * args.dqs[1] + (int64_t)t * args.dqs[2];
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      int p = i * TPR + sub;
+      dqb[2 * p] = from_f32<T>(dqp[i].x);
+      dqb[2 * p + 1] = from_f32<T>(dqp[i].y);
+    }
+  }
+}
+
+// fp32 dk/dv accumulators -> output dtype and strides.
+template <typename T>
+__global__ void exact_bwd_post_kernel(BwdArgs args) {
+  const int64_t n = (int64_t)args.B * args.Hkv * args.S * args.D;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int d = i % args.D;
+    int64_t r = i / args.D;
+    const int j = r % args.S;
+    r /= args.S;
+    const int hk = r % args.Hkv;
+    const int b = r / args.Hkv;
+    ((T*)args.dk)[b * args.dks[0] + hk * args.dks[1] + (int64_t)j * args.dks[2] + d] =
+        from_f32<T>(args.dk32[i]);
+    ((T*)args.dv)[b * args.dvs[0] + hk * args.dvs[1] + (int64_t)j * args.dvs[2] + d] =
+        from_f32<T>(args.dv32[i]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+template <int D> constexpr int tpr_for() { return D >= 8 ? 4 : 2; }
+
+template <typename T, int D>
+static cudaError_t launch_fwd_d(const FwdArgs& a, cudaStream_t st) {
+  constexpr int TPR = tpr_for<D>();
+  dim3 grid((a.S + kBM - 1) / kBM, a.H, a.B);
+  if (a.bias)
+    exact_fwd_kernel<T, D, TPR, true><<<grid, kBM * TPR, 0, st>>>(a);
+  else
+    exact_fwd_kernel<T, D, TPR, false><<<grid, kBM * TPR, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_fwd_t(const FwdArgs& a, cudaStream_t st) {
+  switch (a.D) {
+    case 4: return launch_fwd_d<T, 4>(a, st);
+    case 8: return launch_fwd_d<T, 8>(a, st);
+    case 16: return launch_fwd_d<T, 16>(a, st);
+    case 32: return launch_fwd_d<T, 32>(a, st);
+    case 64: return launch_fwd_d<T, 64>(a, st);
+    case 128: return launch_fwd_d<T, 128>(a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t exact_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st) {
+  switch (dtype) {
+    case COROPE_DTYPE_F32: return launch_fwd_t<float>(a, st);
+    case COROPE_DTYPE_F16: return launch_fwd_t<__half>(a, st);
+    case COROPE_DTYPE_BF16: return launch_fwd_t<__nv_bfloat16>(a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int D>
+static size_t bwd_smem_bytes() {
+  constexpr int P = D / 2;
+  return sizeof(float2) * (2 * kBN * P + 2 * kBM * P) + sizeof(float) * (4 * kBM * (kBN + 1) + P);
+}
+
+template <typename T, int D>
+static cudaError_t launch_bwd_d(const BwdArgs& a, cudaStream_t st) {
+  constexpr int TPR = tpr_for<D>();
+  const size_t smem = bwd_smem_bytes<D>();
+  dim3 grid((a.S + kBM - 1) / kBM, a.H, a.B);
+  cudaError_t e;
+  if (a.bias) {
+    auto kern = exact_bwd_kernel<T, D, TPR, true>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kBM * TPR, smem, st>>>(a);
+  } else {
+    auto kern = exact_bwd_kernel<T, D, TPR, false>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kBM * TPR, smem, st>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_bwd_t(const BwdArgs& a, cudaStream_t st) {
+  const int64_t rows = (int64_t)a.B * a.H * a.S;
+  exact_bwd_pre_kernel<T><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  switch (a.D) {
+    case 4: e = launch_bwd_d<T, 4>(a, st); break;
+    case 8: e = launch_bwd_d<T, 8>(a, st); break;
+    case 16: e = launch_bwd_d<T, 16>(a, st); break;
+    case 32: e = launch_bwd_d<T, 32>(a, st); break;
+    case 64: e = launch_bwd_d<T, 64>(a, st); break;
+    case 128: e = launch_bwd_d<T, 128>(a, st); break;
+    default: return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess) return e;
+  exact_bwd_post_kernel<T><<<148 * 8, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t exact_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st) {
+  switch (dtype) {
+    case COROPE_DTYPE_F32: return launch_bwd_t<float>(a, st);
+    case COROPE_DTYPE_F16: return launch_bwd_t<__half>(a, st);
+    case COROPE_DTYPE_BF16: return launch_bwd_t<__nv_bfloat16>(a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+bool exact_supports_head_dim(int D) {
+  return D == 4 || D == 8 || D == 16 || D == 32 || D == 64 || D == 128;
+}
+
+}  // namespace corope

@@ -1,0 +1,137 @@
+/*
+ * corope.h -- C ABI of the B200 CoRoPE attention library (libcorope_b200.so).
+ *
+ * CoRoPE ("contextual RoPE") attention: for query t and key j <= t the gate
+ * z_tj = sigmoid(q_t . k_j) is summed into the contextual position
+ * a_tj = sum_{i=j+1..t} z_ti, and the logit is
+ * sm_scale * <R(a_tj * theta_p) q_t, k_j> with the interleaved pair rotation
+ * R of RoPE and theta_p = theta^(-2p/D).  Causal softmax, then O = P V.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes,
+ * launches on the given CUDA stream and returns a corope_status_t.  Nothing
+ * throws; corope_last_error() returns a message for the last failing call of
+ * the calling thread.  The library allocates no device memory: the caller
+ * passes outputs and (for the backward) a workspace of the size reported by
+ * corope_bwd_workspace_bytes().  Calls are stateless and may run concurrently
+ * on different streams.
+ *
+ * Tensor layout: q, o, dO, dq are [B, H, S, D]; k, v, dk, dv are
+ * [B, Hkv, S, D] with Hkv dividing H (Hkv == H for MHA, 1 for MQA).  Each
+ * tensor is described by its base pointer and three element strides
+ * (batch, head, seq); the head_dim stride must be 1.  m, l, a (and lse) are
+ * contiguous fp32 [B, H, S].
+ */
+#ifndef COROPE_B200_H
+#define COROPE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; declared here so that callers need no CUDA
+ * headers.  NULL means the legacy default stream. */
+typedef struct CUstream_st *corope_stream_t;
+
+typedef enum {
+  COROPE_DTYPE_F32 = 0,
+  COROPE_DTYPE_F16 = 1,
+  COROPE_DTYPE_BF16 = 2
+} corope_dtype_t;
+
+typedef enum {
+  /* tensor-core kernels where the shape allows them, else exact */
+  COROPE_ALGO_AUTO = 0,
+  /* per-pair sine/cosine on CUDA cores (fp32 math, any supported shape) */
+  COROPE_ALGO_EXACT = 1,
+  /* tcgen05 kernels with the windowed Chebyshev expansion of the rotation;
+   * COROPE_ERR_UNSUPPORTED when the shape or dtype is not covered */
+  COROPE_ALGO_TENSOR = 2
+} corope_algo_t;
+
+typedef enum {
+  COROPE_OK = 0,
+  COROPE_ERR_INVALID = 1,     /* bad argument (shape, stride, pointer) */
+  COROPE_ERR_UNSUPPORTED = 2, /* valid but not implemented (e.g. head_dim) */
+  COROPE_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  COROPE_ERR_WORKSPACE = 4,   /* workspace missing or too small */
+  COROPE_ERR_DEVICE = 5       /* device not sm_100 or kernel image missing */
+} corope_status_t;
+
+typedef struct {
+  const void *q, *k, *v;   /* inputs, dtype `dtype` */
+  void *o;                 /* output [B,H,S,D], dtype `dtype` */
+  float *m, *l, *a;        /* outputs [B,H,S] fp32: running max of the
+                              logits, sum of exp(logit - m), total gate sum */
+  float *lse;              /* optional output [B,H,S] fp32: m + log(l) */
+  const float *thetas;     /* optional [D/2] fp32 frequency table; NULL:
+                              theta^(-2p/D) computed from `theta` */
+  const float *bias;       /* optional additive logit bias [S,S] fp32 */
+  int64_t bias_row_stride; /* elements between bias rows */
+  int64_t q_stride[3], k_stride[3], v_stride[3], o_stride[3];
+  int32_t batch, heads, kv_heads, seq_len, head_dim;
+  float sm_scale, theta;
+  int32_t causal; /* must be 1 */
+  int32_t dtype;  /* corope_dtype_t */
+  int32_t algo;   /* corope_algo_t */
+} corope_fwd_params_t;
+
+typedef struct {
+  const void *q, *k, *v, *o, *dout;   /* saved inputs/output and dO */
+  const float *m, *l, *a;             /* saved forward state [B,H,S] */
+  const float *thetas;                /* optional [D/2] table, as above */
+  const float *bias;                  /* optional bias used in the forward */
+  int64_t bias_row_stride;
+  void *dq, *dk, *dv;                 /* outputs, dtype `dtype` */
+  int64_t q_stride[3], k_stride[3], v_stride[3], o_stride[3], do_stride[3];
+  int64_t dq_stride[3], dk_stride[3], dv_stride[3];
+  int32_t batch, heads, kv_heads, seq_len, head_dim;
+  float sm_scale, theta;
+  int32_t causal;
+  int32_t dtype;
+  int32_t algo;
+  void *workspace;                    /* device scratch, 256-byte aligned */
+  size_t workspace_bytes;
+} corope_bwd_params_t;
+
+/* Forward.  Replaces the launch of co_rope_fwd_kernel in
+ * CoROPE/forward.py:123-178 (host wrapper co_rope_forward, launch at
+ * :149-171); same outputs O, M, L, A (forward.py:110-120). */
+int corope_fwd(const corope_fwd_params_t *p, corope_stream_t stream);
+
+/* MQA/GQA forward: k/v carry kv_heads < heads heads shared by groups of
+ * heads/kv_heads query heads, optional bias.  Replaces the launch of
+ * co_rope_mqa_fwd_kernel in CoROPE/co_rope_mqa_forward.py:107-176 (launch at
+ * :151-174; the bias term of :72-75). */
+int corope_mqa_fwd(const corope_fwd_params_t *p, corope_stream_t stream);
+
+/* Bytes of workspace corope_bwd needs for these parameters. */
+size_t corope_bwd_workspace_bytes(const corope_bwd_params_t *p);
+
+/* Backward: dq, dk, dv of the CoRoPE attention (gradients through the
+ * softmax, the rotation, the contextual positions and the sigmoid gates).
+ * Replaces the launch of co_rope_bwd_kernel in
+ * CoROPE/co_rope_backward.py:116-211 (launch at :158-185), whose own result
+ * is not the gradient of the forward; parity is with autograd through the
+ * reference definition check.py:44-103. */
+int corope_bwd(const corope_bwd_params_t *p, corope_stream_t stream);
+
+/* Message for the last non-zero status returned on this thread. */
+const char *corope_last_error(void);
+
+/* sizeof(corope_fwd_params_t) for which == 0, sizeof(corope_bwd_params_t)
+ * for which == 1, else 0; lets FFI bindings check their struct layout. */
+size_t corope_params_size(int which);
+
+/* ABI version of this header (COROPE_ABI_VERSION). */
+int corope_abi_version(void);
+
+#define COROPE_ABI_VERSION 1
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* COROPE_B200_H */

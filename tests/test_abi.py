@@ -1,0 +1,92 @@
+"""The C-ABI library loads, exports what include/corope.h declares, and its
+argument checks answer before any device work (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from CoROPE import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "corope.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(corope_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load_library()
+    names = declared_functions()
+    assert {"corope_fwd", "corope_mqa_fwd", "corope_bwd", "corope_bwd_workspace_bytes",
+            "corope_last_error", "corope_abi_version"} <= set(names)
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_abi_version_and_struct_layout():
+    lib = _lib.load_library()
+    assert lib.corope_abi_version() == 1
+    assert lib.corope_params_size(0) == ctypes.sizeof(_lib.FwdParams)
+    assert lib.corope_params_size(1) == ctypes.sizeof(_lib.BwdParams)
+
+
+def _fwd_params(**kw):
+    p = _lib.FwdParams()
+    fake = 1 << 20
+    p.q = p.k = p.v = p.o = fake
+    S, D = kw.get("S", 64), kw.get("D", 64)
+    st = _lib._I64x3(4 * S * D, S * D, D)
+    p.q_stride = p.k_stride = p.v_stride = p.o_stride = st
+    p.batch, p.heads, p.kv_heads = 1, kw.get("H", 4), kw.get("Hkv", 4)
+    p.seq_len, p.head_dim = S, D
+    p.sm_scale, p.theta = 0.125, 10000.0
+    p.causal, p.dtype, p.algo = kw.get("causal", 1), kw.get("dtype", 2), kw.get("algo", 0)
+    return p
+
+
+@pytest.mark.parametrize("kw,code,fn", [
+    (dict(Hkv=3), _lib.ERR_INVALID, "corope_mqa_fwd"),
+    (dict(Hkv=1), _lib.ERR_INVALID, "corope_fwd"),
+    (dict(causal=0), _lib.ERR_UNSUPPORTED, "corope_fwd"),
+    (dict(D=256), _lib.ERR_UNSUPPORTED, "corope_fwd"),
+    (dict(D=6), _lib.ERR_UNSUPPORTED, "corope_fwd"),
+    (dict(dtype=7), _lib.ERR_INVALID, "corope_fwd"),
+])
+def test_forward_argument_checks(kw, code, fn):
+    lib = _lib.load_library()
+    p = _fwd_params(**kw)
+    rc = getattr(lib, fn)(ctypes.byref(p), None)
+    assert rc == code
+    assert lib.corope_last_error()
+
+
+def test_null_params_and_bad_stride():
+    lib = _lib.load_library()
+    assert lib.corope_fwd(None, None) == _lib.ERR_INVALID
+    p = _fwd_params()
+    p.q_stride = _lib._I64x3(4 * 64 * 64, 64 * 64, 63)
+    assert lib.corope_fwd(ctypes.byref(p), None) == _lib.ERR_INVALID
+
+
+def test_backward_workspace_checks():
+    lib = _lib.load_library()
+    p = _lib.BwdParams()
+    fake = 1 << 20
+    for n in ("q", "k", "v", "o", "dout", "m", "l", "a", "dq", "dk", "dv"):
+        setattr(p, n, fake)
+    st = _lib._I64x3(2 * 128 * 64, 128 * 64, 64)
+    for n in ("q_stride", "k_stride", "v_stride", "o_stride", "do_stride", "dq_stride",
+              "dk_stride", "dv_stride"):
+        setattr(p, n, st)
+    p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = 1, 2, 2, 128, 64
+    p.sm_scale, p.theta, p.causal, p.dtype = 0.125, 1e4, 1, 2
+    need = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
+    # delta + lse rows, fp32 dk/dv accumulators
+    assert need >= 2 * 2 * 128 * 4 + 2 * 2 * 128 * 64 * 4
+    assert lib.corope_bwd(ctypes.byref(p), None) == _lib.ERR_WORKSPACE
+    p.workspace, p.workspace_bytes = fake, need - 1
+    assert lib.corope_bwd(ctypes.byref(p), None) == _lib.ERR_WORKSPACE

@@ -1,0 +1,69 @@
+"""Host-side behaviour of the drop-in Python package (no GPU needed)."""
+import math
+
+import pytest
+import torch
+
+import CoROPE
+import importlib
+from CoROPE.co_rope_backward import co_rope_backward
+from CoROPE.co_rope_mqa_forward import co_rope_mqa_forward
+from CoROPE.forward import co_rope_forward
+
+
+def test_module_layout_matches_reference_imports():
+    # the imports used by the reference's own callers
+    from CoROPE.co_rope_forward import co_rope_forward as f2  # co_rope_attn.py:2
+    from CoROPE.co_rope_attn import CoRoPEAttention, CoRoPEAttentionFunction  # test.py:2
+    assert f2 is co_rope_forward
+    assert CoROPE.CoRoPEAttention is CoRoPEAttention
+
+
+def test_causal_false_refused():
+    q = torch.zeros(1, 1, 4, 4)
+    with pytest.raises(NotImplementedError):
+        co_rope_forward(q, q, q, 0.5, causal=False)
+    with pytest.raises(NotImplementedError):
+        co_rope_mqa_forward(q, q, q, 0.5, causal=False)
+
+
+def test_cpu_tensors_refused_like_reference():
+    q = torch.zeros(1, 1, 4, 4)
+    with pytest.raises(AssertionError, match="CUDA"):
+        co_rope_forward(q, q, q, 0.5)
+
+
+def test_mqa_shape_error_like_reference():
+    q = torch.zeros(1, 2, 4, 4)
+    with pytest.raises(ValueError):
+        co_rope_mqa_forward(q, q, q, 0.5)
+
+
+def test_backward_accepts_both_conventions(monkeypatch):
+    bwd_mod = importlib.import_module("CoROPE.co_rope_backward")
+    seen = []
+
+    def fake_run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo):
+        seen.append((sm_scale, theta, None if thetas is None else thetas.tolist()))
+        return "dq", "dk", "dv"
+
+    monkeypatch.setattr(bwd_mod, "_run", fake_run)
+    t = torch.zeros(1, 1, 4, 4)
+    r = co_rope_backward((t,) * 7, t, 0.3, 500.0)
+    assert r == ("dq", "dk", "dv") and seen[-1] == (0.3, 500.0, None)
+    D = 4
+    th = 1.0 / (1e4 ** (torch.arange(0, D, 2).float() / D))
+    thetas = th.repeat_interleave(2).unsqueeze(0).repeat(3, 1)
+    r = co_rope_backward(t, t, t, t, t, t, t, t, thetas, True, 0.25)
+    assert r == ("dq", "dk", "dv", None)
+    assert seen[-1][0] == 0.25 and seen[-1][2] == pytest.approx(th.tolist())
+    with pytest.raises(NotImplementedError):
+        co_rope_backward(t, t, t, t, t, t, t, t, thetas, False, 0.25)
+
+
+def test_theta_table_matches_reference_expression():
+    from CoROPE import _lib
+    D, theta = 128, 10000.0
+    ref = 1.0 / (theta ** (torch.arange(0, D, 2).float() / D))
+    assert torch.equal(_lib.theta_table(D, theta, "cpu"), ref)
+    assert _lib.default_scale(64, None) == pytest.approx(1 / math.sqrt(64))

@@ -1,0 +1,243 @@
+"""CUDA kernels (through the C ABI) against the oracle and the golden fixtures.
+
+Tolerances (bf16 inputs, fp32 accumulation): max-abs <= 2e-2 on O, <= 5e-2
+on gradients, relative L2 <= 1e-2.  fp32 inputs through the exact kernels:
+max-abs <= 1e-4 (O) and <= 1e-3 (gradients).
+"""
+import math
+
+import pytest
+import torch
+
+from oracle import corope_oracle as O
+from golden_io import load, MHA_CASES
+
+import CoROPE
+from CoROPE.co_rope_backward import co_rope_backward
+from CoROPE.co_rope_mqa_forward import co_rope_mqa_forward
+from CoROPE.forward import co_rope_forward
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+O_MAXABS, G_MAXABS, REL_L2 = 2e-2, 5e-2, 1e-2
+# kernel families exercised by the forward parity tests
+FWD_ALGOS = ["exact"]
+
+
+def rel_l2(x, y):
+    x, y = x.double().cpu(), y.double().cpu()
+    return ((x - y).norm() / y.norm().clamp_min(1e-30)).item()
+
+
+def maxabs(x, y):
+    return (x.double().cpu() - y.double().cpu()).abs().max().item()
+
+
+def inputs(B, H, S, D, seed, dtype, hkv=None):
+    """q, k, v, dO ~ N(0,1) drawn in that order from a CPU generator, cast to
+    dtype; returns (cuda tensors, fp64 CPU copies of the rounded values)."""
+    hkv = H if hkv is None else hkv
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, S, D, generator=g)
+    k = torch.randn(B, hkv, S, D, generator=g)
+    v = torch.randn(B, hkv, S, D, generator=g)
+    do = torch.randn(B, H, S, D, generator=g)
+    cast = [t.to(dtype) for t in (q, k, v, do)]
+    return [t.to(DEV) for t in cast], [t.double() for t in cast]
+
+
+def algos(dtype, D):
+    out = ["exact"]
+    if dtype in (torch.bfloat16, torch.float16) and D in (64, 128):
+        out.append("tensor")
+    return out
+
+
+# ---------------------------------------------------------------- golden ----
+@pytest.mark.parametrize("name", MHA_CASES)
+def test_golden_forward_backward_fp32_exact(name):
+    f = load(name)
+    q, k, v, do = (f[x].to(DEV) for x in ("q", "k", "v", "do"))
+    saved, o = co_rope_forward(q, k, v, f["sm_scale"], theta=f["theta"], algo="exact")
+    assert maxabs(o, f["o"]) < 1e-4
+    if "tri_m" in f:
+        assert maxabs(saved[4], f["tri_m"]) < 1e-4
+        assert maxabs(saved[6], f["tri_a"]) < 1e-4
+        assert ((saved[5].cpu() - f["tri_l"]).abs() / f["tri_l"]).max() < 1e-4
+    dq, dk, dv = co_rope_backward(saved, do, f["sm_scale"], f["theta"], algo="exact")
+    for mine, ref in ((dq, f["dq"]), (dk, f["dk"]), (dv, f["dv"])):
+        assert maxabs(mine, ref) < 1e-3 * max(1.0, ref.abs().max().item())
+
+
+def test_golden_mqa_bias_exact():
+    f = load("mqa_b1h4s48d16.npz")
+    q, k, v, bias = (f[x].to(DEV) for x in ("q", "k", "v", "bias"))
+    saved, o = co_rope_mqa_forward(q, k, v, f["sm_scale"], theta=f["theta"],
+                                   contextual_bias=bias, algo="exact")
+    assert maxabs(o, f["tri_o"]) < 1e-4
+    assert maxabs(saved[4], f["tri_m"]) < 1e-4
+    assert maxabs(saved[6], f["tri_a"]) < 1e-4
+
+
+# ------------------------------------------------------- sampled forward ----
+def check_rows(o, m, a, cpu, b, h, rows, sm, theta, hkv_div=1, bias=None):
+    qd, kd, vd = cpu[0], cpu[1], cpu[2]
+    ro, rm, rl, ra = O.forward_rows(qd[b, h], kd[b, h // hkv_div], vd[b, h // hkv_div], rows, sm,
+                                    theta, bias=bias)
+    got = o[b, h, rows].cpu()
+    assert maxabs(got, ro) < O_MAXABS
+    assert rel_l2(got, ro) < REL_L2
+    assert maxabs(m[b, h, rows], rm) < 2e-2
+    assert maxabs(a[b, h, rows], ra) < 2e-3 * max(1.0, ra.abs().max().item())
+
+
+def sample_rows(S, n=24):
+    r = torch.unique(torch.cat([torch.tensor([0, 1, S - 1, S - 2]),
+                                torch.randint(0, S, (n,), generator=torch.Generator().manual_seed(S))]))
+    return r
+
+
+@pytest.mark.parametrize("algo", FWD_ALGOS)
+def test_config2_forward_bf16_sampled(algo):
+    """B=4, H=32, S=4096, D=128 bf16, seed 1, theta 1e4 (fwd, fp32 LSE)."""
+    (q, k, v, _), cpu = inputs(4, 32, 4096, 128, 1, torch.bfloat16)
+    sm = 1 / math.sqrt(128)
+    saved, o, lse = co_rope_forward(q, k, v, sm, theta=1e4, algo=algo, return_lse=True)
+    torch.cuda.synchronize()
+    m, l, a = saved[4], saved[5], saved[6]
+    assert torch.isfinite(o).all() and torch.isfinite(lse).all()
+    assert torch.allclose(lse, m + torch.log(l), atol=1e-5)
+    rows = sample_rows(4096)
+    for b, h in ((0, 0), (3, 31), (1, 17)):
+        check_rows(o, m, a, cpu, b, h, rows, sm, 1e4)
+
+
+@pytest.mark.parametrize("algo", FWD_ALGOS)
+def test_config4_mqa_forward_bf16_sampled(algo):
+    """MQA: B=4, Hq=32, Hkv=1, S=8192, D=128 bf16, seed 3, theta 5e5."""
+    (q, k, v, _), cpu = inputs(4, 32, 8192, 128, 3, torch.bfloat16, hkv=1)
+    sm = 1 / math.sqrt(128)
+    saved, o = co_rope_mqa_forward(q, k, v, sm, theta=5e5, algo=algo)
+    torch.cuda.synchronize()
+    rows = sample_rows(8192, 12)
+    for b, h in ((0, 0), (3, 31), (2, 5)):
+        check_rows(o, saved[4], saved[6], cpu, b, h, rows, sm, 5e5, hkv_div=32)
+
+
+def test_mqa_reference_bias_draw_is_reproducible():
+    (q, k, v, _), cpu = inputs(2, 4, 256, 64, 9, torch.bfloat16, hkv=1)
+    torch.manual_seed(123)
+    s1, o1, b1 = co_rope_mqa_forward(q, k, v, None, contextual_bias="reference", return_bias=True)
+    torch.manual_seed(123)
+    expect = torch.tril(torch.randn(256, 256, device=DEV) * 0.02)
+    assert torch.equal(b1, expect)
+    rows = sample_rows(256, 8)
+    for b, h in ((0, 0), (1, 3)):
+        check_rows(o1, s1[4], s1[6], cpu, b, h, rows, 1 / 8, 1e4, hkv_div=4, bias=expect.double().cpu())
+
+
+# ------------------------------------------------------ full fwd + bwd ----
+@pytest.mark.parametrize("algo", ["exact"])
+def test_config3_forward_backward_bf16(algo):
+    """B=8, H=16, S=2048, D=64 bf16, seed 2, theta 1e4: dq, dk, dv of two
+    (b, h) slices against the closed-form oracle gradients."""
+    (q, k, v, do), cpu = inputs(8, 16, 2048, 64, 2, torch.bfloat16)
+    sm = 1 / math.sqrt(64)
+    saved, o = co_rope_forward(q, k, v, sm, theta=1e4, algo=algo)
+    dq, dk, dv = co_rope_backward(saved, do, sm, 1e4, algo=algo)
+    torch.cuda.synchronize()
+    for b, h in ((0, 0), (7, 15)):
+        sl = [t[b:b + 1, h:h + 1].float() for t in cpu]
+        ref = O.forward_dense(sl[0], sl[1], sl[2], sm, 1e4)
+        assert maxabs(o[b, h], ref["o"][0, 0]) < O_MAXABS
+        rq, rk, rv = O.backward_dense(sl[0], sl[1], sl[2], sl[3], sm, 1e4, row_chunk=32)
+        for mine, r in ((dq, rq), (dk, rk), (dv, rv)):
+            assert maxabs(mine[b, h], r[0, 0]) < G_MAXABS
+            assert rel_l2(mine[b, h], r[0, 0]) < REL_L2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("S,D,H,hkv", [(1, 64, 2, 2), (77, 32, 3, 3), (200, 128, 2, 1),
+                                        (129, 16, 4, 2), (64, 64, 2, 2)])
+def test_edge_shapes_forward_backward(dtype, S, D, H, hkv):
+    """Ragged S (not a tile multiple), S = 1, odd head counts, GQA/MQA
+    grouping in the backward, every dtype."""
+    (q, k, v, do), cpu = inputs(2, H, S, D, 11, dtype, hkv=hkv)
+    sm = 1 / math.sqrt(D)
+    fn = co_rope_forward if hkv == H else co_rope_mqa_forward
+    if hkv not in (1, H):
+        # grouped heads go through the C ABI's MQA entry (kv_heads < heads)
+        from CoROPE import _lib
+        o = torch.empty_like(q)
+        m, l, a = (torch.empty(2, H, S, device=DEV) for _ in range(3))
+        _lib.fwd(q, k, v, o, m, l, a, None, sm, 1e4, algo="exact", mqa=True)
+        saved = (q, k, v, o, m, l, a)
+    else:
+        saved, o = fn(q, k, v, sm, algo="exact")
+    dq, dk, dv = co_rope_backward(saved, do, sm, 1e4, algo="exact")
+    ref = O.forward_dense(*[t.float() for t in cpu[:3]], sm, 1e4)
+    rq, rk, rv = O.backward_dense(*[t.float() for t in cpu], sm, 1e4)
+    tol_o = 1e-4 if dtype == torch.float32 else O_MAXABS
+    tol_g = 1e-3 if dtype == torch.float32 else G_MAXABS
+    assert maxabs(o, ref["o"]) < tol_o
+    assert maxabs(saved[6], ref["a"]) < 1e-3
+    for mine, r in ((dq, rq), (dk, rk), (dv, rv)):
+        assert maxabs(mine, r) < tol_g * max(1.0, r.abs().max().item())
+
+
+def test_strided_inputs_and_module():
+    """CoRoPEAttention passes [B,S,H,D]-strided views; gradients through the
+    autograd Function equal those of contiguous inputs."""
+    torch.manual_seed(0)
+    B, S, H, D = 2, 96, 4, 32
+    base = torch.randn(3, B, S, H, D, device=DEV)
+    q, k, v = (base[i].transpose(1, 2).requires_grad_(True) for i in range(3))
+    out = CoROPE.CoRoPEAttentionFunction.apply(q, k, v, True, None, 10000.0)
+    g = torch.randn_like(out)
+    out.backward(g)
+    qc, kc, vc = (x.detach().contiguous().requires_grad_(True) for x in (q, k, v))
+    outc = CoROPE.CoRoPEAttentionFunction.apply(qc, kc, vc, True, None, 10000.0)
+    outc.backward(g.contiguous())
+    assert maxabs(out, outc) < 1e-5
+    for a_, b_ in ((q.grad, qc.grad), (k.grad, kc.grad), (v.grad, vc.grad)):
+        assert maxabs(a_, b_) < 1e-4
+    mod = CoROPE.CoRoPEAttention(128, 4).to(DEV)
+    x = torch.randn(2, 64, 128, device=DEV)
+    y = mod(x)
+    assert y.shape == x.shape and torch.isfinite(y).all()
+    y.sum().backward()
+    for p in mod.parameters():
+        assert p.grad is not None and torch.isfinite(p.grad).all()
+
+
+def test_linearity_in_v_full_size():
+    """O is linear in V for fixed q, k: a size-independent property checked
+    at the config-2 shape."""
+    (q, k, v, do), _ = inputs(4, 32, 4096, 128, 1, torch.bfloat16)
+    _, o1 = co_rope_forward(q, k, v, None)
+    _, o2 = co_rope_forward(q, k, do, None)
+    _, o3 = co_rope_forward(q, k, (v.float() + do.float()).bfloat16(), None)
+    assert rel_l2(o3, o1.float() + o2.float()) < 1e-2
+
+
+def test_state_bounds_full_size():
+    """0 <= A_t <= t+1, 1 <= L_t <= t+1, M_t finite -- at the config-2 shape."""
+    (q, k, v, _), _ = inputs(4, 32, 4096, 128, 1, torch.bfloat16)
+    saved, _ = co_rope_forward(q, k, v, None)
+    m, l, a = saved[4], saved[5], saved[6]
+    t1 = torch.arange(1, 4097, device=DEV, dtype=torch.float32)
+    assert (a >= 0).all() and (a <= t1 + 1e-3).all()
+    assert (l >= 1 - 1e-5).all() and (l <= t1 * (1 + 1e-5)).all()
+    assert torch.isfinite(m).all()
+
+
+def test_exact_and_tensor_agree_on_gate_sum():
+    (q, k, v, _), _ = inputs(1, 4, 1024, 128, 5, torch.bfloat16)
+    s1, o1 = co_rope_forward(q, k, v, None, algo="exact")
+    try:
+        s2, o2 = co_rope_forward(q, k, v, None, algo="tensor")
+    except NotImplementedError:
+        pytest.skip("tensor-core forward not built")
+    assert maxabs(s1[6], s2[6]) < 1e-2
+    assert maxabs(o1, o2) < O_MAXABS
