@@ -88,12 +88,19 @@ def load_library():
             lib.corope_bwd_workspace_bytes.restype = ctypes.c_size_t
             lib.corope_last_error.argtypes = []
             lib.corope_last_error.restype = ctypes.c_char_p
+            lib.corope_take_device_error.argtypes = []
+            lib.corope_take_device_error.restype = ctypes.c_int
             lib.corope_params_size.argtypes = [ctypes.c_int]
             lib.corope_params_size.restype = ctypes.c_size_t
             lib.corope_abi_version.argtypes = []
             lib.corope_abi_version.restype = ctypes.c_int
             _lib = lib
     return _lib
+
+
+def take_device_error() -> int:
+    """Read and clear the tensor-core kernels' device error word (0 = none)."""
+    return load_library().corope_take_device_error()
 
 
 def _dtype_code(t: torch.Tensor) -> int:

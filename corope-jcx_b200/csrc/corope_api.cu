@@ -15,6 +15,7 @@ bool exact_supports_head_dim(int D);
 // shape is outside its coverage
 bool tc_fwd_supported(const FwdArgs& a, int dtype);
 cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st);
+int tc_take_device_error();
 }  // namespace corope
 
 using namespace corope;
@@ -205,6 +206,8 @@ int corope_bwd(const corope_bwd_params_t* p, corope_stream_t stream) {
 }
 
 const char* corope_last_error(void) { return g_err; }
+
+int corope_take_device_error(void) { return tc_take_device_error(); }
 
 size_t corope_params_size(int which) {
   return which == 0 ? sizeof(corope_fwd_params_t) : which == 1 ? sizeof(corope_bwd_params_t) : 0;

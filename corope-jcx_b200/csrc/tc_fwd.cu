@@ -1,12 +1,654 @@
 // Tensor-core (tcgen05) CoRoPE forward for sm_100a.
+//
+// The rotated logit sm * <R(a_tj theta) q_t, k_j> is not a GEMM: the angle
+// depends on the (query, key) pair through the contextual position a_tj.
+// Keys are processed in windows of W = 16 from the diagonal down.  Inside a
+// window the position splits as a_tj = C_t + c0 + c0 * u_tj, where C_t is the
+// gate sum of the keys after the window (a per-row carry), c0 = (W-1)/2 and
+// u_tj in [-1, 1] is the scaled in-window position.  The rotation by
+// (C_t + c0) theta is applied to q_t once per row and window (the A operand
+// "v", kept in tensor memory), and the in-window rotation is expanded in
+// Chebyshev polynomials (Jacobi-Anger):
+//     exp(-i w u) = sum_m eps_m (-i)^m J_m(w) T_m(u),   w = c0 * theta_p,
+// so that  logit_tj = sum_m T_m(u_tj) G_m(t, j)  with
+//     G_m = v . K^(m),   K^(m)_p(j) = eps_m (-i)^m J_m(c0 theta_p) K_p(j),
+// one tensor-core GEMM per window (all m stacked along N).  Sixteen terms
+// keep the expansion error below 7e-5 for every frequency; coefficients
+// below 2e-6 are pruned, which shortens the K extent of the high-m terms.
+//
+// Roles per CTA (128 query rows of one (b, h), 384 threads):
+//   warps 0-3  row warps: gates, carries, A operand, Chebyshev (Clenshaw)
+//              combine, online softmax (stale-max rescaling), P, epilogue
+//   warp 4     TMA: Q once, K/V tiles of 64 keys (2 stages)
+//   warp 5     UMMA issue: gate GEMM Q K^T, G GEMM (A from TMEM), P V
+//   warps 8-11 build the K^(m) operand of each window in shared memory
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace corope {
 
-bool tc_fwd_supported(const FwdArgs& a, int dtype) { return false; }
+// First error recorded by a bounded wait of a tensor-core kernel (0: none).
+__device__ int g_corope_device_error = 0;
+
+// Read and clear the device error word (synchronises with the device).
+int tc_take_device_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_corope_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_corope_device_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+namespace tc {
+
+constexpr int kW = 16;       // keys per window
+constexpr int kM = 16;       // Chebyshev terms
+constexpr int kBM = 128;     // query rows per CTA
+constexpr int kKT = 64;      // keys per K/V tile
+constexpr int kThreads = 384;
+constexpr float kC0 = 7.5f;  // (kW - 1) / 2
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescale = 8.0f;  // stale-max headroom (log2 units)
+
+// error codes recorded by bounded waits
+enum : int {
+  kErrQ = 101, kErrKvEmpty, kErrKvFull, kErrSg, kErrG, kErrGEmpty, kErrB, kErrBEmpty, kErrAv,
+  kErrP, kErrO, kErrDrain
+};
+
+struct Params {
+  CUtensorMap tm_q, tm_k, tm_v;
+  void* o;
+  float *m, *l, *a, *lse;
+  const float* thetas;
+  const float* bias;
+  int64_t bias_rs;
+  int64_t os[3];
+  int B, H, Hkv, S;
+  float theta;
+  int nrow[8];          // B-operand rows read by K-step s (multiple of 16, or 0)
+  float coef[kM][64];   // eps_m J_m(c0 theta_p) * sm_scale * log2(e)
+};
+
+template <int D>
+struct Layout {
+  static constexpr int NS = D / 64;  // 64-element (128-byte) slabs
+  static constexpr int Q = 0;
+  static constexpr int K = Q + NS * 16384;      // [2 stages][NS][64 rows][128 B]
+  static constexpr int V = K + 2 * NS * 8192;
+  static constexpr int Bop = V + 2 * NS * 8192; // [2 halves][NS][128 rows][128 B]
+  static constexpr int COEF = Bop + 2 * NS * 16384;
+  static constexpr int TH = COEF + kM * (D / 2) * 4;
+  static constexpr int BAR = TH + (D / 2) * 4;
+  static constexpr int NBAR = 20;
+  static constexpr int SLOT = BAR + NBAR * 8;
+  static constexpr int TOTAL = SLOT + 16;
+  static constexpr int ALLOC = TOTAL + 1024;  // slack for 1024-byte alignment
+  // tensor-memory columns
+  static constexpr uint32_t T_O = 0;
+  static constexpr uint32_t T_G0 = D;
+  static constexpr uint32_t T_G1 = D + 128;
+  static constexpr uint32_t T_SG0 = D + 256;
+  static constexpr uint32_t T_SG1 = D + 272;
+  static constexpr uint32_t T_AV = D + 288;
+  static_assert(T_AV + D / 2 <= 512, "tensor memory overflow");
+};
+
+// barrier indices
+enum {
+  B_Q = 0, B_KVF = 1, B_KVE = 3, B_SG = 5, B_GF = 7, B_GE = 9, B_BF = 11, B_BE = 13, B_AV = 15,
+  B_P = 16, B_O = 17, B_DRAIN = 18
+};
+
+template <typename T> struct ElemTraits;
+template <> struct ElemTraits<__nv_bfloat16> {
+  static constexpr bool kBf16 = true;
+  __device__ static float lo(uint32_t x) { return __uint_as_float(x << 16); }
+  __device__ static float hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
+  __device__ static uint32_t pack(float a, float b) { return sm100::pack_bf16(a, b); }
+};
+template <> struct ElemTraits<__half> {
+  static constexpr bool kBf16 = false;
+  __device__ static float lo(uint32_t x) { return __half2float(__ushort_as_half((unsigned short)(x & 0xffffu))); }
+  __device__ static float hi(uint32_t x) { return __half2float(__ushort_as_half((unsigned short)(x >> 16))); }
+  __device__ static uint32_t pack(float a, float b) { return sm100::pack_f16(a, b); }
+};
+
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + __expf(-x)); }
+
+template <typename T, int D, bool HAS_BIAS>
+__global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant__ Params P) {
+  using L = Layout<D>;
+  using E = ElemTraits<T>;
+  using namespace sm100;
+  constexpr int NS = L::NS;
+  constexpr int NP = D / 2;
+  constexpr int KSTEPS = D / 16;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + L::SLOT);
+  float* s_coef = reinterpret_cast<float*>(smem + L::COEF);
+  float* s_th = reinterpret_cast<float*>(smem + L::TH);
+  int* err = &g_corope_device_error;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // longest query tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (P.H / P.Hkv);
+  const int q0 = qt * kBM;
+  const int S = P.S;
+  const int W0 = min(S - 1, q0 + kBM - 1) / kW;  // highest window
+  const int T0 = W0 / 4;                         // highest K/V tile
+
+  if (tid == 0) {
+    mbar_init(&bars[B_Q], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[B_KVF + i], 1);
+      mbar_init(&bars[B_KVE + i], 1 + 128);
+      mbar_init(&bars[B_SG + i], 1);
+      mbar_init(&bars[B_GF + i], 1);
+      mbar_init(&bars[B_GE + i], 128);
+      mbar_init(&bars[B_BF + i], 128);
+      mbar_init(&bars[B_BE + i], 1);
+    }
+    mbar_init(&bars[B_AV], 128);
+    mbar_init(&bars[B_P], 128);
+    mbar_init(&bars[B_O], 1);
+    mbar_init(&bars[B_DRAIN], 1);
+    fence_mbar_init();
+  }
+  for (int i = tid; i < kM * NP; i += kThreads) s_coef[i] = P.coef[i / NP][i % NP];
+  for (int p = tid; p < NP; p += kThreads) s_th[p] = theta_at(P.thetas, P.theta, p, D);
+  if (warp == 0) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t sQ = smem_u32(smem + L::Q);
+  const uint32_t sK = smem_u32(smem + L::K);
+  const uint32_t sV = smem_u32(smem + L::V);
+  const uint32_t sB = smem_u32(smem + L::Bop);
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA
+    if (lane == 0) {
+      prefetch_tmap(&P.tm_q);
+      prefetch_tmap(&P.tm_k);
+      prefetch_tmap(&P.tm_v);
+      mbar_expect_tx(&bars[B_Q], NS * 16384);
+      for (int s = 0; s < NS; ++s)
+        tma_load_4d(smem + L::Q + s * 16384, &P.tm_q, &bars[B_Q], 64 * s, q0, h, b);
+      int last_use[2] = {-1, -1};
+      for (int n = 0; T0 - n >= 0; ++n) {
+        const int tile = T0 - n, st = n & 1, u = n >> 1;
+        if (n >= 2 && !mbar_wait(&bars[B_KVE + st], (u - 1) & 1, err, kErrKvEmpty)) break;
+        mbar_expect_tx(&bars[B_KVF + st], 2 * NS * 8192);
+        for (int s = 0; s < NS; ++s) {
+          tma_load_4d(smem + L::K + (st * NS + s) * 8192, &P.tm_k, &bars[B_KVF + st], 64 * s,
+                      kKT * tile, hk, b);
+          tma_load_4d(smem + L::V + (st * NS + s) * 8192, &P.tm_v, &bars[B_KVF + st], 64 * s,
+                      kKT * tile, hk, b);
+        }
+        last_use[st] = u;
+      }
+      // no copy may still be in flight when the CTA exits
+      for (int st = 0; st < 2; ++st)
+        if (last_use[st] >= 0) mbar_wait(&bars[B_KVF + st], last_use[st] & 1, err, kErrDrain);
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ UMMA
+    if (lane == 0) {
+      const uint32_t id_gate = idesc_f16(128, 16, E::kBf16, false);
+      const uint32_t id_pv = idesc_f16(128, D, E::kBf16, true);
+      bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
+      tc_fence_after();
+      auto gate = [&](int w) -> bool {
+        const int n = T0 - w / 4, st = n & 1;
+        if (!mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) return false;
+        tc_fence_after();
+        const uint32_t kt = sK + st * NS * 8192 + (w & 3) * kW * 128;
+        const uint32_t dst = tmem + ((w & 1) ? L::T_SG1 : L::T_SG0);
+#pragma unroll
+        for (int s = 0; s < KSTEPS; ++s) {
+          mma_ss(dst, sdesc_kmajor(sQ + (s >> 2) * 16384 + 32 * (s & 3)),
+                 sdesc_kmajor(kt + (s >> 2) * 8192 + 32 * (s & 3)), id_gate, s > 0);
+        }
+        mma_commit(&bars[B_SG + (w & 1)]);
+        return true;
+      };
+      auto pv = [&](int w) -> bool {
+        if (!mbar_wait(&bars[B_P], (W0 - w) & 1, err, kErrP)) return false;
+        tc_fence_after();
+        const int n = T0 - w / 4, st = n & 1;
+        const uint32_t vt = sV + st * NS * 8192 + (w & 3) * kW * 128;
+        const uint32_t pa = tmem + ((w & 1) ? L::T_SG1 : L::T_SG0);
+        mma_ts(tmem + L::T_O, pa, sdesc_mnmajor(vt, 8192), id_pv, w != W0);
+        mma_commit(&bars[B_O]);
+        if ((w & 3) == 0) mma_commit(&bars[B_KVE + st]);
+        return true;
+      };
+      if (ok) ok = gate(W0);
+      for (int w = W0; ok && w >= 0; --w) {
+        const int k = W0 - w;
+        if (!(ok = mbar_wait(&bars[B_AV], k & 1, err, kErrAv))) break;
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          ok = mbar_wait(&bars[B_BF + hh], k & 1, err, kErrB);
+          if (ok && k > 0) ok = mbar_wait(&bars[B_GE + hh], (k - 1) & 1, err, kErrGEmpty);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t dst = tmem + (hh ? L::T_G1 : L::T_G0);
+#pragma unroll
+          for (int s = 0; s < KSTEPS; ++s) {
+            const int nr = P.nrow[s];
+            if (nr == 0) break;
+            mma_ts(dst, tmem + L::T_AV + 8 * s,
+                   sdesc_kmajor(sB + (hh * NS + (s >> 2)) * 16384 + 32 * (s & 3)),
+                   idesc_f16(128, nr, E::kBf16, false), s > 0);
+          }
+          mma_commit(&bars[B_GF + hh]);
+          mma_commit(&bars[B_BE + hh]);
+        }
+        if (!ok) break;
+        if (w < W0 && !(ok = pv(w + 1))) break;
+        if (w >= 1 && !(ok = gate(w - 1))) break;
+      }
+      if (ok) pv(0);
+      mma_commit(&bars[B_DRAIN]);
+      mbar_wait(&bars[B_DRAIN], 0, err, kErrDrain);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------- K^(m) operand builder
+    const int gt = tid - 256;
+    for (int w = W0; w >= 0; --w) {
+      const int k = W0 - w;
+      const int n = T0 - w / 4, st = n & 1;
+      if (!mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) break;
+      bool ok = true;
+      for (int hh = 0; hh < 2; ++hh) {
+        if (k > 0 && !(ok = mbar_wait(&bars[B_BE + hh], (k - 1) & 1, err, kErrBEmpty))) break;
+        const uint8_t* kt = smem + L::K + st * NS * 8192;
+        uint8_t* bt = smem + L::Bop + hh * NS * 16384;
+        for (int it = gt; it < 128 * (D / 8); it += 128) {
+          const int r = it & 127, c = it >> 7;  // row (m, jj), 16-byte chunk
+          if (r >= P.nrow[c >> 1]) continue;
+          const int m = r >> 3, kr = (w & 3) * kW + hh * 8 + (r & 7);
+          const uint4 kv = *reinterpret_cast<const uint4*>(
+              kt + (c >> 3) * 8192 + sw128_offset(kr, c & 7));
+          const float4 cf = *reinterpret_cast<const float4*>(s_coef + m * NP + 4 * c);
+          const uint32_t in[4] = {kv.x, kv.y, kv.z, kv.w};
+          const float cfa[4] = {cf.x, cf.y, cf.z, cf.w};
+          uint32_t out[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float ke = E::lo(in[i]) * cfa[i], ko = E::hi(in[i]) * cfa[i];
+            float re, im;
+            switch (m & 3) {
+              case 0: re = ke; im = ko; break;
+              case 1: re = ko; im = -ke; break;
+              case 2: re = -ke; im = -ko; break;
+              default: re = -ko; im = ke; break;
+            }
+            out[i] = E::pack(re, im);
+          }
+          *reinterpret_cast<uint4*>(bt + (c >> 3) * 16384 + sw128_offset(r, c & 7)) =
+              make_uint4(out[0], out[1], out[2], out[3]);
+        }
+        fence_async_smem();
+        mbar_arrive(&bars[B_BF + hh]);
+      }
+      if (!ok) break;
+      if ((w & 3) == 0) mbar_arrive(&bars[B_KVE + st]);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ row warps
+    const int r = tid;
+    const int t = q0 + r;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint8_t* qrow = smem + L::Q;
+    float carry = 0.f;                     // gate sum of keys after the window
+    float m_used = -1e30f, m_true = -INFINITY, lsum = 0.f;
+    bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
+
+    // A operand of one window: v = R((carry + c0) theta) q_t in tensor memory
+    auto build_a = [&](float cw) {
+      const float base = cw + kC0;
+#pragma unroll
+      for (int g = 0; g < NP / 16; ++g) {
+        uint32_t regs[16];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = g * 4 + cc;  // 16-byte chunk of the row (4 pairs)
+          const uint4 qv = *reinterpret_cast<const uint4*>(
+              qrow + (c >> 3) * 16384 + sw128_offset(r, c & 7));
+          const uint32_t in[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int p = 4 * c + i;
+            float sn, cs;
+            sincos_reduced(base * s_th[p], &sn, &cs);
+            const float qe = E::lo(in[i]), qo = E::hi(in[i]);
+            regs[cc * 4 + i] = E::pack(qe * cs - qo * sn, qe * sn + qo * cs);
+          }
+        }
+        tmem_st16(lane_base + L::T_AV + 16 * g, regs);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars[B_AV]);
+    };
+
+    // Clenshaw combine of 8 keys from one G half: f_j = sum_m T_m(u_j) G_m
+    auto combine = [&](uint32_t gcol, const float (&u2)[8], const float (&uu)[8],
+                       float (&f)[8], int ge_bar) {
+      float b1[8], b2[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) { b1[j] = 0.f; b2[j] = 0.f; }
+#pragma unroll
+      for (int batch = 0; batch < 2; ++batch) {
+        uint32_t g[4][16];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tmem_ld16(lane_base + gcol + 16 * (7 - batch * 4 - i), g[i]);
+        tmem_wait_ld();
+        if (batch == 1) {
+          tc_fence_before();
+          mbar_arrive(&bars[ge_bar]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = 7 - batch * 4 - i;
+#pragma unroll
+          for (int mm = 1; mm >= 0; --mm) {
+            const int m = 2 * c + mm;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float a = __uint_as_float(g[i][mm * 8 + j]);
+              if (m > 0) {
+                const float bn = fmaf(u2[j], b1[j], a - b2[j]);
+                b2[j] = b1[j];
+                b1[j] = bn;
+              } else {
+                f[j] = fmaf(uu[j], b1[j], a - b2[j]);
+              }
+            }
+          }
+        }
+      }
+    };
+
+    if (ok) {
+      tc_fence_after();
+      build_a(0.f);
+    }
+    for (int w = W0; ok && w >= 0; --w) {
+      const int k = W0 - w;
+      const int j0 = w * kW;
+      const uint32_t sg = (w & 1) ? L::T_SG1 : L::T_SG0;
+      // gates of the window
+      if (!(ok = mbar_wait(&bars[B_SG + (w & 1)], ((W0 - w) >> 1) & 1, err, kErrSg))) break;
+      tc_fence_after();
+      uint32_t sraw[16];
+      tmem_ld16(lane_base + sg, sraw);
+      tmem_wait_ld();
+      float uu[16], u2[16];
+      float acc = 0.f;
+#pragma unroll
+      for (int jj = 15; jj >= 0; --jj) {
+        const float z = (j0 + jj <= t) ? sigmoid_f(__uint_as_float(sraw[jj])) : 0.f;
+        uu[jj] = fmaf(acc, 1.0f / kC0, -1.0f);
+        u2[jj] = 2.0f * uu[jj];
+        acc += z;
+      }
+      const float carry_next = carry + acc;
+      float lg[16];
+      // first half of the window
+      if (!(ok = mbar_wait(&bars[B_GF + 0], k & 1, err, kErrG))) break;
+      tc_fence_after();
+      {
+        float f[8], a8[8], b8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { a8[j] = u2[j]; b8[j] = uu[j]; }
+        combine(L::T_G0, a8, b8, f, B_GE + 0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) lg[j] = f[j];
+      }
+      // second half; once its GEMM is done the A operand is free again
+      if (!(ok = mbar_wait(&bars[B_GF + 1], k & 1, err, kErrG))) break;
+      tc_fence_after();
+      if (w > 0) build_a(carry_next);
+      {
+        float f[8], a8[8], b8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { a8[j] = u2[8 + j]; b8[j] = uu[8 + j]; }
+        combine(L::T_G1, a8, b8, f, B_GE + 1);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) lg[8 + j] = f[j];
+      }
+      // online softmax (log2 units) with stale-max rescaling
+      float mx = -INFINITY;
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        if (HAS_BIAS && j0 + jj <= t) lg[jj] = fmaf(P.bias[(int64_t)t * P.bias_rs + j0 + jj], kLog2e, lg[jj]);
+        lg[jj] = (j0 + jj <= t) ? lg[jj] : -INFINITY;
+        mx = fmaxf(mx, lg[jj]);
+      }
+      m_true = fmaxf(m_true, mx);
+      if (k > 0) {
+        if (!(ok = mbar_wait(&bars[B_O], (k - 1) & 1, err, kErrO))) break;
+        tc_fence_after();
+      }
+      const bool resc = mx > m_used + kRescale;
+      const float alpha = resc ? exp2f(m_used - mx) : 1.0f;
+      if (resc) m_used = mx;
+      lsum *= alpha;
+      if (k > 0 && __any_sync(0xffffffffu, resc)) {
+#pragma unroll 1
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld16(lane_base + L::T_O + 16 * c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st16(lane_base + L::T_O + 16 * c, o);
+        }
+      }
+      uint32_t pk[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float p0 = exp2f(lg[2 * i] - m_used), p1 = exp2f(lg[2 * i + 1] - m_used);
+        lsum += p0 + p1;
+        pk[i] = E::pack(p0, p1);
+      }
+      tmem_st8(lane_base + sg, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars[B_P]);
+      carry = carry_next;
+    }
+    // epilogue
+    if (ok) ok = mbar_wait(&bars[B_O], W0 & 1, err, kErrO);
+    if (ok) {
+      tc_fence_after();
+      const float inv = 1.0f / lsum;
+      T* orow = reinterpret_cast<T*>(P.o) + b * P.os[0] + h * P.os[1] + (int64_t)t * P.os[2];
+#pragma unroll 1
+      for (int c = 0; c < D / 16; ++c) {
+        uint32_t o[16];
+        tmem_ld16(lane_base + L::T_O + 16 * c, o);
+        tmem_wait_ld();
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          pk[i] = E::pack(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+        if (t < S) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + 16 * c);
+          dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+      }
+      if (t < S) {
+        const int64_t ri = ((int64_t)b * P.H + h) * S + t;
+        const float M = m_true * 0.6931471805599453f;
+        const float Lv = lsum * exp2f(m_used - m_true);
+        if (P.m) P.m[ri] = M;
+        if (P.l) P.l[ri] = Lv;
+        if (P.a) P.a[ri] = carry;
+        if (P.lse) P.lse[ri] = M + logf(Lv);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ------------------------------------------------------------------ host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// [B, H, S, D] tensor (element strides) -> 4-D map with a {64, rows} box
+static bool encode(CUtensorMap* m, const void* ptr, int dtype, int B, int H, int S, int D,
+                   const int64_t* st, int box_rows) {
+  EncodeTiledFn enc = get_encoder();
+  if (!enc) return false;
+  const cuuint64_t es = 2;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)st[2] * es, (cuuint64_t)st[1] * es, (cuuint64_t)st[0] * es};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, dtype == COROPE_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Bessel function of the first kind, integer order, by its power series
+// (|x| <= 8 here, where the series converges quickly in double precision).
+static double bessel_j(int m, double x) {
+  double term = 1.0;
+  for (int i = 1; i <= m; ++i) term *= (x / 2.0) / i;
+  double sum = term;
+  const double q = -(x * x) / 4.0;
+  for (int k = 1; k < 80; ++k) {
+    term *= q / (k * (double)(k + m));
+    sum += term;
+    if (std::fabs(term) < 1e-18 * std::fabs(sum) + 1e-300) break;
+  }
+  return sum;
+}
+
+// Chebyshev coefficients (with sm_scale * log2 e folded in) and the pruned
+// K extent of each term for one (D, theta, sm_scale).
+static void fill_coefficients(Params& p, int D, float theta, float sm_scale) {
+  const int NP = D / 2;
+  int kd[kM];
+  for (int m = 0; m < kM; ++m) {
+    int need = 0;
+    for (int q = 0; q < NP; ++q) {
+      const double th = 1.0 / std::pow((double)theta, (double)(2 * q) / (double)D);
+      const double beta = (m == 0 ? 1.0 : 2.0) * bessel_j(m, kC0 * th);
+      p.coef[m][q] = (float)(beta * sm_scale * kLog2e);
+      if (std::fabs(beta) > 2e-6) need = q + 1;
+    }
+    for (int q = NP; q < 64; ++q) p.coef[m][q] = 0.f;
+    kd[m] = std::max(1, (2 * need + 15) / 16);
+  }
+  for (int m = kM - 2; m >= 0; --m) kd[m] = std::max(kd[m], kd[m + 1]);
+  for (int s = 0; s < 8; ++s) {
+    int nm = 0;
+    for (int m = 0; m < kM; ++m) nm += kd[m] > s;
+    nm = (nm + 1) & ~1;
+    p.nrow[s] = (s < D / 16) ? 8 * nm : 0;
+  }
+}
+
+template <typename T, int D>
+static cudaError_t launch_t(const Params& p, const FwdArgs& a, cudaStream_t st) {
+  using L = Layout<D>;
+  dim3 grid((a.S + kBM - 1) / kBM, a.H, a.B);
+  cudaError_t e;
+  if (a.bias) {
+    auto kern = fwd_kernel<T, D, true>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kThreads, L::ALLOC, st>>>(p);
+  } else {
+    auto kern = fwd_kernel<T, D, false>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kThreads, L::ALLOC, st>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace tc
+
+static bool rows_ok(const void* ptr, const int64_t* st) {
+  return (reinterpret_cast<uintptr_t>(ptr) % 16) == 0 && (st[0] * 2) % 16 == 0 &&
+         (st[1] * 2) % 16 == 0 && (st[2] * 2) % 16 == 0;
+}
+
+bool tc_fwd_supported(const FwdArgs& a, int dtype) {
+  if (dtype != COROPE_DTYPE_BF16 && dtype != COROPE_DTYPE_F16) return false;
+  if (a.D != 64 && a.D != 128) return false;
+  if (!rows_ok(a.q, a.qs) || !rows_ok(a.k, a.ks) || !rows_ok(a.v, a.vs) || !rows_ok(a.o, a.os))
+    return false;
+  if (a.bias && (reinterpret_cast<uintptr_t>(a.bias) % 4) != 0) return false;
+  return tc::get_encoder() != nullptr;
+}
 
 cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st) {
-  return cudaErrorNotSupported;
+  using namespace tc;
+  static Params p;  // large (>4 KB); filled per call under a lock
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  std::memset(&p, 0, sizeof(p));
+  if (!encode(&p.tm_q, a.q, dtype, a.B, a.H, a.S, a.D, a.qs, kBM) ||
+      !encode(&p.tm_k, a.k, dtype, a.B, a.Hkv, a.S, a.D, a.ks, kKT) ||
+      !encode(&p.tm_v, a.v, dtype, a.B, a.Hkv, a.S, a.D, a.vs, kKT))
+    return cudaErrorInvalidValue;
+  p.o = a.o;
+  p.m = a.m; p.l = a.l; p.a = a.a; p.lse = a.lse;
+  p.thetas = a.thetas; p.theta = a.theta;
+  p.bias = a.bias; p.bias_rs = a.bias_rs;
+  for (int i = 0; i < 3; ++i) p.os[i] = a.os[i];
+  p.B = a.B; p.H = a.H; p.Hkv = a.Hkv; p.S = a.S;
+  fill_coefficients(p, a.D, a.theta, a.sm_scale);
+  const bool bf = dtype == COROPE_DTYPE_BF16;
+  if (a.D == 64)
+    return bf ? launch_t<__nv_bfloat16, 64>(p, a, st) : launch_t<__half, 64>(p, a, st);
+  return bf ? launch_t<__nv_bfloat16, 128>(p, a, st) : launch_t<__half, 128>(p, a, st);
 }
 
 }  // namespace corope

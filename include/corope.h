@@ -121,6 +121,12 @@ int corope_bwd(const corope_bwd_params_t *p, corope_stream_t stream);
 /* Message for the last non-zero status returned on this thread. */
 const char *corope_last_error(void);
 
+/* Error word of the tensor-core kernels: every wait inside them is bounded
+ * in time; a wait that runs out records a non-zero code here and the kernel
+ * returns early instead of hanging.  Returns the code (0 = none, -1 = the
+ * read failed) and clears it.  Synchronises with the device. */
+int corope_take_device_error(void);
+
 /* sizeof(corope_fwd_params_t) for which == 0, sizeof(corope_bwd_params_t)
  * for which == 1, else 0; lets FFI bindings check their struct layout. */
 size_t corope_params_size(int which);

@@ -22,7 +22,7 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 O_MAXABS, G_MAXABS, REL_L2 = 2e-2, 5e-2, 1e-2
 # kernel families exercised by the forward parity tests
-FWD_ALGOS = ["exact"]
+FWD_ALGOS = ["exact", "tensor"]
 
 
 def rel_l2(x, y):
@@ -241,3 +241,35 @@ def test_exact_and_tensor_agree_on_gate_sum():
         pytest.skip("tensor-core forward not built")
     assert maxabs(s1[6], s2[6]) < 1e-2
     assert maxabs(o1, o2) < O_MAXABS
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("S,D,theta", [(1, 64, 1e4), (40, 128, 1e4), (300, 64, 1e4),
+                                        (513, 128, 5e5), (1024, 128, 1e4)])
+def test_tensor_forward_small_shapes(dtype, S, D, theta):
+    """Tensor-core forward against the full oracle: ragged S (partial
+    windows, tiles and query tiles), both head dims, both half types."""
+    (q, k, v, _), cpu = inputs(2, 3, S, D, 21, dtype)
+    sm = 1 / math.sqrt(D)
+    saved, o, lse = co_rope_forward(q, k, v, sm, theta=theta, algo="tensor", return_lse=True)
+    torch.cuda.synchronize()
+    from CoROPE import _lib
+    assert _lib.take_device_error() == 0
+    ref = O.forward_dense(*[t.double() for t in cpu[:3]], sm, theta)
+    assert maxabs(o, ref["o"]) < O_MAXABS
+    assert rel_l2(o, ref["o"]) < REL_L2
+    assert maxabs(saved[4], ref["m"]) < 2e-2
+    assert maxabs(saved[6], ref["a"]) < 1e-3 * max(1.0, S / 100)
+    assert maxabs(lse, ref["lse"]) < 2e-2
+
+
+def test_tensor_forward_strided_module_layout():
+    """[B,S,H,D]-strided views (the CoRoPEAttention layout) go straight to
+    the TMA descriptors."""
+    torch.manual_seed(3)
+    B, S, H, D = 2, 200, 4, 128
+    base = torch.randn(3, B, S, H, D, device=DEV).bfloat16()
+    q, k, v = (base[i].transpose(1, 2) for i in range(3))
+    _, o1 = co_rope_forward(q, k, v, None, algo="tensor")
+    _, o2 = co_rope_forward(q.contiguous(), k.contiguous(), v.contiguous(), None, algo="tensor")
+    assert maxabs(o1, o2) == 0.0
