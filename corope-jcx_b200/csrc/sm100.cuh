@@ -49,19 +49,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase.  Gives up after ~`limit` clock cycles,
-// records `code` in *err (first error wins) and returns false; callers then
-// skip the rest of their work so the kernel always terminates.
+// Bounded wait on an mbarrier phase.  Spins on try_wait only; every 1024
+// polls it reads the clock, and after ~`limit` cycles it records `code` in
+// *err (first error wins) and returns false so the caller can skip the rest
+// of its work and the kernel always terminates.  Once a wait has lasted
+// ~2^24 cycles it also gives up early when another thread already recorded
+// an error.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
                                           long long limit = 4000000000ll) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (true) {
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*(volatile int*)err != 0) return false;
-    if (clock64() - t0 > limit) {
-      atomicCAS(err, 0, code);
-      return false;
+    if ((i & 1023u) == 0) {
+      const long long dt = clock64() - t0;
+      if (dt > limit) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+      if (dt > (1ll << 24) && *(volatile int*)err != 0) return false;
     }
   }
 }
@@ -77,6 +83,16 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Re-balance registers between warpgroups (all warps of the warpgroup
+// execute it).  The increases draw on what the decreases released; the
+// launch budget (threads x registers at launch) must cover the final split.
+template <int N> __device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N> __device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // generic-proxy shared-memory writes -> visible to the async proxy (UMMA)
@@ -196,6 +212,26 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool b
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
          ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ float4 lds128f(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
 }
 
 // byte offset of 16-byte chunk `c` (0..7) of row `r` in a 128B-swizzled tile

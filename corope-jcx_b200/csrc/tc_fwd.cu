@@ -12,16 +12,20 @@
 //     exp(-i w u) = sum_m eps_m (-i)^m J_m(w) T_m(u),   w = c0 * theta_p,
 // so that  logit_tj = sum_m T_m(u_tj) G_m(t, j)  with
 //     G_m = v . K^(m),   K^(m)_p(j) = eps_m (-i)^m J_m(c0 theta_p) K_p(j),
-// one tensor-core GEMM per window (all m stacked along N).  Sixteen terms
-// keep the expansion error below 7e-5 for every frequency; coefficients
-// below 2e-6 are pruned, which shortens the K extent of the high-m terms.
+// one tensor-core GEMM per window (all m stacked along N).  Fourteen terms
+// keep the expansion error below 1.1e-3 at the highest frequency (w = 7.5)
+// and far below it elsewhere -- under the rounding of the 16-bit GEMM
+// operands; coefficients below 2e-6 are pruned, which shortens the K extent
+// of the high-m terms.
 //
 // Roles per CTA (128 query rows of one (b, h), 384 threads):
 //   warps 0-3  row warps: gates, carries, A operand, Chebyshev (Clenshaw)
 //              combine, online softmax (stale-max rescaling), P, epilogue
 //   warp 4     TMA: Q once, K/V tiles of 64 keys (2 stages)
-//   warp 5     UMMA issue: gate GEMM Q K^T, G GEMM (A from TMEM), P V
+//   warp 5     UMMA issue of the G GEMM (A operand from tensor memory)
+//   warp 6     UMMA issue of the gate GEMM Q K^T and of P V
 //   warps 8-11 build the K^(m) operand of each window in shared memory
+//              (double-buffered when it fits)
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -48,7 +52,7 @@ int tc_take_device_error() {
 namespace tc {
 
 constexpr int kW = 16;       // keys per window
-constexpr int kM = 16;       // Chebyshev terms
+constexpr int kM = 14;       // Chebyshev terms
 constexpr int kBM = 128;     // query rows per CTA
 constexpr int kKT = 64;      // keys per K/V tile
 constexpr int kThreads = 384;
@@ -73,6 +77,9 @@ struct Params {
   int B, H, Hkv, S;
   float theta;
   int nrow[8];          // B-operand rows read by K-step s (multiple of 16, or 0)
+  int nb;               // K^(m) buffers per half window (1 or 2)
+  int b_slab_off[2];    // byte offset of each 64-element slab in a buffer
+  int b_buf_bytes;      // bytes of one buffer (multiple of 1024)
   float coef[kM][64];   // eps_m J_m(c0 theta_p) * sm_scale * log2(e)
 };
 
@@ -82,28 +89,36 @@ struct Layout {
   static constexpr int Q = 0;
   static constexpr int K = Q + NS * 16384;      // [2 stages][NS][64 rows][128 B]
   static constexpr int V = K + 2 * NS * 8192;
-  static constexpr int Bop = V + 2 * NS * 8192; // [2 halves][NS][128 rows][128 B]
-  static constexpr int COEF = Bop + 2 * NS * 16384;
+  static constexpr int COEF = V + 2 * NS * 8192;
   static constexpr int TH = COEF + kM * (D / 2) * 4;
   static constexpr int BAR = TH + (D / 2) * 4;
-  static constexpr int NBAR = 20;
+  static constexpr int NBAR = 32;
   static constexpr int SLOT = BAR + NBAR * 8;
-  static constexpr int TOTAL = SLOT + 16;
-  static constexpr int ALLOC = TOTAL + 1024;  // slack for 1024-byte alignment
+  // builder work items: [kMaxItems][128 threads] x (uint2)
+  static constexpr int MAX_ITEMS = (2 * 8 * 8 * kM + 127) / 128;
+  static constexpr int ITEMS = (SLOT + 16 + 15) & ~15;
+  // K^(m) buffers [2 halves][nb][b_buf_bytes] follow, 1024-aligned
+  static constexpr int BOP = (ITEMS + MAX_ITEMS * 128 * 8 + 1023) & ~1023;
   // tensor-memory columns
+  static constexpr uint32_t GW = 8 * kM;  // columns of one G half
   static constexpr uint32_t T_O = 0;
   static constexpr uint32_t T_G0 = D;
-  static constexpr uint32_t T_G1 = D + 128;
-  static constexpr uint32_t T_SG0 = D + 256;
-  static constexpr uint32_t T_SG1 = D + 272;
-  static constexpr uint32_t T_AV = D + 288;
-  static_assert(T_AV + D / 2 <= 512, "tensor memory overflow");
+  static constexpr uint32_t T_G1 = D + GW;
+  static constexpr uint32_t T_SG0 = D + 2 * GW;
+  static constexpr uint32_t T_SG1 = T_SG0 + 16;
+  static constexpr uint32_t T_AV0 = T_SG1 + 16;   // A operand, two buffers
+  static constexpr uint32_t T_AV1 = T_AV0 + D / 2;
+  static_assert(T_AV1 + D / 2 <= 512, "tensor memory overflow");
 };
+
+constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per block
 
 // barrier indices
 enum {
-  B_Q = 0, B_KVF = 1, B_KVE = 3, B_SG = 5, B_GF = 7, B_GE = 9, B_BF = 11, B_BE = 13, B_AV = 15,
-  B_P = 16, B_O = 17, B_DRAIN = 18
+  B_Q = 0, B_KVF = 1, B_KVE = 3, B_SG = 5, B_GF = 7, B_GE = 9,
+  B_BF = 11,  // [half][buffer] -> B_BF + 2 * half + buffer
+  B_BE = 15,  // [half][buffer]
+  B_AV = 19, B_P = 20, B_O = 21, B_DRAIN = 22, B_DRAIN2 = 23
 };
 
 template <typename T> struct ElemTraits;
@@ -157,6 +172,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       mbar_init(&bars[B_SG + i], 1);
       mbar_init(&bars[B_GF + i], 1);
       mbar_init(&bars[B_GE + i], 128);
+    }
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&bars[B_BF + i], 128);
       mbar_init(&bars[B_BE + i], 1);
     }
@@ -164,6 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
     mbar_init(&bars[B_P], 128);
     mbar_init(&bars[B_O], 1);
     mbar_init(&bars[B_DRAIN], 1);
+    mbar_init(&bars[B_DRAIN2], 1);
     fence_mbar_init();
   }
   for (int i = tid; i < kM * NP; i += kThreads) s_coef[i] = P.coef[i / NP][i % NP];
@@ -179,7 +197,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
   const uint32_t sQ = smem_u32(smem + L::Q);
   const uint32_t sK = smem_u32(smem + L::K);
   const uint32_t sV = smem_u32(smem + L::V);
-  const uint32_t sB = smem_u32(smem + L::Bop);
+  const uint32_t sB = smem_u32(smem + L::BOP);
+  const uint32_t s_th_u = smem_u32(s_th);
+  const uint32_t s_coef_u = smem_u32(s_coef);
+  const int nb = P.nb;
 
   if (warp == 4) {
     // ------------------------------------------------------------ TMA
@@ -208,7 +229,36 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         if (last_use[st] >= 0) mbar_wait(&bars[B_KVF + st], last_use[st] & 1, err, kErrDrain);
     }
   } else if (warp == 5) {
-    // ------------------------------------------------------------ UMMA
+    // ------------------------------------------------------ UMMA: G GEMM
+    if (lane == 0) {
+      bool ok = true;
+      for (int w = W0; ok && w >= 0; --w) {
+        const int k = W0 - w, buf = k % nb, use = k / nb;
+        if (!(ok = mbar_wait(&bars[B_AV], k & 1, err, kErrAv))) break;
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          ok = mbar_wait(&bars[B_BF + 2 * hh + buf], use & 1, err, kErrB);
+          if (ok && k > 0) ok = mbar_wait(&bars[B_GE + hh], (k - 1) & 1, err, kErrGEmpty);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t dst = tmem + (hh ? L::T_G1 : L::T_G0);
+          const uint32_t bb = sB + (hh * nb + buf) * P.b_buf_bytes;
+#pragma unroll
+          for (int s = 0; s < KSTEPS; ++s) {
+            const int nr = P.nrow[s];
+            if (nr == 0) break;
+            mma_ts(dst, tmem + ((w & 1) ? L::T_AV1 : L::T_AV0) + 8 * s,
+                   sdesc_kmajor(bb + P.b_slab_off[s >> 2] + 32 * (s & 3)),
+                   idesc_f16(128, nr, E::kBf16, false), s > 0);
+          }
+          mma_commit(&bars[B_GF + hh]);
+          mma_commit(&bars[B_BE + 2 * hh + buf]);
+        }
+      }
+      mma_commit(&bars[B_DRAIN]);
+      mbar_wait(&bars[B_DRAIN], 0, err, kErrDrain);
+    }
+  } else if (warp == 6) {
+    // ------------------------------------------- UMMA: gate GEMM and P V
     if (lane == 0) {
       const uint32_t id_gate = idesc_f16(128, 16, E::kBf16, false);
       const uint32_t id_pv = idesc_f16(128, D, E::kBf16, true);
@@ -221,15 +271,16 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         const uint32_t kt = sK + st * NS * 8192 + (w & 3) * kW * 128;
         const uint32_t dst = tmem + ((w & 1) ? L::T_SG1 : L::T_SG0);
 #pragma unroll
-        for (int s = 0; s < KSTEPS; ++s) {
+        for (int s = 0; s < KSTEPS; ++s)
           mma_ss(dst, sdesc_kmajor(sQ + (s >> 2) * 16384 + 32 * (s & 3)),
                  sdesc_kmajor(kt + (s >> 2) * 8192 + 32 * (s & 3)), id_gate, s > 0);
-        }
         mma_commit(&bars[B_SG + (w & 1)]);
         return true;
       };
-      auto pv = [&](int w) -> bool {
-        if (!mbar_wait(&bars[B_P], (W0 - w) & 1, err, kErrP)) return false;
+      if (ok) ok = gate(W0);
+      if (ok && W0 >= 1) ok = gate(W0 - 1);
+      for (int w = W0; ok && w >= 0; --w) {
+        if (!(ok = mbar_wait(&bars[B_P], (W0 - w) & 1, err, kErrP))) break;
         tc_fence_after();
         const int n = T0 - w / 4, st = n & 1;
         const uint32_t vt = sV + st * NS * 8192 + (w & 3) * kW * 128;
@@ -237,76 +288,98 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         mma_ts(tmem + L::T_O, pa, sdesc_mnmajor(vt, 8192), id_pv, w != W0);
         mma_commit(&bars[B_O]);
         if ((w & 3) == 0) mma_commit(&bars[B_KVE + st]);
-        return true;
-      };
-      if (ok) ok = gate(W0);
-      for (int w = W0; ok && w >= 0; --w) {
-        const int k = W0 - w;
-        if (!(ok = mbar_wait(&bars[B_AV], k & 1, err, kErrAv))) break;
-        for (int hh = 0; hh < 2 && ok; ++hh) {
-          ok = mbar_wait(&bars[B_BF + hh], k & 1, err, kErrB);
-          if (ok && k > 0) ok = mbar_wait(&bars[B_GE + hh], (k - 1) & 1, err, kErrGEmpty);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t dst = tmem + (hh ? L::T_G1 : L::T_G0);
-#pragma unroll
-          for (int s = 0; s < KSTEPS; ++s) {
-            const int nr = P.nrow[s];
-            if (nr == 0) break;
-            mma_ts(dst, tmem + L::T_AV + 8 * s,
-                   sdesc_kmajor(sB + (hh * NS + (s >> 2)) * 16384 + 32 * (s & 3)),
-                   idesc_f16(128, nr, E::kBf16, false), s > 0);
-          }
-          mma_commit(&bars[B_GF + hh]);
-          mma_commit(&bars[B_BE + hh]);
-        }
-        if (!ok) break;
-        if (w < W0 && !(ok = pv(w + 1))) break;
-        if (w >= 1 && !(ok = gate(w - 1))) break;
+        // P(w) has been consumed (in issue order) -> its buffer takes gate(w-2)
+        if (w >= 2) ok = gate(w - 2);
       }
-      if (ok) pv(0);
-      mma_commit(&bars[B_DRAIN]);
-      mbar_wait(&bars[B_DRAIN], 0, err, kErrDrain);
+      mma_commit(&bars[B_DRAIN2]);
+      mbar_wait(&bars[B_DRAIN2], 0, err, kErrDrain);
     }
   } else if (warp >= 8) {
     // ------------------------------------------------- K^(m) operand builder
+    // Work items are the (K-step s, row, 16-byte chunk) triples the G GEMM
+    // reads: rows [0, nrow[s]) x 2 chunks of K-step s, numbered s-major and
+    // dealt round-robin over the 128 builder threads.  Each thread's item
+    // offsets are fixed for the whole kernel and computed once: the K chunk
+    // (without the window/half row offset), the coefficient quad, the
+    // destination chunk, and the (-i)^m swap/sign flags.
+    constexpr int kMaxItems = L::MAX_ITEMS;
     const int gt = tid - 256;
+    uint2* items = reinterpret_cast<uint2*>(smem + L::ITEMS);
+    int my_n = 0;
+    {
+      int item_end[8];
+      int acc = 0;
+#pragma unroll
+      for (int s2 = 0; s2 < 8; ++s2) {
+        acc += (s2 < KSTEPS) ? 2 * P.nrow[s2] : 0;
+        item_end[s2] = acc;
+      }
+#pragma unroll 1
+      for (int i = 0; i < kMaxItems; ++i) {
+        const int it = gt + 128 * i;
+        uint2 d = make_uint2(0u, 0u);
+        if (it < acc) {
+          int s2 = 0, base = 0;
+#pragma unroll
+          for (int q = 0; q < 7; ++q)
+            if (it >= item_end[q]) { s2 = q + 1; base = item_end[q]; }
+          const int local = it - base;
+          const int r = local >> 1, c = 2 * s2 + (local & 1), m = r >> 3, j = r & 7;
+          const uint32_t kofs = (c >> 3) * 8192 + j * 128 + (((c & 7) ^ j) << 4);
+          const uint32_t cofs = (m * NP + 4 * c) * 4;
+          const uint32_t bofs = P.b_slab_off[c >> 3] + sw128_offset(r, c & 7);
+          const uint32_t flags = (m & 1) | ((m & 2) ? 2u : 0u) | (((m + 1) & 2) ? 4u : 0u);
+          d = make_uint2(kofs | (cofs << 16), bofs | (flags << 16));
+          my_n = i + 1;
+        }
+        items[i * 128 + gt] = d;
+      }
+    }
     for (int w = W0; w >= 0; --w) {
-      const int k = W0 - w;
+      const int k = W0 - w, buf = k % nb, use = k / nb;
       const int n = T0 - w / 4, st = n & 1;
       if (!mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) break;
       bool ok = true;
+#pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
-        if (k > 0 && !(ok = mbar_wait(&bars[B_BE + hh], (k - 1) & 1, err, kErrBEmpty))) break;
-        const uint8_t* kt = smem + L::K + st * NS * 8192;
-        uint8_t* bt = smem + L::Bop + hh * NS * 16384;
-        for (int it = gt; it < 128 * (D / 8); it += 128) {
-          const int r = it & 127, c = it >> 7;  // row (m, jj), 16-byte chunk
-          if (r >= P.nrow[c >> 1]) continue;
-          const int m = r >> 3, kr = (w & 3) * kW + hh * 8 + (r & 7);
-          const uint4 kv = *reinterpret_cast<const uint4*>(
-              kt + (c >> 3) * 8192 + sw128_offset(kr, c & 7));
-          const float4 cf = *reinterpret_cast<const float4*>(s_coef + m * NP + 4 * c);
-          const uint32_t in[4] = {kv.x, kv.y, kv.z, kv.w};
-          const float cfa[4] = {cf.x, cf.y, cf.z, cf.w};
-          uint32_t out[4];
+        if (use > 0 &&
+            !(ok = mbar_wait(&bars[B_BE + 2 * hh + buf], (use - 1) & 1, err, kErrBEmpty)))
+          break;
+        const uint32_t kt = sK + st * NS * 8192 + (2 * (w & 3) + hh) * 1024;
+        const uint32_t bt = sB + (hh * nb + buf) * P.b_buf_bytes;
+#pragma unroll 1
+        for (int i0 = 0; i0 < my_n; i0 += 4) {
+          uint2 d[4];
+          uint4 kv[4];
+          float4 cf[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float ke = E::lo(in[i]) * cfa[i], ko = E::hi(in[i]) * cfa[i];
-            float re, im;
-            switch (m & 3) {
-              case 0: re = ke; im = ko; break;
-              case 1: re = ko; im = -ke; break;
-              case 2: re = -ke; im = -ko; break;
-              default: re = -ko; im = ke; break;
-            }
-            out[i] = E::pack(re, im);
+          for (int j = 0; j < 4; ++j) d[j] = items[(i0 + j < kMaxItems ? i0 + j : 0) * 128 + gt];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            kv[j] = lds128(kt + (d[j].x & 0xffffu));
+            cf[j] = lds128f(s_coef_u + (d[j].x >> 16));
           }
-          *reinterpret_cast<uint4*>(bt + (c >> 3) * 16384 + sw128_offset(r, c & 7)) =
-              make_uint4(out[0], out[1], out[2], out[3]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (i0 + j < my_n) {
+              const uint32_t fl = d[j].y >> 16;
+              const bool swp = fl & 1u;
+              const float sre = (fl & 2u) ? -1.f : 1.f, sim = (fl & 4u) ? -1.f : 1.f;
+              const uint32_t in[4] = {kv[j].x, kv[j].y, kv[j].z, kv[j].w};
+              const float cfa[4] = {cf[j].x, cf[j].y, cf[j].z, cf[j].w};
+              uint32_t out[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float ke = E::lo(in[e]), ko = E::hi(in[e]);
+                const float a = swp ? ko : ke, bq = swp ? ke : ko;
+                out[e] = E::pack(sre * cfa[e] * a, sim * cfa[e] * bq);
+              }
+              sts128(bt + (d[j].y & 0xffffu), make_uint4(out[0], out[1], out[2], out[3]));
+            }
+          }
         }
         fence_async_smem();
-        mbar_arrive(&bars[B_BF + hh]);
+        mbar_arrive(&bars[B_BF + 2 * hh + buf]);
       }
       if (!ok) break;
       if ((w & 3) == 0) mbar_arrive(&bars[B_KVE + st]);
@@ -322,52 +395,64 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
     bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
 
     // A operand of one window: v = R((carry + c0) theta) q_t in tensor memory
-    auto build_a = [&](float cw) {
+    // (angles reduced to [-pi, pi] on the FMA pipe, sine/cosine on MUFU).
+    auto build_a = [&](float cw, uint32_t av_col) {
       const float base = cw + kC0;
-#pragma unroll
+#pragma unroll 1
       for (int g = 0; g < NP / 16; ++g) {
-        uint32_t regs[16];
+        // 16 independent pairs, advanced stage by stage (instruction-level
+        // parallelism across pairs instead of one long chain per pair)
+        uint4 qv[4];
+        float th[16];
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           const int c = g * 4 + cc;  // 16-byte chunk of the row (4 pairs)
-          const uint4 qv = *reinterpret_cast<const uint4*>(
-              qrow + (c >> 3) * 16384 + sw128_offset(r, c & 7));
-          const uint32_t in[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int p = 4 * c + i;
-            float sn, cs;
-            sincos_reduced(base * s_th[p], &sn, &cs);
-            const float qe = E::lo(in[i]), qo = E::hi(in[i]);
-            regs[cc * 4 + i] = E::pack(qe * cs - qo * sn, qe * sn + qo * cs);
-          }
+          qv[cc] = lds128(sQ + (c >> 3) * 16384 + sw128_offset(r, c & 7));
+          const float4 t4 = lds128f(s_th_u + 16 * c);
+          th[4 * cc] = t4.x; th[4 * cc + 1] = t4.y; th[4 * cc + 2] = t4.z; th[4 * cc + 3] = t4.w;
         }
-        tmem_st16(lane_base + L::T_AV + 16 * g, regs);
+        float rr[16], sn[16], cs[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) rr[i] = reduce_2pi(base * th[i]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) __sincosf(rr[i], &sn[i], &cs[i]);
+        uint32_t regs[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t w32 = (i & 3) == 0 ? qv[i >> 2].x : (i & 3) == 1 ? qv[i >> 2].y
+                             : (i & 3) == 2 ? qv[i >> 2].z : qv[i >> 2].w;
+          const float qe = E::lo(w32), qo = E::hi(w32);
+          regs[i] = E::pack(qe * cs[i] - qo * sn[i], qe * sn[i] + qo * cs[i]);
+        }
+        tmem_st16(lane_base + av_col + 16 * g, regs);
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars[B_AV]);
     };
 
-    // Clenshaw combine of 8 keys from one G half: f_j = sum_m T_m(u_j) G_m
-    auto combine = [&](uint32_t gcol, const float (&u2)[8], const float (&uu)[8],
-                       float (&f)[8], int ge_bar) {
+    // Clenshaw combine of 8 keys from one G half: f_j = sum_m T_m(u_j) G_m.
+    // Columns m*8 + j; one 16-column load brings terms 2c and 2c+1.
+    auto combine = [&](uint32_t gcol, const float* uj, float* f, int ge_bar) {
+      constexpr int NC = kM / 2;  // 16-column loads
       float b1[8], b2[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) { b1[j] = 0.f; b2[j] = 0.f; }
 #pragma unroll
-      for (int batch = 0; batch < 2; ++batch) {
-        uint32_t g[4][16];
+      for (int c0 = NC - 1; c0 >= 0; c0 -= 2) {
+        uint32_t g[2][16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) tmem_ld16(lane_base + gcol + 16 * (7 - batch * 4 - i), g[i]);
+        for (int i = 0; i < 2; ++i)
+          if (c0 - i >= 0) tmem_ld16(lane_base + gcol + 16 * (c0 - i), g[i]);
         tmem_wait_ld();
-        if (batch == 1) {
+        if (c0 <= 1) {
           tc_fence_before();
           mbar_arrive(&bars[ge_bar]);
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int c = 7 - batch * 4 - i;
+        for (int i = 0; i < 2; ++i) {
+          const int c = c0 - i;
+          if (c < 0) continue;
 #pragma unroll
           for (int mm = 1; mm >= 0; --mm) {
             const int m = 2 * c + mm;
@@ -375,11 +460,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
             for (int j = 0; j < 8; ++j) {
               const float a = __uint_as_float(g[i][mm * 8 + j]);
               if (m > 0) {
-                const float bn = fmaf(u2[j], b1[j], a - b2[j]);
+                const float bn = fmaf(2.0f * uj[j], b1[j], a - b2[j]);
                 b2[j] = b1[j];
                 b1[j] = bn;
               } else {
-                f[j] = fmaf(uu[j], b1[j], a - b2[j]);
+                f[j] = fmaf(uj[j], b1[j], a - b2[j]);
               }
             }
           }
@@ -389,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
 
     if (ok) {
       tc_fence_after();
-      build_a(0.f);
+      build_a(0.f, (W0 & 1) ? L::T_AV1 : L::T_AV0);
     }
     for (int w = W0; ok && w >= 0; --w) {
       const int k = W0 - w;
@@ -401,40 +486,36 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       uint32_t sraw[16];
       tmem_ld16(lane_base + sg, sraw);
       tmem_wait_ld();
-      float uu[16], u2[16];
+      float uu[16];
       float acc = 0.f;
 #pragma unroll
       for (int jj = 15; jj >= 0; --jj) {
         const float z = (j0 + jj <= t) ? sigmoid_f(__uint_as_float(sraw[jj])) : 0.f;
         uu[jj] = fmaf(acc, 1.0f / kC0, -1.0f);
-        u2[jj] = 2.0f * uu[jj];
         acc += z;
       }
       const float carry_next = carry + acc;
+      // A operand of the next window (its buffer was last read by G(w+1),
+      // which completed before this row group loaded G(w+1))
+      if (w > 0) build_a(carry_next, ((w - 1) & 1) ? L::T_AV1 : L::T_AV0);
       float lg[16];
-      // first half of the window
-      if (!(ok = mbar_wait(&bars[B_GF + 0], k & 1, err, kErrG))) break;
-      tc_fence_after();
-      {
-        float f[8], a8[8], b8[8];
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        if (!(ok = mbar_wait(&bars[B_GF + hh], k & 1, err, kErrG))) break;
+        tc_fence_after();
+        float uj[8], f[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) { a8[j] = u2[j]; b8[j] = uu[j]; }
-        combine(L::T_G0, a8, b8, f, B_GE + 0);
+        for (int j = 0; j < 8; ++j) uj[j] = hh ? uu[8 + j] : uu[j];
+        combine(hh ? L::T_G1 : L::T_G0, uj, f, B_GE + hh);
+        if (hh == 0) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) lg[j] = f[j];
+          for (int j = 0; j < 8; ++j) lg[j] = f[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) lg[8 + j] = f[j];
+        }
       }
-      // second half; once its GEMM is done the A operand is free again
-      if (!(ok = mbar_wait(&bars[B_GF + 1], k & 1, err, kErrG))) break;
-      tc_fence_after();
-      if (w > 0) build_a(carry_next);
-      {
-        float f[8], a8[8], b8[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) { a8[j] = u2[8 + j]; b8[j] = uu[8 + j]; }
-        combine(L::T_G1, a8, b8, f, B_GE + 1);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) lg[8 + j] = f[j];
-      }
+      if (!ok) break;
       // online softmax (log2 units) with stale-max rescaling
       float mx = -INFINITY;
 #pragma unroll
@@ -593,21 +674,37 @@ static void fill_coefficients(Params& p, int D, float theta, float sm_scale) {
   }
 }
 
-template <typename T, int D>
-static cudaError_t launch_t(const Params& p, const FwdArgs& a, cudaStream_t st) {
+// Lay out the K^(m) buffers (rows actually read per slab) and choose double
+// buffering when it fits in shared memory.  Returns the dynamic smem bytes.
+template <int D>
+static int plan_buffers(Params& p) {
   using L = Layout<D>;
+  int off = 0;
+  for (int s = 0; s < L::NS; ++s) {
+    p.b_slab_off[s] = off;
+    off += p.nrow[4 * s] * 128;
+  }
+  p.b_buf_bytes = (off + 1023) & ~1023;
+  p.nb = (L::BOP + 4 * p.b_buf_bytes + 1024 <= kSmemLimit) ? 2 : 1;
+  return L::BOP + 2 * p.nb * p.b_buf_bytes + 1024;
+}
+
+template <typename T, int D>
+static cudaError_t launch_t(Params& p, const FwdArgs& a, cudaStream_t st) {
+  const int smem = plan_buffers<D>(p);
+  if (smem > kSmemLimit) return cudaErrorInvalidValue;
   dim3 grid((a.S + kBM - 1) / kBM, a.H, a.B);
   cudaError_t e;
   if (a.bias) {
     auto kern = fwd_kernel<T, D, true>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kThreads, L::ALLOC, st>>>(p);
+    kern<<<grid, kThreads, smem, st>>>(p);
   } else {
     auto kern = fwd_kernel<T, D, false>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return e;
-    kern<<<grid, kThreads, L::ALLOC, st>>>(p);
+    kern<<<grid, kThreads, smem, st>>>(p);
   }
   return cudaGetLastError();
 }
