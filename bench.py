@@ -136,18 +136,29 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(x, world):
+def max_over_ranks(x, world, device="cuda"):
+    """Max of a per-rank float over all ranks (the job time is the slowest rank)."""
     if world == 1:
         return x
     import torch.distributed as dist
-    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    t = torch.tensor([x], device=device, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return t.item()
 
 
+def rank_batches(rank, per_rank=WORKLOAD["B"]):
+    """Global batch indices owned by `rank` (batch x head sharding: each rank
+    owns whole batch entries, all heads, so no data crosses ranks)."""
+    return list(range(rank * per_rank, (rank + 1) * per_rank))
+
+
+def rank_seed(rank):
+    return 1 + 1000 * rank
+
+
 def make_inputs(rank, dev, dtype=torch.bfloat16):
     B, H, S, D = (WORKLOAD[k] for k in "BHSD")
-    g = torch.Generator(device=dev).manual_seed(1 + 1000 * rank)
+    g = torch.Generator(device=dev).manual_seed(rank_seed(rank))
     return [torch.randn(B, H, S, D, device=dev, generator=g, dtype=torch.float32).to(dtype)
             for _ in range(4)]
 
