@@ -88,6 +88,10 @@ def load_library():
             lib.corope_bwd_workspace_bytes.restype = ctypes.c_size_t
             lib.corope_last_error.argtypes = []
             lib.corope_last_error.restype = ctypes.c_char_p
+            lib.corope_bwd_noalloc.argtypes = [ctypes.POINTER(BwdParams), ctypes.c_void_p]
+            lib.corope_bwd_noalloc.restype = ctypes.c_int
+            lib.corope_bwd_noalloc_scratch_bytes.argtypes = []
+            lib.corope_bwd_noalloc_scratch_bytes.restype = ctypes.c_size_t
             lib.corope_take_device_error.argtypes = []
             lib.corope_take_device_error.restype = ctypes.c_int
             lib.corope_params_size.argtypes = [ctypes.c_int]

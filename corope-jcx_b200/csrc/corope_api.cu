@@ -30,6 +30,15 @@ static int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+namespace corope {
+// Record `msg` as this thread's last error and return `code` (for the other
+// translation units of the library).
+int set_last_error(int code, const char* msg) {
+  snprintf(g_err, sizeof(g_err), "%s", msg);
+  return code;
+}
+}  // namespace corope
+
 static int cuda_fail(cudaError_t e, const char* what) {
   return fail(COROPE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }

@@ -118,6 +118,22 @@ size_t corope_bwd_workspace_bytes(const corope_bwd_params_t *p);
  * reference definition check.py:44-103. */
 int corope_bwd(const corope_bwd_params_t *p, corope_stream_t stream);
 
+/* Backward without a caller workspace.  No counterpart in the reference:
+ * it exists for callers that cannot allocate device memory (a host engine
+ * whose plugin interface passes only inputs and outputs, or a process under
+ * a fixed pre-reserved memory budget).  The scratch corope_bwd would take
+ * from `workspace` comes instead from a 64 MiB array built into the library
+ * (every GPU that loads the library holds it until exit); `workspace` and
+ * `workspace_bytes` are ignored.  Shapes whose scratch exceeds
+ * corope_bwd_noalloc_scratch_bytes() are rejected with COROPE_ERR_WORKSPACE.
+ * The first call on a device looks up the array's device address (make it
+ * before any stream capture).  All calls on a device share the array, so
+ * calls that overlap on the GPU race; serialise them.  Calls no allocator. */
+int corope_bwd_noalloc(const corope_bwd_params_t *p, corope_stream_t stream);
+
+/* Size in bytes of the built-in scratch of corope_bwd_noalloc. */
+size_t corope_bwd_noalloc_scratch_bytes(void);
+
 /* Message for the last non-zero status returned on this thread. */
 const char *corope_last_error(void);
 
