@@ -43,9 +43,10 @@ UNIT = "TFLOP/s"
 CPU_SAMPLE_ROWS = 48
 
 # DRAM traffic per launch of the dominant kernel from one ncu capture
-# (dram__bytes_read.sum + dram__bytes_write.sum), scaled to this workload;
-# see the profile summaries under profiles/.  None until captured.
-NCU_TRAFFIC_BYTES = {"exact": None, "tensor": None}
+# (dram__bytes_read.sum + dram__bytes_write.sum) of B=1,H=8,S=2048,D=128,
+# scaled by the query rows x heads of this workload (x32); see
+# profiles/exact_bwd_b1h8s2048d128.md.
+NCU_TRAFFIC_BYTES = {"exact": 33.78e6 * 32, "tensor": None}
 
 
 def causal_pairs(B, H, S):
@@ -296,8 +297,13 @@ def run_ours(args):
 
     burst, sustained, hbm, peak_src = measured_peaks()
     bwd_tflops = fl_bwd / (bwd_ms * 1e-3) / 1e12
-    used = algo if algo != "auto" else "exact"
-    launches_per_step = {"exact": 4, "tensor": 4}[used]
+    # kernel families actually used: the tensor-core forward covers bf16/f16
+    # with D in {64, 128}; the backward has no tensor-core kernel yet
+    fwd_used = "exact" if algo == "exact" else "tensor"
+    bwd_used = "exact"
+    used = f"fwd {fwd_used}, bwd {bwd_used}"
+    # our kernels per step: forward 1; backward 3 (delta/lse, main, convert)
+    launches_per_step = 1 + 3
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -317,10 +323,10 @@ def run_ours(args):
                        "flop_convention": "FA causal: fwd 4*D*P, bwd 10*D*P"},
             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
             "pct_of_peak": 100 * value / world / sustained,
-            "roofline": {"bound": "tensor", "kernel": f"corope_bwd ({used})",
+            "roofline": {"bound": "tensor", "kernel": f"corope_bwd ({bwd_used})",
                          "achieved": bwd_tflops, "peak": sustained, "unit": "TFLOP/s",
                          "frac": bwd_tflops / sustained, "peak_source": f"{peak_src} sustained",
-                         "traffic": NCU_TRAFFIC_BYTES.get(used)},
+                         "traffic": NCU_TRAFFIC_BYTES.get(bwd_used)},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e_ms},
             "gpu_launches": launches_per_step * args.steps,
