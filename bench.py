@@ -297,13 +297,15 @@ def run_ours(args):
 
     burst, sustained, hbm, peak_src = measured_peaks()
     bwd_tflops = fl_bwd / (bwd_ms * 1e-3) / 1e12
-    # kernel families actually used: the tensor-core forward covers bf16/f16
-    # with D in {64, 128}; the backward has no tensor-core kernel yet
+    # kernel families actually used: the tensor-core kernels cover bf16/f16
+    # (forward: D in {64, 128}; backward: D = 128)
     fwd_used = "exact" if algo == "exact" else "tensor"
-    bwd_used = "exact"
+    bwd_used = "exact" if algo == "exact" else "tensor"
     used = f"fwd {fwd_used}, bwd {bwd_used}"
-    # our kernels per step: forward 1; backward 3 (delta/lse, main, convert)
-    launches_per_step = 1 + 3
+    # our kernels per step: forward 1; backward: delta/lse, then either the
+    # exact main kernel or the dQ and dK tensor-core kernels, then the fp32
+    # dk/dv conversion
+    launches_per_step = 1 + (3 if bwd_used == "exact" else 4)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -16,6 +16,11 @@ bool exact_supports_head_dim(int D);
 bool tc_fwd_supported(const FwdArgs& a, int dtype);
 cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st);
 int tc_take_device_error();
+bool tc_bwd_supported(const BwdArgs& a, int dtype);
+cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st);
+int tcb_take_device_error();
+cudaError_t bwd_pre_launch(const BwdArgs& a, int dtype, cudaStream_t st);
+cudaError_t bwd_post_launch(const BwdArgs& a, int dtype, cudaStream_t st);
 }  // namespace corope
 
 using namespace corope;
@@ -178,8 +183,8 @@ int corope_bwd(const corope_bwd_params_t* p, corope_stream_t stream) {
   if (!p->m || !p->l || !p->a) return fail(COROPE_ERR_INVALID, "m, l and a are required");
   if (p->bias && p->bias_row_stride < p->seq_len)
     return fail(COROPE_ERR_INVALID, "bias_row_stride must be >= seq_len");
-  if (p->algo == COROPE_ALGO_TENSOR)
-    return fail(COROPE_ERR_UNSUPPORTED, "tensor-core backward is not available in this build");
+  if (p->algo != COROPE_ALGO_EXACT && p->algo != COROPE_ALGO_AUTO && p->algo != COROPE_ALGO_TENSOR)
+    return fail(COROPE_ERR_INVALID, "unknown algo %d", p->algo);
   const size_t need = bwd_ws(p);
   if (!p->workspace || p->workspace_bytes < need)
     return fail(COROPE_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need,
@@ -207,16 +212,30 @@ int corope_bwd(const corope_bwd_params_t* p, corope_stream_t stream) {
   a.dv32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4) + align256(kv * 4));
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool tc_ok = tc_bwd_supported(a, p->dtype);
+  if (p->algo == COROPE_ALGO_TENSOR && !tc_ok)
+    return fail(COROPE_ERR_UNSUPPORTED,
+                "tensor-core backward needs bf16/f16, head_dim 128 and 16-byte aligned rows");
   cudaError_t e = cudaMemsetAsync(a.dk32, 0, 2 * align256(kv * 4), st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
-  e = exact_bwd_launch(a, p->dtype, st);
+  if (p->algo != COROPE_ALGO_EXACT && tc_ok) {
+    e = bwd_pre_launch(a, p->dtype, st);
+    if (e == cudaSuccess) e = tc_bwd_launch(a, p->dtype, st);
+    if (e == cudaSuccess) e = bwd_post_launch(a, p->dtype, st);
+  } else {
+    e = exact_bwd_launch(a, p->dtype, st);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "backward launch");
   return COROPE_OK;
 }
 
 const char* corope_last_error(void) { return g_err; }
 
-int corope_take_device_error(void) { return tc_take_device_error(); }
+int corope_take_device_error(void) {
+  const int f = tc_take_device_error();
+  const int g = tcb_take_device_error();
+  return f != 0 ? f : g;
+}
 
 size_t corope_params_size(int which) {
   return which == 0 ? sizeof(corope_fwd_params_t) : which == 1 ? sizeof(corope_bwd_params_t) : 0;

@@ -475,6 +475,38 @@ static cudaError_t launch_bwd_t(const BwdArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+template <typename T>
+static cudaError_t pre_t(const BwdArgs& a, cudaStream_t st) {
+  const int64_t rows = (int64_t)a.B * a.H * a.S;
+  exact_bwd_pre_kernel<T><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+template <typename T>
+static cudaError_t post_t(const BwdArgs& a, cudaStream_t st) {
+  exact_bwd_post_kernel<T><<<148 * 8, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// delta = rowsum(dO * O) and lse = m + log(l) into the workspace
+cudaError_t bwd_pre_launch(const BwdArgs& a, int dtype, cudaStream_t st) {
+  switch (dtype) {
+    case COROPE_DTYPE_F32: return pre_t<float>(a, st);
+    case COROPE_DTYPE_F16: return pre_t<__half>(a, st);
+    case COROPE_DTYPE_BF16: return pre_t<__nv_bfloat16>(a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// fp32 dk/dv accumulators -> output dtype
+cudaError_t bwd_post_launch(const BwdArgs& a, int dtype, cudaStream_t st) {
+  switch (dtype) {
+    case COROPE_DTYPE_F32: return post_t<float>(a, st);
+    case COROPE_DTYPE_F16: return post_t<__half>(a, st);
+    case COROPE_DTYPE_BF16: return post_t<__nv_bfloat16>(a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 cudaError_t exact_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st) {
   switch (dtype) {
     case COROPE_DTYPE_F32: return launch_bwd_t<float>(a, st);
