@@ -26,10 +26,16 @@
 //               dV^T = dO^T P and dK_gate^T = Q^T dS; fp32 atomics into the
 //               dk/dv accumulators of the workspace (query tiles race on keys).
 //
-// Roles per CTA (128 query rows of one (b, h), 384 threads): warps 0-3 row
-// work; warp 4 TMA; warp 5 UMMA for the gate, dP and G GEMMs; warp 6 UMMA
-// for the mode's GEMMs; warps 8-11 build K^(m) (and, in the dK launch, run
-// the per-dimension combine).  Every wait is bounded as in the forward.
+// Roles per CTA (128 query rows of one (b, h), 512 threads): warps 0-7 are
+// two row warpgroups that share every row -- warpgroup g takes keys 4g..4g+3
+// of each 8-key half window and rotation pairs 32g..32g+31 of the A operand
+// and the dQ update, and the two meet once per half through shared memory
+// for the running gate-gradient prefix; warp 8 TMA; warp 9 UMMA for the
+// gate, dP and G GEMMs; warp 10 UMMA for the launch's own GEMMs; warps 12-15
+// build K^(m) (and, in the dK launch, run the per-dimension combine).
+// Registers are re-balanced with setmaxnreg: rows 176, builders 104, the
+// TMA/UMMA warpgroup 56 (2 x 176 + 104 + 56 = 4 x 128, the launch budget).
+// Every wait is bounded as in the forward.
 #include <cstring>
 
 #include "common.cuh"
@@ -68,12 +74,14 @@ constexpr int NP = 64;       // rotation pairs
 constexpr int KSTEPS = 8;    // 16-element K steps over the head dim
 constexpr int kBM = 128;     // query rows per CTA
 constexpr int kKT = 32;      // keys per K/V tile (2 windows)
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
+constexpr int kRowRegs = 176, kBldRegs = 104, kCtlRegs = 56;
+static_assert(2 * kRowRegs + kBldRegs + kCtlRegs == 4 * 128, "register split");
 constexpr int MODE_DQ = 0, MODE_DK = 1;
 
 enum : int {
   kErrQ = 201, kErrKvEmpty, kErrKvFull, kErrSd, kErrSdEmpty, kErrAv, kErrAvEmpty, kErrB,
-  kErrBEmpty, kErrG, kErrGEmpty, kErrY, kErrX, kErrXFree, kErrC, kErrCEmpty, kErrDrain
+  kErrBEmpty, kErrG, kErrGEmpty, kErrY, kErrX, kErrXFree, kErrC, kErrCEmpty, kErrDrain, kErrXch
 };
 
 struct Params {
@@ -100,32 +108,34 @@ constexpr int S_DO = S_Q + NS * 16384;
 constexpr int S_K = S_DO + NS * 16384;       // [2 stages][NS][32 rows][128 B]
 constexpr int S_V = S_K + 2 * NS * 4096;
 constexpr int S_AV = S_V + 2 * NS * 4096;    // A operand rows [NS][128][128 B]
-constexpr int S_Y = S_AV + NS * 16384;       // dK launch: Y | P | dS rows [NS][128][128 B]
-template <int MODE> struct SmemTail {
-  static constexpr int COEF = (MODE == MODE_DK) ? S_Y + NS * 16384 : S_Y;
+constexpr int S_Y = S_AV + NS * 16384;       // dK: Y | P | dS rows [NS][128][128 B];
+                                             // dQ: staged (cos, sin) [8 chunks][256 threads][16 B]
+struct SmemTail {
+  static constexpr int COEF = S_Y + NS * 16384;
   static constexpr int TH = COEF + kM * NP * 4;
   static constexpr int BAR = TH + NP * 4;
   static constexpr int NBAR = 40;
   static constexpr int SLOT = BAR + NBAR * 8;
+  static constexpr int XCH = (SLOT + 16 + 15) & ~15;  // gate-gradient sums [half][group][128]
   static constexpr int MAX_ITEMS = (2 * 8 * 8 * kM + 127) / 128;
-  static constexpr int ITEMS = (SLOT + 16 + 15) & ~15;
+  static constexpr int ITEMS = XCH + 2 * 2 * 128 * 4;
   static constexpr int BOP = (ITEMS + MAX_ITEMS * 128 * 8 + 1023) & ~1023;
 };
 
 // tensor memory columns
 namespace tq {  // dQ launch
-constexpr uint32_t X = 0, DQ = 128, G = 256, SG0 = 368, SG1 = 384, DP0 = 400, DP1 = 416,
+constexpr uint32_t X = 0, DQ = 128, G = 256, SG0 = 368, DP0 = 400,
                    YT = 432;  // Y (56 cols) | dS (8 cols)
 static_assert(YT + 64 <= 512, "tmem");
 }  // namespace tq
 namespace tk {  // dK launch
-constexpr uint32_t G = 0, SG0 = 112, SG1 = 128, DP0 = 144, DP1 = 160, C0 = 176, C1 = 320;
+constexpr uint32_t G = 0, SG0 = 112, DP0 = 128, AVT = 144, C0 = 208, C1 = 352;
 // C region: [0,112) C^T terms x keys, [112,128) dO^T (P | dS), [128,144) Q^T (P | dS)
 static_assert(C1 + 144 <= 512, "tmem");
 }  // namespace tk
 
 enum {
-  B_Q = 0, B_KVF = 1, B_KVE = 3, B_SDF = 5, B_SDE = 7, B_AVF = 9, B_AVE = 10,
+  B_Q = 0, B_KVF = 1, B_KVE = 3, B_SDF = 5, B_SDE = 7, B_AVF = 9,
   B_BF = 11,  // [half][buf]
   B_BE = 15,  // [half][buf]
   B_GF = 19,  // [half]
@@ -133,7 +143,8 @@ enum {
   B_YA = 22, B_YDONE = 23, B_YB = 24,
   B_XF = 25, B_XFREE = 26, B_YTFREE = 27,        // dQ launch
   B_CF = 28, B_CE = 30, B_YFREE = 32,            // dK launch: [half] x 2
-  B_DRAIN5 = 34, B_DRAIN6 = 35
+  B_DRAIN5 = 34, B_DRAIN6 = 35,
+  B_XCH = 36                                     // [half]
 };
 
 __device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&r)[4]) {
@@ -142,11 +153,22 @@ __device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&r)[4])
                : "memory");
 }
 
+__device__ __forceinline__ uint32_t pack_cs(float c, float s) {
+  const __half2 h = __floats2half2_rn(c, s);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ float2 unpack_cs(uint32_t v) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&v));
+}
+
 template <typename T, int MODE, bool HAS_BIAS>
 __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant__ Params P) {
   using E = ElemTraits<T>;
-  using L = SmemTail<MODE>;
+  using L = SmemTail;
   using namespace sm100;
+  // gate/dP accumulators: double-buffered in the dQ launch, single in the dK
+  // launch (its tensor memory holds the A operand and two C regions)
+  constexpr int NSD = MODE == MODE_DQ ? 2 : 1;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -172,23 +194,23 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       mbar_init(&bars[B_KVF + i], 1);
       mbar_init(&bars[B_KVE + i], 2 + 128);  // two UMMA issuers + the builders
       mbar_init(&bars[B_SDF + i], 1);
-      mbar_init(&bars[B_SDE + i], 128);
+      mbar_init(&bars[B_SDE + i], 256);
       mbar_init(&bars[B_GF + i], 1);
       mbar_init(&bars[B_CF + i], 1);
       mbar_init(&bars[B_CE + i], 128);
+      mbar_init(&bars[B_XCH + i], 256);
     }
     for (int i = 0; i < 4; ++i) {
       mbar_init(&bars[B_BF + i], 128);
       mbar_init(&bars[B_BE + i], MODE == MODE_DQ ? 2 : 1);  // G (+ X) done with K^(m)
     }
-    mbar_init(&bars[B_AVF], 128);
-    mbar_init(&bars[B_AVE], 1);
-    mbar_init(&bars[B_GE], 128);
-    mbar_init(&bars[B_YA], 128);
+    mbar_init(&bars[B_AVF], 256);
+    mbar_init(&bars[B_GE], 256);
+    mbar_init(&bars[B_YA], 256);
     mbar_init(&bars[B_YDONE], 1);
-    mbar_init(&bars[B_YB], 128);
+    mbar_init(&bars[B_YB], 256);
     mbar_init(&bars[B_XF], 1);
-    mbar_init(&bars[B_XFREE], 128);
+    mbar_init(&bars[B_XFREE], 256);
     mbar_init(&bars[B_YTFREE], 1);
     mbar_init(&bars[B_YFREE], 1);
     mbar_init(&bars[B_DRAIN5], 1);
@@ -219,176 +241,188 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
   const uint32_t sB = smem_u32(smem + L::BOP);
   const uint32_t s_th_u = smem_u32(s_th), s_coef_u = smem_u32(s_coef);
   const uint32_t T_SG0 = MODE == MODE_DQ ? tq::SG0 : tk::SG0;
-  const uint32_t T_SG1 = MODE == MODE_DQ ? tq::SG1 : tk::SG1;
   const uint32_t T_DP0 = MODE == MODE_DQ ? tq::DP0 : tk::DP0;
-  const uint32_t T_DP1 = MODE == MODE_DQ ? tq::DP1 : tk::DP1;
   const uint32_t T_G = MODE == MODE_DQ ? tq::G : tk::G;
 
-  if (warp == 4) {
-    // ------------------------------------------------------------ TMA
-    if (lane == 0) {
-      prefetch_tmap(&P.tm_q);
-      prefetch_tmap(&P.tm_k);
-      prefetch_tmap(&P.tm_v);
-      prefetch_tmap(&P.tm_do);
-      mbar_expect_tx(&bars[B_Q], 2 * NS * 16384);
-      for (int s = 0; s < NS; ++s) {
-        tma_load_4d(smem + S_Q + s * 16384, &P.tm_q, &bars[B_Q], 64 * s, q0, h, b);
-        tma_load_4d(smem + S_DO + s * 16384, &P.tm_do, &bars[B_Q], 64 * s, q0, h, b);
-      }
-      const int TL = WL / 2;  // last K/V tile
-      int last_use[2] = {-1, -1};
-      for (int n = 0; n <= TL; ++n) {
-        const int st = n & 1, u = n >> 1;
-        if (n >= 2 && !mbar_wait(&bars[B_KVE + st], (u - 1) & 1, err, kErrKvEmpty)) break;
-        mbar_expect_tx(&bars[B_KVF + st], 2 * NS * 4096);
+  // Register split.  The barrier after it matters: a warp that finished its
+  // role early (warp 11 at once) re-raises its count to 128 at the end, and
+  // must not draw on the pool before the row warps have taken their share.
+  if (warp >= 8 && warp < 12) {
+    regs_dec<kCtlRegs>();
+    named_bar(1, kThreads);
+    if (warp == 8) {
+      // ---------------------------------------------------------- TMA
+      if (lane == 0) {
+        prefetch_tmap(&P.tm_q);
+        prefetch_tmap(&P.tm_k);
+        prefetch_tmap(&P.tm_v);
+        prefetch_tmap(&P.tm_do);
+        mbar_expect_tx(&bars[B_Q], 2 * NS * 16384);
         for (int s = 0; s < NS; ++s) {
-          tma_load_4d(smem + S_K + (st * NS + s) * 4096, &P.tm_k, &bars[B_KVF + st], 64 * s,
-                      kKT * n, hk, b);
-          tma_load_4d(smem + S_V + (st * NS + s) * 4096, &P.tm_v, &bars[B_KVF + st], 64 * s,
-                      kKT * n, hk, b);
+          tma_load_4d(smem + S_Q + s * 16384, &P.tm_q, &bars[B_Q], 64 * s, q0, h, b);
+          tma_load_4d(smem + S_DO + s * 16384, &P.tm_do, &bars[B_Q], 64 * s, q0, h, b);
         }
-        last_use[st] = u;
+        const int TL = WL / 2;  // last K/V tile
+        int last_use[2] = {-1, -1};
+        for (int n = 0; n <= TL; ++n) {
+          const int st = n & 1, u = n >> 1;
+          if (n >= 2 && !mbar_wait(&bars[B_KVE + st], (u - 1) & 1, err, kErrKvEmpty)) break;
+          mbar_expect_tx(&bars[B_KVF + st], 2 * NS * 4096);
+          for (int s = 0; s < NS; ++s) {
+            tma_load_4d(smem + S_K + (st * NS + s) * 4096, &P.tm_k, &bars[B_KVF + st], 64 * s,
+                        kKT * n, hk, b);
+            tma_load_4d(smem + S_V + (st * NS + s) * 4096, &P.tm_v, &bars[B_KVF + st], 64 * s,
+                        kKT * n, hk, b);
+          }
+          last_use[st] = u;
+        }
+        for (int st = 0; st < 2; ++st)
+          if (last_use[st] >= 0) mbar_wait(&bars[B_KVF + st], last_use[st] & 1, err, kErrDrain);
       }
-      for (int st = 0; st < 2; ++st)
-        if (last_use[st] >= 0) mbar_wait(&bars[B_KVF + st], last_use[st] & 1, err, kErrDrain);
-    }
-  } else if (warp == 5) {
-    // ---------------------------------- UMMA: gate, dP and G GEMMs
-    if (lane == 0) {
-      const uint32_t id_n16 = idesc_f16(128, 16, E::kBf16, false);
-      bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
-      tc_fence_after();
-      // gate scores Q K^T and dP = dO V^T of window w into buffer w & 1
-      auto sd = [&](int w) -> bool {
-        const int n = w >> 1, st = n & 1;
-        if (!mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) return false;
-        if (w >= 2 && !mbar_wait(&bars[B_SDE + (w & 1)], ((w >> 1) - 1) & 1, err, kErrSdEmpty))
-          return false;
+    } else if (warp == 9) {
+      // -------------------------------- UMMA: gate, dP and G GEMMs
+      if (lane == 0) {
+        const uint32_t id_n16 = idesc_f16(128, 16, E::kBf16, false);
+        bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
         tc_fence_after();
-        const uint32_t kt = sK + st * NS * 4096 + (w & 1) * kW * 128;
-        const uint32_t vt = sV + st * NS * 4096 + (w & 1) * kW * 128;
-        const uint32_t dsg = tmem + ((w & 1) ? T_SG1 : T_SG0);
-        const uint32_t ddp = tmem + ((w & 1) ? T_DP1 : T_DP0);
-#pragma unroll
-        for (int s = 0; s < KSTEPS; ++s) {
-          const uint32_t off = (s >> 2) * 16384 + 32 * (s & 3);
-          const uint32_t koff = (s >> 2) * 4096 + 32 * (s & 3);
-          mma_ss(dsg, sdesc_kmajor(sQ + off), sdesc_kmajor(kt + koff), id_n16, s > 0);
-          mma_ss(ddp, sdesc_kmajor(sDO + off), sdesc_kmajor(vt + koff), id_n16, s > 0);
-        }
-        mma_commit(&bars[B_SDF + (w & 1)]);
-        if (w & 1) mma_commit(&bars[B_KVE + st]);  // last window of the tile
-        return true;
-      };
-      if (ok) ok = sd(0);
-      if (ok && WL >= 1) ok = sd(1);
-      for (int w = 0; ok && w <= WL; ++w) {
-        const int buf = w % nb, use = w / nb;
-        if (!(ok = mbar_wait(&bars[B_AVF], w & 1, err, kErrAv))) break;
-        for (int hh = 0; hh < 2 && ok; ++hh) {
-          ok = mbar_wait(&bars[B_BF + 2 * hh + buf], use & 1, err, kErrB);
-          // the single G region: the rows have consumed the previous half
-          const int prev = 2 * w + hh - 1;
-          if (ok && prev >= 0) ok = mbar_wait(&bars[B_GE], prev & 1, err, kErrGEmpty);
-          if (!ok) break;
+        // gate scores Q K^T and dP = dO V^T of window w into buffer w % NSD
+        auto sd = [&](int w) -> bool {
+          const int n = w >> 1, st = n & 1, sb = w % NSD;
+          if (!mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) return false;
+          if (w >= NSD && !mbar_wait(&bars[B_SDE + sb], ((w / NSD) - 1) & 1, err, kErrSdEmpty))
+            return false;
           tc_fence_after();
-          const uint32_t bb = sB + (hh * nb + buf) * P.b_buf_bytes;
+          const uint32_t kt = sK + st * NS * 4096 + (w & 1) * kW * 128;
+          const uint32_t vt = sV + st * NS * 4096 + (w & 1) * kW * 128;
+          const uint32_t dsg = tmem + T_SG0 + 16 * sb;
+          const uint32_t ddp = tmem + T_DP0 + 16 * sb;
 #pragma unroll
           for (int s = 0; s < KSTEPS; ++s) {
-            const int nr = P.nrow[s];
-            if (nr == 0) break;
-            mma_ss(tmem + T_G, sdesc_kmajor(sAV + (s >> 2) * 16384 + 32 * (s & 3)),
-                   sdesc_kmajor(bb + P.b_slab_off[s >> 2] + 32 * (s & 3)),
-                   idesc_f16(128, nr, E::kBf16, false), s > 0);
+            const uint32_t off = (s >> 2) * 16384 + 32 * (s & 3);
+            const uint32_t koff = (s >> 2) * 4096 + 32 * (s & 3);
+            mma_ss(dsg, sdesc_kmajor(sQ + off), sdesc_kmajor(kt + koff), id_n16, s > 0);
+            mma_ss(ddp, sdesc_kmajor(sDO + off), sdesc_kmajor(vt + koff), id_n16, s > 0);
           }
-          mma_commit(&bars[B_GF + hh]);
-          mma_commit(&bars[B_BE + 2 * hh + buf]);
-        }
-        if (!ok) break;
-        if (w + 2 <= WL) ok = sd(w + 2);
-      }
-      mma_commit(&bars[B_DRAIN5]);
-      mbar_wait(&bars[B_DRAIN5], 0, err, kErrDrain);
-    }
-  } else if (warp == 6) {
-    // ---------------------------------- UMMA: the launch's own GEMMs
-    if (lane == 0) {
-      bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
-      tc_fence_after();
-      if (MODE == MODE_DQ) {
-        const uint32_t id_x = idesc_f16(128, 64, E::kBf16, true);   // B = K^(m), MN-major
-        const uint32_t id_g = idesc_f16(128, D, E::kBf16, true);    // B = K tile, MN-major
+          mma_commit(&bars[B_SDF + sb]);
+          if (w & 1) mma_commit(&bars[B_KVE + st]);  // last window of the tile
+          return true;
+        };
+        for (int w = 0; ok && w < NSD && w <= WL; ++w) ok = sd(w);
         for (int w = 0; ok && w <= WL; ++w) {
-          const int buf = w % nb;
-          const int n = w >> 1, st = n & 1;
+          const int buf = w % nb, use = w / nb;
+          if (!(ok = mbar_wait(&bars[B_AVF], w & 1, err, kErrAv))) break;
           for (int hh = 0; hh < 2 && ok; ++hh) {
-            ok = mbar_wait(&bars[hh ? B_YB : B_YA], w & 1, err, kErrY);
-            // X is free once the rows have folded the previous window into dq
-            if (ok && hh == 0 && w > 0) ok = mbar_wait(&bars[B_XFREE], (w - 1) & 1, err, kErrXFree);
+            ok = mbar_wait(&bars[B_BF + 2 * hh + buf], use & 1, err, kErrB);
+            // the single G region: the rows have consumed the previous half
+            const int prev = 2 * w + hh - 1;
+            if (ok && prev >= 0) ok = mbar_wait(&bars[B_GE], prev & 1, err, kErrGEmpty);
             if (!ok) break;
             tc_fence_after();
             const uint32_t bb = sB + (hh * nb + buf) * P.b_buf_bytes;
-            // X[:, 0:64) += Y_hh K^(m)[slab 0];  X[:, 64:128) += Y_hh K^(m)[slab 1]
-#pragma unroll 1
-            for (int s = 0; s < kM / 2; ++s) {  // 16 (term, key) rows per step
-              mma_ts(tmem + tq::X, tmem + tq::YT + 8 * s,
-                     sdesc_mnmajor(bb + P.b_slab_off[0] + 2048 * s, 16384), id_x,
-                     hh > 0 || s > 0);
-              if (16 * (s + 1) <= P.nrow[4])
-                mma_ts(tmem + tq::X + 64, tmem + tq::YT + 8 * s,
-                       sdesc_mnmajor(bb + P.b_slab_off[1] + 2048 * s, 16384), id_x,
-                       hh > 0 || s > 0);
+#pragma unroll
+            for (int s = 0; s < KSTEPS; ++s) {
+              const int nr = P.nrow[s];
+              if (nr == 0) break;
+              const uint64_t bd = sdesc_kmajor(bb + P.b_slab_off[s >> 2] + 32 * (s & 3));
+              const uint32_t id = idesc_f16(128, nr, E::kBf16, false);
+              if (MODE == MODE_DQ)
+                mma_ss(tmem + T_G, sdesc_kmajor(sAV + (s >> 2) * 16384 + 32 * (s & 3)), bd, id,
+                       s > 0);
+              else
+                mma_ts(tmem + T_G, tmem + tk::AVT + 8 * s, bd, id, s > 0);
             }
+            mma_commit(&bars[B_GF + hh]);
             mma_commit(&bars[B_BE + 2 * hh + buf]);
-            if (hh == 0) mma_commit(&bars[B_YDONE]);  // Y half A consumed
           }
           if (!ok) break;
-          // gate part: dq += dS K_w  (A = dS from tensor memory, B = K tile)
-          if (!(ok = mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull))) break;
-          mma_ts(tmem + tq::DQ, tmem + tq::YT + 56,
-                 sdesc_mnmajor(sK + st * NS * 4096 + (w & 1) * kW * 128, 4096), id_g, w > 0);
-          mma_commit(&bars[B_XF]);
-          mma_commit(&bars[B_YTFREE]);
-          if (w & 1) mma_commit(&bars[B_KVE + st]);
+          if (w + NSD <= WL) ok = sd(w + NSD);
         }
-      } else {
-        const uint32_t id_c = idesc_f16(128, 112, E::kBf16, true) | (1u << 15);  // A, B MN-major
-        const uint32_t id_s = idesc_f16(128, 16, E::kBf16, true) | (1u << 15);
-        for (int w = 0; ok && w <= WL; ++w) {
-          for (int hh = 0; hh < 2 && ok; ++hh) {
-            ok = mbar_wait(&bars[hh ? B_YB : B_YA], w & 1, err, kErrY);
-            if (ok && w > 0) ok = mbar_wait(&bars[B_CE + hh], (w - 1) & 1, err, kErrCEmpty);
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t creg = tmem + (hh ? tk::C1 : tk::C0);
-#pragma unroll 1
-            for (int s = 0; s < 8; ++s) {  // K = 128 query rows, 16 per step
-              const uint32_t ko = 2048 * s;
-              // C^T = v^T Y: A = v^T (M = head dim), B = Y^T (N = term x key)
-              mma_ss(creg, sdesc_mnmajor(sAV + ko, 16384), sdesc_mnmajor(sY + ko, 16384), id_c,
-                     s > 0);
-              // dO^T (P | dS) and Q^T (P | dS): B = elements 112..127 of the rows
-              mma_ss(creg + 112, sdesc_mnmajor(sDO + ko, 16384),
-                     sdesc_mnmajor(sY + 16384 + ko + 96, 16384), id_s, s > 0);
-              mma_ss(creg + 128, sdesc_mnmajor(sQ + ko, 16384),
-                     sdesc_mnmajor(sY + 16384 + ko + 96, 16384), id_s, s > 0);
-            }
-            mma_commit(&bars[B_CF + hh]);
-            mma_commit(&bars[hh ? B_YFREE : B_YDONE]);
-            if (hh == 1) mma_commit(&bars[B_AVE]);
-          }
-          if (!ok) break;
-          if (w & 1) mma_commit(&bars[B_KVE + ((w >> 1) & 1)]);
-        }
+        mma_commit(&bars[B_DRAIN5]);
+        mbar_wait(&bars[B_DRAIN5], 0, err, kErrDrain);
       }
-      mma_commit(&bars[B_DRAIN6]);
-      mbar_wait(&bars[B_DRAIN6], 0, err, kErrDrain);
+    } else if (warp == 10) {
+      // -------------------------------- UMMA: the launch's own GEMMs
+      if (lane == 0) {
+        bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
+        tc_fence_after();
+        if (MODE == MODE_DQ) {
+          const uint32_t id_x = idesc_f16(128, 64, E::kBf16, true);   // B = K^(m), MN-major
+          const uint32_t id_g = idesc_f16(128, D, E::kBf16, true);    // B = K tile, MN-major
+          for (int w = 0; ok && w <= WL; ++w) {
+            const int buf = w % nb;
+            const int n = w >> 1, st = n & 1;
+            for (int hh = 0; hh < 2 && ok; ++hh) {
+              ok = mbar_wait(&bars[hh ? B_YB : B_YA], w & 1, err, kErrY);
+              // X is free once the rows have folded the previous window into dq
+              if (ok && hh == 0 && w > 0)
+                ok = mbar_wait(&bars[B_XFREE], (w - 1) & 1, err, kErrXFree);
+              if (!ok) break;
+              tc_fence_after();
+              const uint32_t bb = sB + (hh * nb + buf) * P.b_buf_bytes;
+              // X[:, 0:64) += Y_hh K^(m)[slab 0];  X[:, 64:128) += Y_hh K^(m)[slab 1]
+#pragma unroll 1
+              for (int s = 0; s < kM / 2; ++s) {  // 16 (term, key) rows per step
+                mma_ts(tmem + tq::X, tmem + tq::YT + 8 * s,
+                       sdesc_mnmajor(bb + P.b_slab_off[0] + 2048 * s, 16384), id_x,
+                       hh > 0 || s > 0);
+                if (16 * (s + 1) <= P.nrow[4])
+                  mma_ts(tmem + tq::X + 64, tmem + tq::YT + 8 * s,
+                         sdesc_mnmajor(bb + P.b_slab_off[1] + 2048 * s, 16384), id_x,
+                         hh > 0 || s > 0);
+              }
+              mma_commit(&bars[B_BE + 2 * hh + buf]);
+              if (hh == 0) mma_commit(&bars[B_YDONE]);  // Y half A consumed
+            }
+            if (!ok) break;
+            // gate part: dq += dS K_w  (A = dS from tensor memory, B = K tile)
+            if (!(ok = mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull))) break;
+            mma_ts(tmem + tq::DQ, tmem + tq::YT + 56,
+                   sdesc_mnmajor(sK + st * NS * 4096 + (w & 1) * kW * 128, 4096), id_g, w > 0);
+            mma_commit(&bars[B_XF]);
+            mma_commit(&bars[B_YTFREE]);
+            if (w & 1) mma_commit(&bars[B_KVE + st]);
+          }
+        } else {
+          const uint32_t id_c = idesc_f16(128, 112, E::kBf16, true) | (1u << 15);  // A, B MN-major
+          const uint32_t id_s = idesc_f16(128, 16, E::kBf16, true) | (1u << 15);
+          for (int w = 0; ok && w <= WL; ++w) {
+            for (int hh = 0; hh < 2 && ok; ++hh) {
+              ok = mbar_wait(&bars[hh ? B_YB : B_YA], w & 1, err, kErrY);
+              if (ok && w > 0) ok = mbar_wait(&bars[B_CE + hh], (w - 1) & 1, err, kErrCEmpty);
+              if (!ok) break;
+              tc_fence_after();
+              const uint32_t creg = tmem + (hh ? tk::C1 : tk::C0);
+#pragma unroll 1
+              for (int s = 0; s < 8; ++s) {  // K = 128 query rows, 16 per step
+                const uint32_t ko = 2048 * s;
+                // C^T = v^T Y: A = v^T (M = head dim), B = Y^T (N = term x key)
+                mma_ss(creg, sdesc_mnmajor(sAV + ko, 16384), sdesc_mnmajor(sY + ko, 16384), id_c,
+                       s > 0);
+                // dO^T (P | dS) and Q^T (P | dS): B = elements 112..127 of the rows
+                mma_ss(creg + 112, sdesc_mnmajor(sDO + ko, 16384),
+                       sdesc_mnmajor(sY + 16384 + ko + 96, 16384), id_s, s > 0);
+                mma_ss(creg + 128, sdesc_mnmajor(sQ + ko, 16384),
+                       sdesc_mnmajor(sY + 16384 + ko + 96, 16384), id_s, s > 0);
+              }
+              mma_commit(&bars[B_CF + hh]);
+              mma_commit(&bars[hh ? B_YFREE : B_YDONE]);
+            }
+            if (!ok) break;
+            if (w & 1) mma_commit(&bars[B_KVE + ((w >> 1) & 1)]);
+          }
+        }
+        mma_commit(&bars[B_DRAIN6]);
+        mbar_wait(&bars[B_DRAIN6], 0, err, kErrDrain);
+      }
     }
-  } else if (warp >= 8) {
-    // ------------------------- K^(m) builder (+ per-dimension combine, dK launch)
+    __syncwarp();
+    regs_inc<128>();
+  } else if (warp >= 12) {
+    // ----------------------- K^(m) builder (+ per-dimension combine, dK launch)
+    regs_dec<kBldRegs>();
+    named_bar(1, kThreads);
     constexpr int kMaxItems = L::MAX_ITEMS;
-    const int gt = tid - 256;
+    const int gt = tid - 384;
     uint2* items = reinterpret_cast<uint2*>(smem + L::ITEMS);
     int my_n = 0;
     {
@@ -438,17 +472,17 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         cm[m] = kLn2 * s_coef[m * NP + p] * sgn;
       }
     }
-    const uint32_t lane_base = tmem + ((uint32_t)((warp - 8) * 32) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
     float* dk32 = P.dk32 + ((int64_t)b * P.Hkv + hk) * S * D;
     float* dv32 = P.dv32 + ((int64_t)b * P.Hkv + hk) * S * D;
 
     auto build = [&](int w) -> bool {
       const int buf = w % nb, use = w / nb;
       const int n = w >> 1, st = n & 1;
-      if (!mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) return false;
+      if (!wwait(bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) return false;
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
-        if (use > 0 && !mbar_wait(&bars[B_BE + 2 * hh + buf], (use - 1) & 1, err, kErrBEmpty))
+        if (use > 0 && !wwait(bars[B_BE + 2 * hh + buf], (use - 1) & 1, err, kErrBEmpty))
           return false;
         const uint32_t kt = sK + st * NS * 4096 + (2 * (w & 1) + hh) * 1024;
         const uint32_t bt = sB + (hh * nb + buf) * P.b_buf_bytes;
@@ -493,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     auto combine = [&](int w) -> bool {
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
-        if (!mbar_wait(&bars[B_CF + hh], w & 1, err, kErrC)) return false;
+        if (!wwait(bars[B_CF + hh], w & 1, err, kErrC)) return false;
         tc_fence_after();
         const uint32_t creg = lane_base + (hh ? tk::C1 : tk::C0);
         float dk[8], dv[8];
@@ -542,70 +576,149 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       if (w + 1 <= WL) ok = build(w + 1);
       if (ok && MODE == MODE_DK) ok = combine(w);
     }
-  } else if (warp < 4) {
+    __syncwarp();
+    regs_inc<128>();
+  } else {
     // ------------------------------------------------------------ row warps
-    const int r = tid;
+    regs_inc<kRowRegs>();
+    named_bar(1, kThreads);
+    const int rg = warp >> 2;  // row warpgroup
+    const int r = tid & 127;
     const int t = q0 + r;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const bool row_ok = t < S;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const int64_t ri = ((int64_t)b * P.H + h) * S + min(t, S - 1);
     const float A_t = P.a[ri];
     const float lse2 = P.lse[ri] * kLog2e;
     const float delta = P.delta[ri];
-    float base = 0.f;    // gate prefix before the window
-    float da_run = 0.f;  // prefix of da before the current key
-    bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
+    const uint32_t s_xch = smem_u32(smem + L::XCH);
+    const uint32_t s_cs = sY + (rg * 128 + r) * 16;  // dQ: staged (cos, sin), chunk q at + 4096 q
+    float base = 0.f;    // gate prefix through the current window
+    float carry = 0.f;   // gate sum of the keys after the current window
+    float da_run = 0.f;  // gate-gradient prefix before the current half
+    // this group's keys of the window: i -> key 8 (i >> 2) + 4 rg + (i & 3)
+    float zo[8], uo[8], dpo[8];
+    uint32_t csc[32];    // dQ: (cos, sin) halves of this group's 32 pairs
+    bool ok = wwait(bars[B_Q], 0, err, kErrQ);
 
-    // sin/cos of (carry + c0) theta for 16 pairs starting at pair 16 g
-    auto angles = [&](float cw, int g, float (&sn)[16], float (&cs)[16]) {
-      const float bse = cw + kC0;
+    // gates and positions of window w; reads the gate scores and dP
+    auto gates = [&](int w) -> bool {
+      const int sb = w % NSD;
+      if (!wwait(bars[B_SDF + sb], (w / NSD) & 1, err, kErrSd)) return false;
+      tc_fence_after();
+      uint32_t sraw[16], d4a[4], d4b[4];
+      tmem_ld16(lane_base + T_SG0 + 16 * sb, sraw);
+      tmem_ld4(lane_base + T_DP0 + 16 * sb + 4 * rg, d4a);
+      tmem_ld4(lane_base + T_DP0 + 16 * sb + 8 + 4 * rg, d4b);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bars[B_SDE + sb]);
+      const int j0 = w * kW;
+      float z[16], uu[16];
+      float zsum = 0.f;
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const float4 t4 = lds128f(s_th_u + 16 * (g * 4 + cc));
-        const float th[4] = {t4.x, t4.y, t4.z, t4.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float rr = reduce_2pi(bse * th[i]);
-          __sincosf(rr, &sn[4 * cc + i], &cs[4 * cc + i]);
-        }
+      for (int jj = 0; jj < 16; ++jj) {
+        z[jj] = (row_ok && j0 + jj <= t) ? sigmoid_f(__uint_as_float(sraw[jj])) : 0.f;
+        zsum += z[jj];
       }
+      float suf = 0.f;  // in-window suffix after key jj
+#pragma unroll
+      for (int jj = 15; jj >= 0; --jj) {
+        uu[jj] = fmaf(suf, 1.0f / kC0, -1.0f);
+        suf += z[jj];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int kk = 8 * (i >> 2) + (i & 3);
+        zo[i] = rg ? z[kk + 4] : z[kk];
+        uo[i] = rg ? uu[kk + 4] : uu[kk];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        dpo[i] = __uint_as_float(d4a[i]);
+        dpo[4 + i] = __uint_as_float(d4b[i]);
+      }
+      base += zsum;
+      carry = A_t - base;
+      return true;
     };
 
-    // A operand rows v = R((carry + c0) theta) q_t into shared memory
-    auto build_a = [&](float cw) {
+    // this group's half of the A operand v = R((carry + c0) theta) q_t:
+    // dQ launch -> shared memory (and the (cos, sin) staging); dK launch ->
+    // tensor memory (the G GEMM's A; copied to shared memory later for C)
+    auto build_a = [&]() {
+      const float bse = carry + kC0;
 #pragma unroll 1
-      for (int g = 0; g < NP / 16; ++g) {
-        float sn[16], cs[16];
-        angles(cw, g, sn, cs);
+      for (int g = 0; g < 2; ++g) {
+        uint4 qv[4];
+        float th[16];
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
-          const int c = g * 4 + cc;
-          const uint4 qv = lds128(sQ + (c >> 3) * 16384 + sw128_offset(r, c & 7));
-          const uint32_t in[4] = {qv.x, qv.y, qv.z, qv.w};
-          uint32_t o[4];
+          const int c = 4 * g + cc;  // chunk within the slab (4 pairs)
+          qv[cc] = lds128(sQ + rg * 16384 + sw128_offset(r, c));
+          const float4 t4 = lds128f(s_th_u + 16 * (8 * rg + c));
+          th[4 * cc] = t4.x; th[4 * cc + 1] = t4.y; th[4 * cc + 2] = t4.z; th[4 * cc + 3] = t4.w;
+        }
+        float rr[16], sn[16], cs[16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float qe = E::lo(in[i]), qo = E::hi(in[i]);
-            const float s_ = sn[4 * cc + i], c_ = cs[4 * cc + i];
-            o[i] = E::pack(qe * c_ - qo * s_, qe * s_ + qo * c_);
+        for (int i = 0; i < 16; ++i) rr[i] = reduce_2pi(bse * th[i]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) __sincosf(rr[i], &sn[i], &cs[i]);
+        uint32_t o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t w32 = (i & 3) == 0 ? qv[i >> 2].x : (i & 3) == 1 ? qv[i >> 2].y
+                             : (i & 3) == 2 ? qv[i >> 2].z : qv[i >> 2].w;
+          const float qe = E::lo(w32), qo = E::hi(w32);
+          o[i] = E::pack(qe * cs[i] - qo * sn[i], qe * sn[i] + qo * cs[i]);
+        }
+        if (MODE == MODE_DQ) {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int c = 4 * g + cc;
+            sts128(sAV + rg * 16384 + sw128_offset(r, c),
+                   make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]));
+            sts128(s_cs + c * 4096,
+                   make_uint4(pack_cs(cs[4 * cc], sn[4 * cc]), pack_cs(cs[4 * cc + 1], sn[4 * cc + 1]),
+                              pack_cs(cs[4 * cc + 2], sn[4 * cc + 2]),
+                              pack_cs(cs[4 * cc + 3], sn[4 * cc + 3])));
           }
-          sts128(sAV + (c >> 3) * 16384 + sw128_offset(r, c & 7), make_uint4(o[0], o[1], o[2], o[3]));
+        } else {
+          tmem_st16(lane_base + tk::AVT + 32 * rg + 16 * g, o);
         }
       }
-      fence_async_smem();
+      if (MODE == MODE_DQ) {
+        fence_async_smem();
+      } else {
+        tmem_wait_st();
+        tc_fence_before();
+      }
       mbar_arrive(&bars[B_AVF]);
     };
 
-    // Clenshaw: logits (log2 units) and their derivative in u for 8 keys
-    auto clenshaw = [&](const float* uj, float* f, float* fd) {
-      float b1[8], b2[8], d1[8], d2[8];
+    auto load_cs = [&]() {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) { b1[j] = b2[j] = d1[j] = d2[j] = 0.f; }
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = lds128(s_cs + c * 4096);
+        csc[4 * c] = v.x; csc[4 * c + 1] = v.y; csc[4 * c + 2] = v.z; csc[4 * c + 3] = v.w;
+      }
+    };
+
+    // Clenshaw for this group's 4 keys of a half: logits (log2 units) and
+    // their derivative in u.  G columns: 16 c + 8 (m & 1) + key, m = 2 c + (m & 1).
+    auto clenshaw = [&](const float (&uj)[4], float (&f)[4], float (&fd)[4]) {
+      float b1[4], b2[4], d1[4], d2[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { b1[j] = b2[j] = d1[j] = d2[j] = 0.f; }
 #pragma unroll
       for (int c0 = kM / 2 - 1; c0 >= 0; c0 -= 2) {
-        uint32_t g[2][16];
+        uint32_t g[2][2][4];
 #pragma unroll
         for (int i = 0; i < 2; ++i)
-          if (c0 - i >= 0) tmem_ld16(lane_base + T_G + 16 * (c0 - i), g[i]);
+          if (c0 - i >= 0) {
+            tmem_ld4(lane_base + T_G + 16 * (c0 - i) + 4 * rg, g[i][0]);
+            tmem_ld4(lane_base + T_G + 16 * (c0 - i) + 8 + 4 * rg, g[i][1]);
+          }
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
@@ -615,8 +728,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           for (int mm = 1; mm >= 0; --mm) {
             const int m = 2 * c + mm;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float a = __uint_as_float(g[i][mm * 8 + j]);
+            for (int j = 0; j < 4; ++j) {
+              const float a = __uint_as_float(g[i][mm][j]);
               const float u2 = 2.0f * uj[j];
               if (m > 0) {
                 const float dn = fmaf(u2, d1[j], fmaf(2.0f, b1[j], -d2[j]));
@@ -633,77 +746,61 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       }
     };
 
-    for (int w = 0; ok && w <= WL; ++w) {
+    // the two halves of window w
+    auto halves = [&](int w) -> bool {
       const int j0 = w * kW;
-      // ---- gates, positions
-      if (!(ok = mbar_wait(&bars[B_SDF + (w & 1)], (w >> 1) & 1, err, kErrSd))) break;
-      tc_fence_after();
-      float z[16], uu[16];
-      {
-        uint32_t sraw[16];
-        tmem_ld16(lane_base + ((w & 1) ? T_SG1 : T_SG0), sraw);
-        tmem_wait_ld();
-        float zsum = 0.f;
+      if (MODE == MODE_DK) {
+        // the previous window's C GEMMs are done with the A rows and the Y
+        // buffer: copy this window's A half from tensor to shared memory
+        if (w > 0 && !wwait(bars[B_YFREE], (w - 1) & 1, err, kErrY)) return false;
+        tc_fence_after();
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          z[jj] = (j0 + jj <= t) ? sigmoid_f(__uint_as_float(sraw[jj])) : 0.f;
-          zsum += z[jj];
+        for (int g = 0; g < 2; ++g) {
+          uint32_t o[16];
+          tmem_ld16(lane_base + tk::AVT + 32 * rg + 16 * g, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc)
+            sts128(sAV + rg * 16384 + sw128_offset(r, 4 * g + cc),
+                   make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]));
         }
-        float suf = 0.f;  // in-window suffix after key jj
-#pragma unroll
-        for (int jj = 15; jj >= 0; --jj) {
-          uu[jj] = fmaf(suf, 1.0f / kC0, -1.0f);
-          suf += z[jj];
-        }
-        base += zsum;
       }
-      const float carry = A_t - base;  // gate sum of the keys after the window
-      // ---- A operand (its buffer is free: the previous window's GEMMs that
-      // read it have completed)
-      if (MODE == MODE_DK && w > 0 && !(ok = mbar_wait(&bars[B_AVE], (w - 1) & 1, err, kErrAvEmpty)))
-        break;
-      build_a(carry);
-      // ---- the two halves of the window
-      float dpv[16];
-      {
-        uint32_t dr[16];
-        tmem_ld16(lane_base + ((w & 1) ? T_DP1 : T_DP0), dr);
-        tmem_wait_ld();
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) dpv[jj] = __uint_as_float(dr[jj]);
-      }
-      tc_fence_before();
-      mbar_arrive(&bars[B_SDE + (w & 1)]);
-      uint32_t dspk[8];  // dS (bf16 pairs) for the 16 keys
+      uint32_t dsa0 = 0u, dsa1 = 0u;  // dS of half A (packed), written with half B
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
-        if (!(ok = mbar_wait(&bars[B_GF + hh], w & 1, err, kErrG))) break;
+        if (!wwait(bars[B_GF + hh], w & 1, err, kErrG)) return false;
         tc_fence_after();
-        float uj[8], f[8], fd[8];
+        float uj[4], zj[4], dpj[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) uj[j] = hh ? uu[8 + j] : uu[j];
+        for (int i = 0; i < 4; ++i) {
+          uj[i] = hh ? uo[4 + i] : uo[i];
+          zj[i] = hh ? zo[4 + i] : zo[i];
+          dpj[i] = hh ? dpo[4 + i] : dpo[i];
+        }
+        float f[4], fd[4];
         clenshaw(uj, f, fd);
         tc_fence_before();
         mbar_arrive(&bars[B_GE]);
-        float dl[8], ds[8];
+        float dl[4], da[4], pr[4];
+        float sum4 = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int jj = hh * 8 + j;
-          const bool valid = j0 + jj <= t;
-          float lg = f[j];
-          if (HAS_BIAS && valid) lg = fmaf(P.bias[(int64_t)t * P.bias_rs + j0 + jj], kLog2e, lg);
-          const float pr = valid ? exp2f(lg - lse2) : 0.f;
-          dl[j] = pr * ((hh ? dpv[8 + j] : dpv[j]) - delta);
-          const float da = dl[j] * (kLn2 / kC0) * fd[j];
-          const float zj = hh ? z[8 + j] : z[j];
-          ds[j] = valid ? da_run * zj * (1.f - zj) : 0.f;
-          da_run += valid ? da : 0.f;
-          f[j] = pr;  // keep P for the dK launch
+        for (int i = 0; i < 4; ++i) {
+          const int kj = j0 + 8 * hh + 4 * rg + i;
+          const bool valid = row_ok && kj <= t;
+          float lg = f[i];
+          if (HAS_BIAS && valid) lg = fmaf(P.bias[(int64_t)t * P.bias_rs + kj], kLog2e, lg);
+          pr[i] = valid ? exp2f(lg - lse2) : 0.f;
+          dl[i] = pr[i] * (dpj[i] - delta);
+          da[i] = valid ? dl[i] * (kLn2 / kC0) * fd[i] : 0.f;
+          sum4 += da[i];
         }
-        // Y_m = dl T_m(u), packed per term for the 8 keys
-        uint32_t y[kM][4];
+        // publish this group's sum for the partner group
+        sts32f(s_xch + ((hh * 2 + rg) * 128 + r) * 4, sum4);
+        mbar_arrive(&bars[B_XCH + hh]);
+        // Y_m = dl T_m(u), packed per term for the group's 4 keys
+        uint32_t y[kM][2];
 #pragma unroll
-        for (int jp = 0; jp < 4; ++jp) {
+        for (int jp = 0; jp < 2; ++jp) {
           float ta0 = 1.f, tb0 = 1.f;
           float ta1 = uj[2 * jp], tb1 = uj[2 * jp + 1];
           y[0][jp] = E::pack(dl[2 * jp], dl[2 * jp + 1]);
@@ -716,106 +813,125 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             y[m][jp] = E::pack(dl[2 * jp] * ta2, dl[2 * jp + 1] * tb2);
           }
         }
-#pragma unroll
-        for (int jp = 0; jp < 4; ++jp) dspk[hh * 4 + jp] = E::pack(ds[2 * jp], ds[2 * jp + 1]);
         if (MODE == MODE_DQ) {
-          // Y half into tensor memory (A operand of X); half B waits until X
-          // has consumed half A, half A until the previous window's GEMMs are done
-          if (hh == 0 && w > 0 && !(ok = mbar_wait(&bars[B_YTFREE], (w - 1) & 1, err, kErrX))) break;
-          if (hh == 1 && !(ok = mbar_wait(&bars[B_YDONE], w & 1, err, kErrX))) break;
+          // Y half into tensor memory (A operand of X): half A waits until the
+          // previous window's GEMMs are done with it, half B until X has
+          // consumed half A
+          if (hh == 0 && w > 0 && !wwait(bars[B_YTFREE], (w - 1) & 1, err, kErrX)) return false;
+          if (hh == 1 && !wwait(bars[B_YDONE], w & 1, err, kErrX)) return false;
           tc_fence_after();
 #pragma unroll
-          for (int q = 0; q < 3; ++q) {
-            uint32_t v16[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v16[i] = y[(16 * q + i) >> 2][i & 3];
-            tmem_st16(lane_base + tq::YT + 16 * q, v16);
+          for (int m = 0; m < kM; ++m) tmem_st2(lane_base + tq::YT + 4 * m + 2 * rg, y[m][0], y[m][1]);
+          if (hh == 0) {
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&bars[B_YA]);
           }
-          {
-            uint32_t v8[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v8[i] = y[(48 + i) >> 2][i & 3];
-            tmem_st8(lane_base + tq::YT + 48, v8);
-          }
-          if (hh == 1) {
-            uint32_t v8[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v8[i] = dspk[i];
-            tmem_st8(lane_base + tq::YT + 56, v8);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(&bars[hh ? B_YB : B_YA]);
         } else {
-          // Y | P | dS rows into shared memory (B operand of the C GEMMs)
-          if (hh == 0 && w > 0 && !(ok = mbar_wait(&bars[B_YFREE], (w - 1) & 1, err, kErrY))) break;
-          if (hh == 1 && !(ok = mbar_wait(&bars[B_YDONE], w & 1, err, kErrY))) break;
+          // Y | P rows into shared memory (B operand of the C GEMMs)
+          if (hh == 1 && !wwait(bars[B_YDONE], w & 1, err, kErrY)) return false;
 #pragma unroll
-          for (int m = 0; m < kM; ++m)  // element m*8 + jj: chunk m of the row
-            sts128(sY + (m >> 3) * 16384 + sw128_offset(r, m & 7),
-                   make_uint4(y[m][0], y[m][1], y[m][2], y[m][3]));
-          sts128(sY + 16384 + sw128_offset(r, 6),
-                 make_uint4(E::pack(f[0], f[1]), E::pack(f[2], f[3]), E::pack(f[4], f[5]),
-                            E::pack(f[6], f[7])));
-          sts128(sY + 16384 + sw128_offset(r, 7),
-                 make_uint4(dspk[hh * 4], dspk[hh * 4 + 1], dspk[hh * 4 + 2], dspk[hh * 4 + 3]));
+          for (int m = 0; m < kM; ++m)  // element 8 m + key: chunk m of the row
+            sts64(sY + (m >> 3) * 16384 + sw128_offset(r, m & 7) + 8 * rg, y[m][0], y[m][1]);
+          sts64(sY + 16384 + sw128_offset(r, 6) + 8 * rg, E::pack(pr[0], pr[1]),
+                E::pack(pr[2], pr[3]));
+        }
+        // gate-gradient prefix: group 0's keys precede group 1's in the half
+        if (!wwait(bars[B_XCH + hh], w & 1, err, kErrXch)) return false;
+        const float other = lds32f(s_xch + ((hh * 2 + (rg ^ 1)) * 128 + r) * 4);
+        float run = da_run + (rg ? other : 0.f);
+        float ds[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          ds[i] = run * zj[i] * (1.f - zj[i]);
+          run += da[i];
+        }
+        da_run += sum4 + other;
+        const uint32_t ds0 = E::pack(ds[0], ds[1]), ds1 = E::pack(ds[2], ds[3]);
+        if (MODE == MODE_DQ) {
+          if (hh == 0) {
+            dsa0 = ds0;
+            dsa1 = ds1;
+          } else {
+            tmem_st2(lane_base + tq::YT + 56 + 2 * rg, dsa0, dsa1);
+            tmem_st2(lane_base + tq::YT + 60 + 2 * rg, ds0, ds1);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&bars[B_YB]);
+          }
+        } else {
+          sts64(sY + 16384 + sw128_offset(r, 7) + 8 * rg, ds0, ds1);
           fence_async_smem();
           mbar_arrive(&bars[hh ? B_YB : B_YA]);
         }
       }
-      if (!ok) break;
-      if (MODE == MODE_DQ) {
-        // ---- dq += ln2 R(-(carry + c0) theta) X   (X and the gate UMMA done)
-        if (!(ok = mbar_wait(&bars[B_XF], w & 1, err, kErrX))) break;
-        tc_fence_after();
-#pragma unroll 1
-        for (int g = 0; g < NP / 16; ++g) {
-          float sn[16], cs[16];
-          angles(carry, g, sn, cs);
-          uint32_t xv[2][16], qv2[2][16];
+      return true;
+    };
+
+    // dq += ln2 R(-(carry + c0) theta) X for this group's 32 pairs
+    auto dq_update = [&](int w) -> bool {
+      if (!wwait(bars[B_XF], w & 1, err, kErrX)) return false;
+      tc_fence_after();
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            tmem_ld16(lane_base + tq::X + 32 * g + 16 * i, xv[i]);
-            tmem_ld16(lane_base + tq::DQ + 32 * g + 16 * i, qv2[i]);
-          }
-          tmem_wait_ld();
+      for (int g = 0; g < 4; ++g) {  // 8 pairs (16 columns) per step
+        uint32_t xv[16], qv2[16];
+        tmem_ld16(lane_base + tq::X + 64 * rg + 16 * g, xv);
+        tmem_ld16(lane_base + tq::DQ + 64 * rg + 16 * g, qv2);
+        tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
-#pragma unroll
-            for (int e2 = 0; e2 < 8; ++e2) {
-              const int pl = 8 * i + e2;  // pair within the group
-              const float xe = __uint_as_float(xv[i][2 * e2]), xo = __uint_as_float(xv[i][2 * e2 + 1]);
-              const float c_ = cs[pl] * kLn2, s_ = sn[pl] * kLn2;
-              qv2[i][2 * e2] = __float_as_uint(__uint_as_float(qv2[i][2 * e2]) + fmaf(c_, xe, s_ * xo));
-              qv2[i][2 * e2 + 1] =
-                  __float_as_uint(__uint_as_float(qv2[i][2 * e2 + 1]) + fmaf(c_, xo, -s_ * xe));
-            }
-            tmem_st16(lane_base + tq::DQ + 32 * g + 16 * i, qv2[i]);
-          }
+        for (int e2 = 0; e2 < 8; ++e2) {
+          const float2 cs = unpack_cs(csc[8 * g + e2]);
+          const float c_ = cs.x * kLn2, s_ = cs.y * kLn2;
+          const float xe = __uint_as_float(xv[2 * e2]), xo = __uint_as_float(xv[2 * e2 + 1]);
+          qv2[2 * e2] = __float_as_uint(__uint_as_float(qv2[2 * e2]) + fmaf(c_, xe, s_ * xo));
+          qv2[2 * e2 + 1] =
+              __float_as_uint(__uint_as_float(qv2[2 * e2 + 1]) + fmaf(c_, xo, -s_ * xe));
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&bars[B_XFREE]);
+        tmem_st16(lane_base + tq::DQ + 64 * rg + 16 * g, qv2);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars[B_XFREE]);
+      return true;
+    };
+
+    if (ok) ok = gates(0);
+    if (ok) {
+      build_a();
+      if (MODE == MODE_DQ) load_cs();
+    }
+    for (int w = 0; ok && w <= WL; ++w) {
+      if (!(ok = halves(w))) break;
+      // next window's A operand first, so its G GEMM overlaps the dQ update
+      if (w < WL) {
+        if (!(ok = gates(w + 1))) break;
+        build_a();
+      }
+      if (MODE == MODE_DQ) {
+        if (!(ok = dq_update(w))) break;
+        if (w < WL) load_cs();
       }
     }
     if (MODE == MODE_DQ && ok) {
       // all GEMMs into DQ are done (the last window's B_XF was waited above)
       T* dqrow = reinterpret_cast<T*>(P.dq) + b * P.dqs[0] + h * P.dqs[1] + (int64_t)t * P.dqs[2];
 #pragma unroll 1
-      for (int c = 0; c < D / 16; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint32_t o[16];
-        tmem_ld16(lane_base + tq::DQ + 16 * c, o);
+        tmem_ld16(lane_base + tq::DQ + 64 * rg + 16 * c, o);
         tmem_wait_ld();
         uint32_t pk[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) pk[i] = E::pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
-        if (t < S) {
-          uint4* dst = reinterpret_cast<uint4*>(dqrow + 16 * c);
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(dqrow + 64 * rg + 16 * c);
           dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
       }
     }
+    __syncwarp();
+    regs_dec<128>();
   }
 
   tc_fence_before();
@@ -825,9 +941,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 }
 
 // ------------------------------------------------------------------ host
-template <int MODE>
+// K^(m) buffer layout and count; returns the dynamic shared memory needed
 static int plan(Params& p) {
-  using L = SmemTail<MODE>;
+  using L = SmemTail;
   int off = 0;
   for (int s = 0; s < NS; ++s) {
     p.b_slab_off[s] = off;
@@ -840,7 +956,7 @@ static int plan(Params& p) {
 
 template <typename T, int MODE>
 static cudaError_t launch_mode(Params& p, bool bias, int B, int H, int S, cudaStream_t st) {
-  const int smem = plan<MODE>(p);
+  const int smem = plan(p);
   if (smem > kSmemLimit) return cudaErrorInvalidValue;
   dim3 grid((S + kBM - 1) / kBM, H, B);
   cudaError_t e;
@@ -871,6 +987,10 @@ bool tc_bwd_supported(const BwdArgs& a, int dtype) {
   if (!rows16(a.q, a.qs) || !rows16(a.k, a.ks) || !rows16(a.v, a.vs) ||
       !rows16(a.dout, a.dos) || !rows16(a.dq, a.dqs))
     return false;
+  // small theta keeps more Chebyshev terms: the K^(m) buffers must still fit
+  tcb::Params p;
+  tcx::fill_coefficients(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
+  if (tcb::plan(p) > tcx::kSmemLimit) return false;
   return tcx::get_encoder() != nullptr;
 }
 
