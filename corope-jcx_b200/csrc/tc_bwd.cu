@@ -30,9 +30,12 @@
 // two row warpgroups that share every row -- warpgroup g takes keys 4g..4g+3
 // of each 8-key half window and rotation pairs 32g..32g+31 of the A operand
 // and the dQ update, and the two meet once per half through shared memory
-// for the running gate-gradient prefix; warp 8 TMA; warp 9 UMMA for the
-// gate, dP and G GEMMs; warp 10 UMMA for the launch's own GEMMs; warps 12-15
-// build K^(m) (and, in the dK launch, run the per-dimension combine).
+// for the running gate-gradient prefix; warp 8 TMA; warp 9 UMMA for the G
+// GEMMs; warp 10 UMMA for the launch's own GEMMs; warp 11 UMMA for the gate
+// and dP GEMMs; warps 12-15 build K^(m) (and, in the dK launch, run the
+// per-dimension combine).  Each UMMA issue costs the issuing thread about
+// as long as the tensor core takes to read the operands from shared memory,
+// so the GEMM families sit on separate threads.
 // Registers are re-balanced with setmaxnreg: rows 176, builders 104, the
 // TMA/UMMA warpgroup 56 (2 x 176 + 104 + 56 = 4 x 128, the launch budget).
 // Every wait is bounded as in the forward.
@@ -99,6 +102,8 @@ struct Params {
   int nb;
   int b_slab_off[2];
   int b_buf_bytes;
+  int max_items;   // K^(m) item descriptors per builder thread
+  int bop;         // shared-memory offset of the K^(m) buffers
   float coef[kM][64];
 };
 
@@ -108,18 +113,17 @@ constexpr int S_DO = S_Q + NS * 16384;
 constexpr int S_K = S_DO + NS * 16384;       // [2 stages][NS][32 rows][128 B]
 constexpr int S_V = S_K + 2 * NS * 4096;
 constexpr int S_AV = S_V + 2 * NS * 4096;    // A operand rows [NS][128][128 B]
-constexpr int S_Y = S_AV + NS * 16384;       // dK: Y | P | dS rows [NS][128][128 B];
+constexpr int S_Y = S_AV + NS * 16384;       // dK: Y | P rows [NS][128][128 B];
                                              // dQ: staged (cos, sin) [8 chunks][256 threads][16 B]
-struct SmemTail {
-  static constexpr int COEF = S_Y + NS * 16384;
+constexpr int S_DS = S_Y + NS * 16384;       // dK: dS rows [128][128 B] (bytes 96..127 used)
+template <int MODE> struct SmemTail {
+  static constexpr int COEF = S_DS + (MODE == MODE_DK ? 16384 : 0);
   static constexpr int TH = COEF + kM * NP * 4;
   static constexpr int BAR = TH + NP * 4;
   static constexpr int NBAR = 40;
   static constexpr int SLOT = BAR + NBAR * 8;
   static constexpr int XCH = (SLOT + 16 + 15) & ~15;  // gate-gradient sums [half][group][128]
-  static constexpr int MAX_ITEMS = (2 * 8 * 8 * kM + 127) / 128;
-  static constexpr int ITEMS = XCH + 2 * 2 * 128 * 4;
-  static constexpr int BOP = (ITEMS + MAX_ITEMS * 128 * 8 + 1023) & ~1023;
+  static constexpr int ITEMS = XCH + 2 * 2 * 128 * 4;  // then the K^(m) buffers at Params::bop
 };
 
 // tensor memory columns
@@ -129,9 +133,9 @@ constexpr uint32_t X = 0, DQ = 128, G = 256, SG0 = 368, DP0 = 400,
 static_assert(YT + 64 <= 512, "tmem");
 }  // namespace tq
 namespace tk {  // dK launch
-constexpr uint32_t G = 0, SG0 = 112, DP0 = 128, AVT = 144, C0 = 208, C1 = 352;
-// C region: [0,112) C^T terms x keys, [112,128) dO^T (P | dS), [128,144) Q^T (P | dS)
-static_assert(C1 + 144 <= 512, "tmem");
+// C0 / C1: C^T of the window's halves (terms x keys); DVK: dV^T (16 keys) | dK_gate^T (16 keys)
+constexpr uint32_t G = 0, SG0 = 112, DP0 = 128, AVT = 144, C0 = 208, C1 = 320, DVK = 432;
+static_assert(DVK + 32 <= 512, "tmem");
 }  // namespace tk
 
 enum {
@@ -143,8 +147,9 @@ enum {
   B_YA = 22, B_YDONE = 23, B_YB = 24,
   B_XF = 25, B_XFREE = 26, B_YTFREE = 27,        // dQ launch
   B_CF = 28, B_CE = 30, B_YFREE = 32,            // dK launch: [half] x 2
-  B_DRAIN5 = 34, B_DRAIN6 = 35,
-  B_XCH = 36                                     // [half]
+  B_DRAIN11 = 33, B_DRAIN5 = 34, B_DRAIN6 = 35,
+  B_XCH = 36,                                    // [half]
+  B_CF2 = 38, B_CE2 = 39                         // dK launch: dV / dK_gate GEMMs
 };
 
 __device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&r)[4]) {
@@ -164,7 +169,7 @@ __device__ __forceinline__ float2 unpack_cs(uint32_t v) {
 template <typename T, int MODE, bool HAS_BIAS>
 __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant__ Params P) {
   using E = ElemTraits<T>;
-  using L = SmemTail;
+  using L = SmemTail<MODE>;
   using namespace sm100;
   // gate/dP accumulators: double-buffered in the dQ launch, single in the dK
   // launch (its tensor memory holds the A operand and two C regions)
@@ -192,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     mbar_init(&bars[B_Q], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[B_KVF + i], 1);
-      mbar_init(&bars[B_KVE + i], 2 + 128);  // two UMMA issuers + the builders
+      mbar_init(&bars[B_KVE + i], 2 + 128);  // warps 10 and 11 + the builders
       mbar_init(&bars[B_SDF + i], 1);
       mbar_init(&bars[B_SDE + i], 256);
       mbar_init(&bars[B_GF + i], 1);
@@ -200,6 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       mbar_init(&bars[B_CE + i], 128);
       mbar_init(&bars[B_XCH + i], 256);
     }
+    mbar_init(&bars[B_CF2], 1);
+    mbar_init(&bars[B_CE2], 128);
     for (int i = 0; i < 4; ++i) {
       mbar_init(&bars[B_BF + i], 128);
       mbar_init(&bars[B_BE + i], MODE == MODE_DQ ? 2 : 1);  // G (+ X) done with K^(m)
@@ -214,6 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     mbar_init(&bars[B_YTFREE], 1);
     mbar_init(&bars[B_YFREE], 1);
     mbar_init(&bars[B_DRAIN5], 1);
+    mbar_init(&bars[B_DRAIN11], 1);
     mbar_init(&bars[B_DRAIN6], 1);
     fence_mbar_init();
   }
@@ -222,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
   // The K^(m) buffers start at zero: the builders skip the pruned (term,
   // head-dim) entries, which the dQ launch's X GEMM still reads densely.
   {
-    uint4* kb = reinterpret_cast<uint4*>(smem + L::BOP);
+    uint4* kb = reinterpret_cast<uint4*>(smem + P.bop);
     const int n16 = (2 * P.nb * P.b_buf_bytes) / 16;
     for (int i = tid; i < n16; i += kThreads) kb[i] = make_uint4(0u, 0u, 0u, 0u);
     fence_async_smem();
@@ -238,7 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
   const uint32_t sQ = smem_u32(smem + S_Q), sDO = smem_u32(smem + S_DO);
   const uint32_t sK = smem_u32(smem + S_K), sV = smem_u32(smem + S_V);
   const uint32_t sAV = smem_u32(smem + S_AV), sY = smem_u32(smem + S_Y);
-  const uint32_t sB = smem_u32(smem + L::BOP);
+  const uint32_t sB = smem_u32(smem + P.bop);
+  const uint32_t sDS = smem_u32(smem + S_DS);
   const uint32_t s_th_u = smem_u32(s_th), s_coef_u = smem_u32(s_coef);
   const uint32_t T_SG0 = MODE == MODE_DQ ? tq::SG0 : tk::SG0;
   const uint32_t T_DP0 = MODE == MODE_DQ ? tq::DP0 : tk::DP0;
@@ -280,42 +289,20 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           if (last_use[st] >= 0) mbar_wait(&bars[B_KVF + st], last_use[st] & 1, err, kErrDrain);
       }
     } else if (warp == 9) {
-      // -------------------------------- UMMA: gate, dP and G GEMMs
+      // ---------------------------------------------- UMMA: G GEMMs
+      // The barriers that complete early (K^(m) built, previous half read)
+      // are checked before the A operand's, so each half is issued as soon
+      // as its last input lands.
       if (lane == 0) {
-        const uint32_t id_n16 = idesc_f16(128, 16, E::kBf16, false);
         bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
-        tc_fence_after();
-        // gate scores Q K^T and dP = dO V^T of window w into buffer w % NSD
-        auto sd = [&](int w) -> bool {
-          const int n = w >> 1, st = n & 1, sb = w % NSD;
-          if (!mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) return false;
-          if (w >= NSD && !mbar_wait(&bars[B_SDE + sb], ((w / NSD) - 1) & 1, err, kErrSdEmpty))
-            return false;
-          tc_fence_after();
-          const uint32_t kt = sK + st * NS * 4096 + (w & 1) * kW * 128;
-          const uint32_t vt = sV + st * NS * 4096 + (w & 1) * kW * 128;
-          const uint32_t dsg = tmem + T_SG0 + 16 * sb;
-          const uint32_t ddp = tmem + T_DP0 + 16 * sb;
-#pragma unroll
-          for (int s = 0; s < KSTEPS; ++s) {
-            const uint32_t off = (s >> 2) * 16384 + 32 * (s & 3);
-            const uint32_t koff = (s >> 2) * 4096 + 32 * (s & 3);
-            mma_ss(dsg, sdesc_kmajor(sQ + off), sdesc_kmajor(kt + koff), id_n16, s > 0);
-            mma_ss(ddp, sdesc_kmajor(sDO + off), sdesc_kmajor(vt + koff), id_n16, s > 0);
-          }
-          mma_commit(&bars[B_SDF + sb]);
-          if (w & 1) mma_commit(&bars[B_KVE + st]);  // last window of the tile
-          return true;
-        };
-        for (int w = 0; ok && w < NSD && w <= WL; ++w) ok = sd(w);
         for (int w = 0; ok && w <= WL; ++w) {
           const int buf = w % nb, use = w / nb;
-          if (!(ok = mbar_wait(&bars[B_AVF], w & 1, err, kErrAv))) break;
           for (int hh = 0; hh < 2 && ok; ++hh) {
             ok = mbar_wait(&bars[B_BF + 2 * hh + buf], use & 1, err, kErrB);
             // the single G region: the rows have consumed the previous half
             const int prev = 2 * w + hh - 1;
             if (ok && prev >= 0) ok = mbar_wait(&bars[B_GE], prev & 1, err, kErrGEmpty);
+            if (ok && hh == 0) ok = mbar_wait(&bars[B_AVF], w & 1, err, kErrAv);
             if (!ok) break;
             tc_fence_after();
             const uint32_t bb = sB + (hh * nb + buf) * P.b_buf_bytes;
@@ -334,11 +321,40 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             mma_commit(&bars[B_GF + hh]);
             mma_commit(&bars[B_BE + 2 * hh + buf]);
           }
-          if (!ok) break;
-          if (w + NSD <= WL) ok = sd(w + NSD);
         }
         mma_commit(&bars[B_DRAIN5]);
         mbar_wait(&bars[B_DRAIN5], 0, err, kErrDrain);
+      }
+    } else if (warp == 11) {
+      // ------------------------------------ UMMA: gate scores and dP
+      // Q K^T and dO V^T of window w into buffer w % NSD, running ahead of
+      // the rows as far as the buffers allow.
+      if (lane == 0) {
+        const uint32_t id_n16 = idesc_f16(128, 16, E::kBf16, false);
+        bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
+        for (int w = 0; ok && w <= WL; ++w) {
+          const int n = w >> 1, st = n & 1, sb = w % NSD;
+          if (!(ok = mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull))) break;
+          if (w >= NSD &&
+              !(ok = mbar_wait(&bars[B_SDE + sb], ((w / NSD) - 1) & 1, err, kErrSdEmpty)))
+            break;
+          tc_fence_after();
+          const uint32_t kt = sK + st * NS * 4096 + (w & 1) * kW * 128;
+          const uint32_t vt = sV + st * NS * 4096 + (w & 1) * kW * 128;
+          const uint32_t dsg = tmem + T_SG0 + 16 * sb;
+          const uint32_t ddp = tmem + T_DP0 + 16 * sb;
+#pragma unroll
+          for (int s = 0; s < KSTEPS; ++s) {
+            const uint32_t off = (s >> 2) * 16384 + 32 * (s & 3);
+            const uint32_t koff = (s >> 2) * 4096 + 32 * (s & 3);
+            mma_ss(dsg, sdesc_kmajor(sQ + off), sdesc_kmajor(kt + koff), id_n16, s > 0);
+            mma_ss(ddp, sdesc_kmajor(sDO + off), sdesc_kmajor(vt + koff), id_n16, s > 0);
+          }
+          mma_commit(&bars[B_SDF + sb]);
+          if (w & 1) mma_commit(&bars[B_KVE + st]);  // last window of the tile
+        }
+        mma_commit(&bars[B_DRAIN11]);
+        mbar_wait(&bars[B_DRAIN11], 0, err, kErrDrain);
       }
     } else if (warp == 10) {
       // -------------------------------- UMMA: the launch's own GEMMs
@@ -392,22 +408,30 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
               if (!ok) break;
               tc_fence_after();
               const uint32_t creg = tmem + (hh ? tk::C1 : tk::C0);
+              // C^T = v^T Y: A = v^T (M = head dim), B = Y^T (N = term x key),
+              // K = the 128 query rows, 16 per step
 #pragma unroll 1
-              for (int s = 0; s < 8; ++s) {  // K = 128 query rows, 16 per step
-                const uint32_t ko = 2048 * s;
-                // C^T = v^T Y: A = v^T (M = head dim), B = Y^T (N = term x key)
-                mma_ss(creg, sdesc_mnmajor(sAV + ko, 16384), sdesc_mnmajor(sY + ko, 16384), id_c,
-                       s > 0);
-                // dO^T (P | dS) and Q^T (P | dS): B = elements 112..127 of the rows
-                mma_ss(creg + 112, sdesc_mnmajor(sDO + ko, 16384),
-                       sdesc_mnmajor(sY + 16384 + ko + 96, 16384), id_s, s > 0);
-                mma_ss(creg + 128, sdesc_mnmajor(sQ + ko, 16384),
-                       sdesc_mnmajor(sY + 16384 + ko + 96, 16384), id_s, s > 0);
-              }
+              for (int s = 0; s < 8; ++s)
+                mma_ss(creg, sdesc_mnmajor(sAV + 2048 * s, 16384), sdesc_mnmajor(sY + 2048 * s, 16384),
+                       id_c, s > 0);
               mma_commit(&bars[B_CF + hh]);
-              mma_commit(&bars[hh ? B_YFREE : B_YDONE]);
+              if (hh == 0) mma_commit(&bars[B_YDONE]);
             }
             if (!ok) break;
+            // once per window: dV^T = dO^T P and dK_gate^T = Q^T dS over the
+            // 16 keys (B = bytes 96..127 of the P rows and of the dS rows)
+            if (w > 0 && !(ok = mbar_wait(&bars[B_CE2], (w - 1) & 1, err, kErrCEmpty))) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int s = 0; s < 8; ++s) {
+              const uint32_t ko = 2048 * s;
+              mma_ss(tmem + tk::DVK, sdesc_mnmajor(sDO + ko, 16384),
+                     sdesc_mnmajor(sY + 16384 + ko + 96, 16384), id_s, s > 0);
+              mma_ss(tmem + tk::DVK + 16, sdesc_mnmajor(sQ + ko, 16384),
+                     sdesc_mnmajor(sDS + ko + 96, 16384), id_s, s > 0);
+            }
+            mma_commit(&bars[B_CF2]);
+            mma_commit(&bars[B_YFREE]);  // A rows, Y | P rows and dS rows all read
             if (w & 1) mma_commit(&bars[B_KVE + ((w >> 1) & 1)]);
           }
         }
@@ -421,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     // ----------------------- K^(m) builder (+ per-dimension combine, dK launch)
     regs_dec<kBldRegs>();
     named_bar(1, kThreads);
-    constexpr int kMaxItems = L::MAX_ITEMS;
+    const int kMaxItems = P.max_items;
     const int gt = tid - 384;
     uint2* items = reinterpret_cast<uint2*>(smem + L::ITEMS);
     int my_n = 0;
@@ -525,47 +549,60 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     };
 
     auto combine = [&](int w) -> bool {
-#pragma unroll 1
+      float dk[16];
+#pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         if (!wwait(bars[B_CF + hh], w & 1, err, kErrC)) return false;
         tc_fence_after();
         const uint32_t creg = lane_base + (hh ? tk::C1 : tk::C0);
-        float dk[8], dv[8];
-        {
-          uint32_t g[16];
-          tmem_ld16(creg + 112, g);  // dO^T P (0..7) | dO^T dS (8..15)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dk[8 * hh + j] = 0.f;
+#pragma unroll
+        for (int c0 = 0; c0 < kM / 2; c0 += 2) {  // terms 2c, 2c+1 for the 8 keys
+          uint32_t g[2][16];
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+            if (c0 + i < kM / 2) tmem_ld16(creg + 16 * (c0 + i), g[i]);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 8; ++j) dv[j] = __uint_as_float(g[j]);
-          tmem_ld16(creg + 128, g);  // Q^T P | Q^T dS (8..15)
-          tmem_wait_ld();
+          for (int i = 0; i < 2; ++i) {
+            const int c = c0 + i;
+            if (c >= kM / 2) continue;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) dk[j] = __uint_as_float(g[8 + j]);
-        }
-#pragma unroll
-        for (int c = 0; c < kM / 2; ++c) {  // terms 2c, 2c+1 for the 8 keys
-          uint32_t g[16];
-          tmem_ld16(creg + 16 * c, g);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float own = __uint_as_float(g[j]);
-            const float odd = __uint_as_float(g[8 + j]);
-            const float partner = __shfl_xor_sync(0xffffffffu, odd, 1);
-            dk[j] = fmaf(cm[2 * c], own, dk[j]);
-            dk[j] = fmaf(cm[2 * c + 1], partner, dk[j]);
+            for (int j = 0; j < 8; ++j) {
+              const float own = __uint_as_float(g[i][j]);
+              const float partner = __shfl_xor_sync(0xffffffffu, __uint_as_float(g[i][8 + j]), 1);
+              dk[8 * hh + j] = fmaf(cm[2 * c], own, dk[8 * hh + j]);
+              dk[8 * hh + j] = fmaf(cm[2 * c + 1], partner, dk[8 * hh + j]);
+            }
           }
         }
         tc_fence_before();
         mbar_arrive(&bars[B_CE + hh]);
-        const int d = gt;
+      }
+      float dv[16];
+      {
+        if (!wwait(bars[B_CF2], w & 1, err, kErrC)) return false;
+        tc_fence_after();
+        uint32_t g[2][16];
+        tmem_ld16(lane_base + tk::DVK, g[0]);       // dO^T P  (16 keys)
+        tmem_ld16(lane_base + tk::DVK + 16, g[1]);  // Q^T dS  (16 keys)
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars[B_CE2]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int key = w * kW + hh * 8 + j;
-          if (key < S) {
-            atomicAdd(dk32 + (int64_t)key * D + d, dk[j]);
-            atomicAdd(dv32 + (int64_t)key * D + d, dv[j]);
-          }
+        for (int j = 0; j < 16; ++j) {
+          dv[j] = __uint_as_float(g[0][j]);
+          dk[j] += __uint_as_float(g[1][j]);
+        }
+      }
+      const int d = gt;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int key = w * kW + j;
+        if (key < S) {
+          atomicAdd(dk32 + (int64_t)key * D + d, dk[j]);
+          atomicAdd(dv32 + (int64_t)key * D + d, dv[j]);
         }
       }
       return true;
@@ -833,7 +870,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 #pragma unroll
           for (int m = 0; m < kM; ++m)  // element 8 m + key: chunk m of the row
             sts64(sY + (m >> 3) * 16384 + sw128_offset(r, m & 7) + 8 * rg, y[m][0], y[m][1]);
-          sts64(sY + 16384 + sw128_offset(r, 6) + 8 * rg, E::pack(pr[0], pr[1]),
+          sts64(sY + 16384 + sw128_offset(r, 6 + hh) + 8 * rg, E::pack(pr[0], pr[1]),
                 E::pack(pr[2], pr[3]));
         }
         // gate-gradient prefix: group 0's keys precede group 1's in the half
@@ -860,7 +897,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             mbar_arrive(&bars[B_YB]);
           }
         } else {
-          sts64(sY + 16384 + sw128_offset(r, 7) + 8 * rg, ds0, ds1);
+          sts64(sDS + sw128_offset(r, 6 + hh) + 8 * rg, ds0, ds1);
           fence_async_smem();
           mbar_arrive(&bars[hh ? B_YB : B_YA]);
         }
@@ -942,21 +979,25 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 
 // ------------------------------------------------------------------ host
 // K^(m) buffer layout and count; returns the dynamic shared memory needed
+template <int MODE>
 static int plan(Params& p) {
-  using L = SmemTail;
-  int off = 0;
+  using L = SmemTail<MODE>;
+  int off = 0, rows = 0;
   for (int s = 0; s < NS; ++s) {
     p.b_slab_off[s] = off;
     off += p.nrow[4 * s] * 128;
   }
+  for (int s = 0; s < KSTEPS; ++s) rows += p.nrow[s];
+  p.max_items = (2 * rows + 127) / 128;  // (term x key row, 8-element chunk) items per builder
+  p.bop = (L::ITEMS + p.max_items * 128 * 8 + 1023) & ~1023;
   p.b_buf_bytes = (off + 1023) & ~1023;
-  p.nb = (L::BOP + 4 * p.b_buf_bytes + 1024 <= kSmemLimit) ? 2 : 1;
-  return L::BOP + 2 * p.nb * p.b_buf_bytes + 1024;
+  p.nb = (p.bop + 4 * p.b_buf_bytes + 1024 <= kSmemLimit) ? 2 : 1;
+  return p.bop + 2 * p.nb * p.b_buf_bytes + 1024;
 }
 
 template <typename T, int MODE>
 static cudaError_t launch_mode(Params& p, bool bias, int B, int H, int S, cudaStream_t st) {
-  const int smem = plan(p);
+  const int smem = plan<MODE>(p);
   if (smem > kSmemLimit) return cudaErrorInvalidValue;
   dim3 grid((S + kBM - 1) / kBM, H, B);
   cudaError_t e;
@@ -990,7 +1031,8 @@ bool tc_bwd_supported(const BwdArgs& a, int dtype) {
   // small theta keeps more Chebyshev terms: the K^(m) buffers must still fit
   tcb::Params p;
   tcx::fill_coefficients(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
-  if (tcb::plan(p) > tcx::kSmemLimit) return false;
+  if (tcb::plan<tcb::MODE_DQ>(p) > tcx::kSmemLimit || tcb::plan<tcb::MODE_DK>(p) > tcx::kSmemLimit)
+    return false;
   return tcx::get_encoder() != nullptr;
 }
 
