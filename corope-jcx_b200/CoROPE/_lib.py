@@ -86,6 +86,8 @@ def load_library():
             lib.corope_bwd.restype = ctypes.c_int
             lib.corope_bwd_workspace_bytes.argtypes = [ctypes.POINTER(BwdParams)]
             lib.corope_bwd_workspace_bytes.restype = ctypes.c_size_t
+            lib.corope_bwd_min_workspace_bytes.argtypes = [ctypes.POINTER(BwdParams)]
+            lib.corope_bwd_min_workspace_bytes.restype = ctypes.c_size_t
             lib.corope_last_error.argtypes = []
             lib.corope_last_error.restype = ctypes.c_char_p
             lib.corope_bwd_noalloc.argtypes = [ctypes.POINTER(BwdParams), ctypes.c_void_p]
@@ -198,9 +200,10 @@ def fwd(q, k, v, o, m, l, a, lse, sm_scale, theta, bias=None, algo="auto", theta
 
 
 def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="auto",
-        thetas=None):
+        thetas=None, workspace="full"):
     """Launch corope_bwd on the current stream of q with a torch-allocated
-    workspace."""
+    workspace: "full" (corope_bwd_workspace_bytes, the fastest), "min"
+    (corope_bwd_min_workspace_bytes) or a byte count in between."""
     lib = load_library()
     B, H, S, D = q.shape
     p = BwdParams()
@@ -219,7 +222,12 @@ def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="a
     p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, k.shape[1], S, D
     p.sm_scale, p.theta = float(sm_scale), float(theta)
     p.causal, p.dtype, p.algo = 1, _dtype_code(q), algo_code(algo)
-    nbytes = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
+    if workspace == "full":
+        nbytes = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
+    elif workspace == "min":
+        nbytes = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
+    else:
+        nbytes = int(workspace)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
     p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
     stream = torch.cuda.current_stream(q.device).cuda_stream

@@ -17,7 +17,9 @@ bool tc_fwd_supported(const FwdArgs& a, int dtype);
 cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st);
 int tc_take_device_error();
 bool tc_bwd_supported(const BwdArgs& a, int dtype);
-cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st);
+cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* handoff,
+                          size_t handoff_bytes);
+int64_t tc_bwd_handoff_bytes_per_bh(int S);
 int tcb_take_device_error();
 cudaError_t bwd_pre_launch(const BwdArgs& a, int dtype, cudaStream_t st);
 cudaError_t bwd_post_launch(const BwdArgs& a, int dtype, cudaStream_t st);
@@ -144,10 +146,22 @@ static int fwd_common(const corope_fwd_params_t* p, corope_stream_t stream, bool
 
 static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
+// Minimum workspace: delta and lse rows, fp32 dk / dv accumulators.
 static size_t bwd_ws(const corope_bwd_params_t* p) {
   const size_t rows = (size_t)p->batch * p->heads * p->seq_len;
   const size_t kv = (size_t)p->batch * p->kv_heads * p->seq_len * p->head_dim;
   return 2 * align256(rows * 4) + 2 * align256(kv * 4);
+}
+
+// Optional hand-off region after it (tensor-core backward only): the dQ
+// kernel's per-(row, key) results for the dK kernel, 20,992 bytes per 128 query
+// rows x 16 keys; with less, the (b, h) slices go through it in chunks, or the
+// dK kernel recomputes them.
+static size_t bwd_handoff_ws(const corope_bwd_params_t* p) {
+  if (p->head_dim != 128 || p->algo == COROPE_ALGO_EXACT ||
+      (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16))
+    return 0;
+  return align256((size_t)p->batch * p->heads * (size_t)tc_bwd_handoff_bytes_per_bh(p->seq_len));
 }
 
 extern "C" {
@@ -161,6 +175,13 @@ int corope_mqa_fwd(const corope_fwd_params_t* p, corope_stream_t stream) {
 }
 
 size_t corope_bwd_workspace_bytes(const corope_bwd_params_t* p) {
+  if (!p || p->batch <= 0 || p->heads <= 0 || p->kv_heads <= 0 || p->seq_len <= 0 ||
+      p->head_dim <= 0)
+    return 0;
+  return bwd_ws(p) + bwd_handoff_ws(p);
+}
+
+size_t corope_bwd_min_workspace_bytes(const corope_bwd_params_t* p) {
   if (!p || p->batch <= 0 || p->heads <= 0 || p->kv_heads <= 0 || p->seq_len <= 0 ||
       p->head_dim <= 0)
     return 0;
@@ -220,7 +241,10 @@ int corope_bwd(const corope_bwd_params_t* p, corope_stream_t stream) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
   if (p->algo != COROPE_ALGO_EXACT && tc_ok) {
     e = bwd_pre_launch(a, p->dtype, st);
-    if (e == cudaSuccess) e = tc_bwd_launch(a, p->dtype, st);
+    const size_t base = bwd_ws(p);
+    if (e == cudaSuccess)
+      e = tc_bwd_launch(a, p->dtype, st, static_cast<char*>(p->workspace) + base,
+                        p->workspace_bytes - base);
     if (e == cudaSuccess) e = bwd_post_launch(a, p->dtype, st);
   } else {
     e = exact_bwd_launch(a, p->dtype, st);

@@ -47,13 +47,13 @@ void* g_scratch_ptr[kMaxDevices] = {};
 extern "C" {
 
 int corope_bwd(const corope_bwd_params_t* p, corope_stream_t stream);
-size_t corope_bwd_workspace_bytes(const corope_bwd_params_t* p);
+size_t corope_bwd_min_workspace_bytes(const corope_bwd_params_t* p);
 
 size_t corope_bwd_noalloc_scratch_bytes(void) { return kScratchBytes; }
 
 int corope_bwd_noalloc(const corope_bwd_params_t* p, corope_stream_t stream) {
   if (!p) return corope_bwd(p, stream);  // reports the NULL-params error
-  const size_t need = corope_bwd_workspace_bytes(p);
+  const size_t need = corope_bwd_min_workspace_bytes(p);
   if (need > kScratchBytes) {
     char msg[200];
     snprintf(msg, sizeof(msg),
@@ -80,7 +80,7 @@ int corope_bwd_noalloc(const corope_bwd_params_t* p, corope_stream_t stream) {
   }
   corope_bwd_params_t q = *p;
   q.workspace = scratch;
-  q.workspace_bytes = kScratchBytes;
+  q.workspace_bytes = kScratchBytes;  // what is left after the minimum may serve as hand-off
   return corope_bwd(&q, stream);
 }
 

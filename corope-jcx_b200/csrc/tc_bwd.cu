@@ -104,6 +104,9 @@ struct Params {
   int b_buf_bytes;
   int max_items;   // K^(m) item descriptors per builder thread
   int bop;         // shared-memory offset of the K^(m) buffers
+  uint8_t* handoff;     // dQ launch -> dK launch, per (b, h, query tile, window) block
+  int64_t blocks_bh;    // hand-off blocks per (b, h)
+  int bh0;              // first (b, h) of this launch (blockIdx.y counts from it)
   float coef[kM][64];
 };
 
@@ -137,6 +140,22 @@ namespace tk {  // dK launch
 constexpr uint32_t G = 0, SG0 = 112, DP0 = 128, AVT = 144, C0 = 208, C1 = 320, DVK = 432;
 static_assert(DVK + 32 <= 512, "tmem");
 }  // namespace tk
+
+// Hand-off block (one per (b, h, query tile, window), 128 rows): what the dK
+// launch needs to rebuild Y without the gates, the G GEMM or the Clenshaw
+// sums.  Quad q = 2 * half + row group holds keys 8 half + 4 group + 0..3.
+constexpr int HB_DL = 0;                       // dl, fp32        [4 quads][128 rows][4]
+constexpr int HB_PD = HB_DL + 4 * 128 * 16;    // P | dS, 16-bit  [4 quads][128 rows][4 + 4]
+constexpr int HB_U = HB_PD + 4 * 128 * 16;     // u, 16-bit fixed [4 quads][128 rows][4]
+constexpr int HB_C = HB_U + 4 * 128 * 8;       // carry, fp32     [128 rows]
+constexpr int kHB = HB_C + 128 * 4;
+// first block of query tile qt within its (b, h): tiles before it are full
+// (8 (q + 1) windows each)
+__host__ __device__ constexpr int64_t tile_block0(int qt) { return 4ll * qt * (qt + 1); }
+__device__ __forceinline__ uint32_t u_encode(float u) {
+  return __float2uint_rn(fminf(fmaxf((u + 1.0f) * 32767.5f, 0.0f), 65535.0f));
+}
+__device__ __forceinline__ float u_decode(uint32_t q) { return fmaf((float)q, 1.0f / 32767.5f, -1.0f); }
 
 enum {
   B_Q = 0, B_KVF = 1, B_KVE = 3, B_SDF = 5, B_SDE = 7, B_AVF = 9,
@@ -186,7 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int qt = gridDim.x - 1 - blockIdx.x;
-  const int h = blockIdx.y, b = blockIdx.z;
+  const int bh = P.bh0 + blockIdx.y;
+  const int h = bh % P.H, b = bh / P.H;
   const int hk = h / (P.H / P.Hkv);
   const int q0 = qt * kBM;
   const int S = P.S;
@@ -784,8 +804,14 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     };
 
     // the two halves of window w
+    uint8_t* const hblk0 =
+        (MODE == MODE_DQ && P.handoff)
+            ? P.handoff + ((int64_t)blockIdx.y * P.blocks_bh + tile_block0(qt)) * kHB
+            : nullptr;
     auto halves = [&](int w) -> bool {
       const int j0 = w * kW;
+      uint8_t* const hblk = hblk0 ? hblk0 + (int64_t)w * kHB : nullptr;
+      if (hblk && rg == 0) *reinterpret_cast<float*>(hblk + HB_C + 4 * r) = carry;
       if (MODE == MODE_DK) {
         // the previous window's C GEMMs are done with the A rows and the Y
         // buffer: copy this window's A half from tensor to shared memory
@@ -885,6 +911,16 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         }
         da_run += sum4 + other;
         const uint32_t ds0 = E::pack(ds[0], ds[1]), ds1 = E::pack(ds[2], ds[3]);
+        if (hblk) {
+          const int qd = 2 * hh + rg;
+          *reinterpret_cast<float4*>(hblk + HB_DL + (qd * 128 + r) * 16) =
+              make_float4(dl[0], dl[1], dl[2], dl[3]);
+          *reinterpret_cast<uint4*>(hblk + HB_PD + (qd * 128 + r) * 16) =
+              make_uint4(E::pack(pr[0], pr[1]), E::pack(pr[2], pr[3]), ds0, ds1);
+          *reinterpret_cast<uint2*>(hblk + HB_U + (qd * 128 + r) * 8) =
+              make_uint2(u_encode(uj[0]) | (u_encode(uj[1]) << 16),
+                         u_encode(uj[2]) | (u_encode(uj[3]) << 16));
+        }
         if (MODE == MODE_DQ) {
           if (hh == 0) {
             dsa0 = ds0;
@@ -977,6 +1013,309 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
+// ------------------------------------------------------------------
+// dK launch fed by the dQ launch's hand-off.  Per window it only rebuilds
+// the A rows v = R((carry + c0) theta) q and Y_m = dl T_m(u), then runs
+//   C^T = v^T Y (each half), dV^T = dO^T P and dK_gate^T = Q^T dS
+// on the tensor cores and the per-dimension combine with fp32 atomics into
+// the dk / dv accumulators.  No K/V tiles, gates, G GEMM or K^(m) are needed.
+//
+// Roles (512 threads): warps 0-7 two row warpgroups (group g: pairs
+// 32g..32g+31 of the A rows, keys 4g..4g+3 of each half); warp 8 TMA; warp 9
+// UMMA; warps 12-15 combine (one head dim per thread).  The A rows and the
+// tensor-memory accumulators are double-buffered over windows.
+namespace k2 {
+constexpr int Q = 0, DO = 32768, AV = 65536;  // AV: 2 buffers of [NS][128][128 B]
+constexpr int YA = AV + 2 * 32768;            // Y half A | P (chunks 6-7 of slab 1)
+constexpr int YB = YA + 32768;                // Y half B | dS (chunks 6-7 of slab 1)
+constexpr int COEF = YB + 32768;
+constexpr int TH = COEF + kM * NP * 4;
+constexpr int BAR = TH + NP * 4;
+constexpr int SLOT = BAR + 16 * 8;
+constexpr int TOTAL = SLOT + 16;
+enum { B_Q = 0, B_RDY = 1, B_AVE = 2, B_YFREE = 4, B_CF = 5, B_CE = 7, B_DRAIN = 9 };
+// tensor memory: buffer b at 256 b: C^T half A, C^T half B, dV^T | dK_gate^T
+constexpr uint32_t C0 = 0, C1 = 112, DVK = 224, BUF = 256;
+}  // namespace k2
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant__ Params P) {
+  using E = ElemTraits<T>;
+  using namespace sm100;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + k2::BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + k2::SLOT);
+  float* s_coef = reinterpret_cast<float*>(smem + k2::COEF);
+  float* s_th = reinterpret_cast<float*>(smem + k2::TH);
+  int* err = &g_corope_bwd_error;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qt = gridDim.x - 1 - blockIdx.x;
+  const int bh = P.bh0 + blockIdx.y;
+  const int h = bh % P.H, b = bh / P.H;
+  const int hk = h / (P.H / P.Hkv);
+  const int q0 = qt * kBM;
+  const int S = P.S;
+  const int WL = min(S - 1, q0 + kBM - 1) / kW;
+
+  if (tid == 0) {
+    mbar_init(&bars[k2::B_Q], 1);
+    mbar_init(&bars[k2::B_RDY], 256);
+    mbar_init(&bars[k2::B_YFREE], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[k2::B_AVE + i], 1);
+      mbar_init(&bars[k2::B_CF + i], 1);
+      mbar_init(&bars[k2::B_CE + i], 128);
+    }
+    mbar_init(&bars[k2::B_DRAIN], 1);
+    fence_mbar_init();
+  }
+  for (int i = tid; i < kM * NP; i += kThreads) s_coef[i] = P.coef[i / NP][i % NP];
+  for (int p = tid; p < NP; p += kThreads) s_th[p] = theta_at(P.thetas, P.theta, p, D);
+  if (warp == 0) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t sQ = smem_u32(smem + k2::Q), sDO = smem_u32(smem + k2::DO);
+  const uint32_t sAV = smem_u32(smem + k2::AV);
+  const uint32_t sYA = smem_u32(smem + k2::YA), sYB = smem_u32(smem + k2::YB);
+  const uint32_t s_th_u = smem_u32(s_th);
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA
+    if (lane == 0) {
+      prefetch_tmap(&P.tm_q);
+      prefetch_tmap(&P.tm_do);
+      mbar_expect_tx(&bars[k2::B_Q], 2 * NS * 16384);
+      for (int s = 0; s < NS; ++s) {
+        tma_load_4d(smem + k2::Q + s * 16384, &P.tm_q, &bars[k2::B_Q], 64 * s, q0, h, b);
+        tma_load_4d(smem + k2::DO + s * 16384, &P.tm_do, &bars[k2::B_Q], 64 * s, q0, h, b);
+      }
+      mbar_wait(&bars[k2::B_Q], 0, err, kErrDrain);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ UMMA
+    if (lane == 0) {
+      const uint32_t id_c = idesc_f16(128, 112, E::kBf16, true) | (1u << 15);  // A, B MN-major
+      const uint32_t id_s = idesc_f16(128, 16, E::kBf16, true) | (1u << 15);
+      bool ok = mbar_wait(&bars[k2::B_Q], 0, err, kErrQ);
+      for (int w = 0; ok && w <= WL; ++w) {
+        const int bf = w & 1;
+        if (!(ok = mbar_wait(&bars[k2::B_RDY], w & 1, err, kErrY))) break;
+        if (w >= 2 && !(ok = mbar_wait(&bars[k2::B_CE + bf], ((w >> 1) - 1) & 1, err, kErrCEmpty)))
+          break;
+        tc_fence_after();
+        const uint32_t acc = tmem + k2::BUF * bf;
+        const uint32_t av = sAV + 32768 * bf;
+        // K = the 128 query rows, 16 per step
+#pragma unroll 1
+        for (int s = 0; s < 8; ++s)
+          mma_ss(acc + k2::C0, sdesc_mnmajor(av + 2048 * s, 16384),
+                 sdesc_mnmajor(sYA + 2048 * s, 16384), id_c, s > 0);
+#pragma unroll 1
+        for (int s = 0; s < 8; ++s)
+          mma_ss(acc + k2::C1, sdesc_mnmajor(av + 2048 * s, 16384),
+                 sdesc_mnmajor(sYB + 2048 * s, 16384), id_c, s > 0);
+#pragma unroll 1
+        for (int s = 0; s < 8; ++s) {
+          mma_ss(acc + k2::DVK, sdesc_mnmajor(sDO + 2048 * s, 16384),
+                 sdesc_mnmajor(sYA + 16384 + 2048 * s + 96, 16384), id_s, s > 0);
+          mma_ss(acc + k2::DVK + 16, sdesc_mnmajor(sQ + 2048 * s, 16384),
+                 sdesc_mnmajor(sYB + 16384 + 2048 * s + 96, 16384), id_s, s > 0);
+        }
+        mma_commit(&bars[k2::B_CF + bf]);
+        mma_commit(&bars[k2::B_AVE + bf]);
+        mma_commit(&bars[k2::B_YFREE]);
+      }
+      mma_commit(&bars[k2::B_DRAIN]);
+      mbar_wait(&bars[k2::B_DRAIN], 0, err, kErrDrain);
+    }
+  } else if (warp >= 12) {
+    // ------------------------------------------------------------ combine
+    const int gt = tid - 384;  // head dim
+    float cm[kM];
+    {
+      const int p = gt >> 1, e = gt & 1;
+#pragma unroll
+      for (int m = 0; m < kM; ++m) {
+        float sgn;
+        switch (m & 3) {
+          case 0: sgn = 1.f; break;
+          case 1: sgn = e ? 1.f : -1.f; break;
+          case 2: sgn = -1.f; break;
+          default: sgn = e ? -1.f : 1.f; break;
+        }
+        cm[m] = kLn2 * s_coef[m * NP + p] * sgn;
+      }
+    }
+    const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
+    float* dk32 = P.dk32 + ((int64_t)b * P.Hkv + hk) * S * D + gt;
+    float* dv32 = P.dv32 + ((int64_t)b * P.Hkv + hk) * S * D + gt;
+    for (int w = 0; w <= WL; ++w) {
+      const int bf = w & 1;
+      if (!wwait(bars[k2::B_CF + bf], (w >> 1) & 1, err, kErrC)) break;
+      tc_fence_after();
+      const uint32_t acc = lane_base + k2::BUF * bf;
+      float dk[16], dv[16];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t creg = acc + (hh ? k2::C1 : k2::C0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dk[8 * hh + j] = 0.f;
+#pragma unroll
+        for (int c0 = 0; c0 < kM / 2; c0 += 2) {  // terms 2c, 2c+1 for the 8 keys
+          uint32_t g[2][16];
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+            if (c0 + i < kM / 2) tmem_ld16(creg + 16 * (c0 + i), g[i]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int c = c0 + i;
+            if (c >= kM / 2) continue;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float own = __uint_as_float(g[i][j]);
+              const float partner = __shfl_xor_sync(0xffffffffu, __uint_as_float(g[i][8 + j]), 1);
+              dk[8 * hh + j] = fmaf(cm[2 * c], own, dk[8 * hh + j]);
+              dk[8 * hh + j] = fmaf(cm[2 * c + 1], partner, dk[8 * hh + j]);
+            }
+          }
+        }
+      }
+      {
+        uint32_t g[2][16];
+        tmem_ld16(acc + k2::DVK, g[0]);       // dO^T P  (16 keys)
+        tmem_ld16(acc + k2::DVK + 16, g[1]);  // Q^T dS  (16 keys)
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          dv[j] = __uint_as_float(g[0][j]);
+          dk[j] += __uint_as_float(g[1][j]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars[k2::B_CE + bf]);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int key = w * kW + j;
+        if (key < S) {
+          atomicAdd(dk32 + (int64_t)key * D, dk[j]);
+          atomicAdd(dv32 + (int64_t)key * D, dv[j]);
+        }
+      }
+    }
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ row warps
+    const int rg = warp >> 2;
+    const int r = tid & 127;
+    const uint8_t* hb0 = P.handoff + ((int64_t)blockIdx.y * P.blocks_bh + tile_block0(qt)) * kHB;
+    struct Rec {
+      float4 dl[2];
+      uint2 u[2];
+      uint4 pd[2];
+      float carry;
+    };
+    auto load = [&](int w, Rec& x) {
+      const uint8_t* hb = hb0 + (int64_t)w * kHB;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int qd = 2 * hh + rg;
+        x.dl[hh] = __ldg(reinterpret_cast<const float4*>(hb + HB_DL + (qd * 128 + r) * 16));
+        x.pd[hh] = __ldg(reinterpret_cast<const uint4*>(hb + HB_PD + (qd * 128 + r) * 16));
+        x.u[hh] = __ldg(reinterpret_cast<const uint2*>(hb + HB_U + (qd * 128 + r) * 8));
+      }
+      x.carry = __ldg(reinterpret_cast<const float*>(hb + HB_C + 4 * r));
+    };
+    bool ok = wwait(bars[k2::B_Q], 0, err, kErrQ);
+    Rec cur, nxt;
+    load(0, cur);
+    for (int w = 0; ok && w <= WL; ++w) {
+      if (w < WL) load(w + 1, nxt);
+      // ---- A rows of this group's slab into buffer w & 1
+      if (w >= 2 && !(ok = wwait(bars[k2::B_AVE + (w & 1)], ((w >> 1) - 1) & 1, err, kErrAvEmpty)))
+        break;
+      {
+        const float bse = cur.carry + kC0;
+        const uint32_t av = sAV + 32768 * (w & 1) + rg * 16384;
+#pragma unroll 1
+        for (int g = 0; g < 2; ++g) {
+          uint4 qv[4];
+          float th[16];
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int c = 4 * g + cc;
+            qv[cc] = lds128(sQ + rg * 16384 + sw128_offset(r, c));
+            const float4 t4 = lds128f(s_th_u + 16 * (8 * rg + c));
+            th[4 * cc] = t4.x; th[4 * cc + 1] = t4.y; th[4 * cc + 2] = t4.z; th[4 * cc + 3] = t4.w;
+          }
+          float rr[16], sn[16], cs[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) rr[i] = reduce_2pi(bse * th[i]);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) __sincosf(rr[i], &sn[i], &cs[i]);
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const uint32_t in[4] = {qv[cc].x, qv[cc].y, qv[cc].z, qv[cc].w};
+            uint32_t o[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float qe = E::lo(in[i]), qo = E::hi(in[i]);
+              const float s_ = sn[4 * cc + i], c_ = cs[4 * cc + i];
+              o[i] = E::pack(qe * c_ - qo * s_, qe * s_ + qo * c_);
+            }
+            sts128(av + sw128_offset(r, 4 * g + cc), make_uint4(o[0], o[1], o[2], o[3]));
+          }
+        }
+      }
+      // ---- Y | P rows and Y | dS rows (the previous window's GEMMs are done with them)
+      if (w >= 1 && !(ok = wwait(bars[k2::B_YFREE], (w - 1) & 1, err, kErrY))) break;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t yrow = hh ? sYB : sYA;
+        const float dl[4] = {cur.dl[hh].x, cur.dl[hh].y, cur.dl[hh].z, cur.dl[hh].w};
+        const float uj[4] = {u_decode(cur.u[hh].x & 0xffffu), u_decode(cur.u[hh].x >> 16),
+                             u_decode(cur.u[hh].y & 0xffffu), u_decode(cur.u[hh].y >> 16)};
+        uint32_t y[kM][2];
+#pragma unroll
+        for (int jp = 0; jp < 2; ++jp) {
+          float ta0 = 1.f, tb0 = 1.f;
+          float ta1 = uj[2 * jp], tb1 = uj[2 * jp + 1];
+          y[0][jp] = E::pack(dl[2 * jp], dl[2 * jp + 1]);
+          y[1][jp] = E::pack(dl[2 * jp] * ta1, dl[2 * jp + 1] * tb1);
+#pragma unroll
+          for (int m = 2; m < kM; ++m) {
+            const float ta2 = fmaf(2.f * uj[2 * jp], ta1, -ta0);
+            const float tb2 = fmaf(2.f * uj[2 * jp + 1], tb1, -tb0);
+            ta0 = ta1; ta1 = ta2; tb0 = tb1; tb1 = tb2;
+            y[m][jp] = E::pack(dl[2 * jp] * ta2, dl[2 * jp + 1] * tb2);
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < kM; ++m)
+          sts64(yrow + (m >> 3) * 16384 + sw128_offset(r, m & 7) + 8 * rg, y[m][0], y[m][1]);
+        // P of the half -> chunk 6 + hh of the Y | P rows; dS -> the Y | dS rows
+        sts64(sYA + 16384 + sw128_offset(r, 6 + hh) + 8 * rg, cur.pd[hh].x, cur.pd[hh].y);
+        sts64(sYB + 16384 + sw128_offset(r, 6 + hh) + 8 * rg, cur.pd[hh].z, cur.pd[hh].w);
+      }
+      fence_async_smem();
+      mbar_arrive(&bars[k2::B_RDY]);
+      cur = nxt;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
 // ------------------------------------------------------------------ host
 // K^(m) buffer layout and count; returns the dynamic shared memory needed
 template <int MODE>
@@ -996,10 +1335,10 @@ static int plan(Params& p) {
 }
 
 template <typename T, int MODE>
-static cudaError_t launch_mode(Params& p, bool bias, int B, int H, int S, cudaStream_t st) {
+static cudaError_t launch_mode(Params& p, bool bias, int S, int nbh, cudaStream_t st) {
   const int smem = plan<MODE>(p);
   if (smem > kSmemLimit) return cudaErrorInvalidValue;
-  dim3 grid((S + kBM - 1) / kBM, H, B);
+  dim3 grid((S + kBM - 1) / kBM, nbh);
   cudaError_t e;
   if (bias) {
     auto kern = bwd_kernel<T, MODE, true>;
@@ -1015,7 +1354,52 @@ static cudaError_t launch_mode(Params& p, bool bias, int B, int H, int S, cudaSt
   return cudaGetLastError();
 }
 
+template <typename T>
+static cudaError_t launch_dk2(Params& p, int S, int nbh, cudaStream_t st) {
+  const int smem = k2::TOTAL + 1024;
+  dim3 grid((S + kBM - 1) / kBM, nbh);
+  auto kern = dk2_kernel<T>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+// hand-off blocks of one (b, h): one per (query tile, window)
+static int64_t blocks_per_bh(int S) {
+  int64_t n = 0;
+  for (int qt = 0; qt * kBM < S; ++qt) n += min(S - 1, qt * kBM + kBM - 1) / kW + 1;
+  return n;
+}
+
+template <typename T>
+static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* handoff,
+                              size_t handoff_bytes, cudaStream_t st) {
+  const int64_t per_bh = blocks_per_bh(S) * kHB;
+  int chunk = handoff ? (int)std::min<int64_t>(BH, (int64_t)(handoff_bytes / per_bh)) : 0;
+  if (chunk < std::min(BH, 16)) chunk = 0;  // too few (b, h) per launch: recompute instead
+  cudaError_t e = cudaSuccess;
+  if (chunk == 0) {
+    p.handoff = nullptr;
+    p.bh0 = 0;
+    e = launch_mode<T, MODE_DQ>(p, bias, S, BH, st);
+    if (e == cudaSuccess) e = launch_mode<T, MODE_DK>(p, bias, S, BH, st);
+    return e;
+  }
+  p.handoff = handoff;
+  p.blocks_bh = blocks_per_bh(S);
+  for (int bh0 = 0; bh0 < BH && e == cudaSuccess; bh0 += chunk) {
+    p.bh0 = bh0;
+    const int nbh = std::min(chunk, BH - bh0);
+    e = launch_mode<T, MODE_DQ>(p, bias, S, nbh, st);
+    if (e == cudaSuccess) e = launch_dk2<T>(p, S, nbh, st);
+  }
+  return e;
+}
+
 }  // namespace tcb
+
+int64_t tc_bwd_handoff_bytes_per_bh(int S) { return tcb::blocks_per_bh(S) * tcb::kHB; }
 
 static bool rows16(const void* ptr, const int64_t* st) {
   return (reinterpret_cast<uintptr_t>(ptr) % 16) == 0 && (st[0] * 2) % 16 == 0 &&
@@ -1037,8 +1421,12 @@ bool tc_bwd_supported(const BwdArgs& a, int dtype) {
 }
 
 // Launches the dQ and dK kernels; the caller runs the delta/lse pre-kernel
-// before and the fp32 -> dtype conversion of dk/dv after.
-cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st) {
+// before and the fp32 -> dtype conversion of dk/dv after.  With a hand-off
+// region large enough for at least min(B H, 16) (b, h) slices the dK launch
+// reads the dQ launch's per-pair results (slice by slice through the region);
+// otherwise it recomputes them.
+cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* handoff,
+                          size_t handoff_bytes) {
   using namespace tcb;
   static Params p;
   static std::mutex mu;
@@ -1063,15 +1451,10 @@ cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st) {
   p.B = a.B; p.H = a.H; p.Hkv = a.Hkv; p.S = a.S;
   tcx::fill_coefficients(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
   const bool bias = a.bias != nullptr;
-  cudaError_t e;
-  if (dtype == COROPE_DTYPE_BF16) {
-    e = launch_mode<__nv_bfloat16, MODE_DQ>(p, bias, a.B, a.H, a.S, st);
-    if (e == cudaSuccess) e = launch_mode<__nv_bfloat16, MODE_DK>(p, bias, a.B, a.H, a.S, st);
-  } else {
-    e = launch_mode<__half, MODE_DQ>(p, bias, a.B, a.H, a.S, st);
-    if (e == cudaSuccess) e = launch_mode<__half, MODE_DK>(p, bias, a.B, a.H, a.S, st);
-  }
-  return e;
+  uint8_t* hp = static_cast<uint8_t*>(handoff);
+  if (dtype == COROPE_DTYPE_BF16)
+    return launch_all<__nv_bfloat16>(p, bias, a.B * a.H, a.S, hp, handoff_bytes, st);
+  return launch_all<__half>(p, bias, a.B * a.H, a.S, hp, handoff_bytes, st);
 }
 
 }  // namespace corope

@@ -107,8 +107,17 @@ int corope_fwd(const corope_fwd_params_t *p, corope_stream_t stream);
  * :151-174; the bias term of :72-75). */
 int corope_mqa_fwd(const corope_fwd_params_t *p, corope_stream_t stream);
 
-/* Bytes of workspace corope_bwd needs for these parameters. */
+/* Bytes of workspace corope_bwd uses at its fastest for these parameters:
+ * the minimum below plus, for the tensor-core path (head_dim 128, bf16/f16),
+ * a hand-off region of 20,992 bytes per 128 query rows x 16 keys through
+ * which the dQ kernel passes its per-(row, key) results to the dK kernel.
+ * Any size between the two works (smaller hand-off regions are used slice by
+ * slice, or not at all). */
 size_t corope_bwd_workspace_bytes(const corope_bwd_params_t *p);
+
+/* Smallest workspace corope_bwd accepts (the dK kernel then recomputes the
+ * per-(row, key) results).  No counterpart in the reference. */
+size_t corope_bwd_min_workspace_bytes(const corope_bwd_params_t *p);
 
 /* Backward: dq, dk, dv of the CoRoPE attention (gradients through the
  * softmax, the rotation, the contextual positions and the sigmoid gates).

@@ -4,6 +4,7 @@ Tolerances (bf16 inputs, fp32 accumulation): max-abs <= 2e-2 on O, <= 5e-2
 on gradients, relative L2 <= 1e-2.  fp32 inputs through the exact kernels:
 max-abs <= 1e-4 (O) and <= 1e-3 (gradients).
 """
+import ctypes
 import math
 
 import pytest
@@ -314,5 +315,41 @@ def test_tensor_backward_s2048_d128():
     torch.cuda.synchronize()
     rq, rk, rv = O.backward_dense(*[t.float() for t in cpu], sm, 1e4, row_chunk=32)
     for name, mine, r in (("dq", dq, rq), ("dk", dk, rk), ("dv", dv, rv)):
+        assert maxabs(mine, r) < G_MAXABS, name
+        assert rel_l2(mine, r) < REL_L2, name
+
+
+@pytest.mark.parametrize("mode", ["full", "chunked", "min"])
+def test_tensor_backward_workspace_paths(mode):
+    """The three ways the tensor-core backward uses its workspace give the
+    oracle's gradients: a full hand-off region (the dK kernel reads the dQ
+    kernel's per-pair results), a region for 17 of the 24 (b, h) slices
+    (two rounds of both kernels), and the minimum (the dK kernel recomputes)."""
+    from CoROPE import _lib
+    B, H, S, D = 2, 12, 300, 128
+    (q, k, v, do), cpu = inputs(B, H, S, D, 57, torch.bfloat16)
+    sm = 1 / math.sqrt(D)
+    saved, o = co_rope_forward(q, k, v, sm, algo="tensor")
+    q_, k_, v_, o_, m_, l_, a_ = saved
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def sizes():
+        p = _lib.BwdParams()
+        p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, H, S, D
+        p.dtype, p.algo = _lib._dtype_code(q), _lib.algo_code("tensor")
+        lib = _lib.load_library()
+        return (lib.corope_bwd_min_workspace_bytes(ctypes.byref(p)),
+                lib.corope_bwd_workspace_bytes(ctypes.byref(p)))
+
+    lo, hi = sizes()
+    per_bh = (hi - lo) // (B * H)
+    assert per_bh > 0 and lo + per_bh * B * H == hi
+    ws = {"full": "full", "min": "min", "chunked": lo + 17 * per_bh}[mode]
+    _lib.bwd(q_, k_, v_, o_, do, m_, l_, a_, dq, dk, dv, sm, 1e4, algo="tensor", workspace=ws)
+    torch.cuda.synchronize()
+    assert _lib.take_device_error() == 0
+    rq, rk, rv = O.backward_dense(*[t.double() for t in cpu], sm, 1e4)
+    for name, mine, r in (("dq", dq, rq), ("dk", dk, rk), ("dv", dv, rv)):
+        assert torch.isfinite(mine).all(), name
         assert maxabs(mine, r) < G_MAXABS, name
         assert rel_l2(mine, r) < REL_L2, name
