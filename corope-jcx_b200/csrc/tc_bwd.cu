@@ -1033,7 +1033,9 @@ constexpr int TH = COEF + kM * NP * 4;
 constexpr int BAR = TH + NP * 4;
 constexpr int SLOT = BAR + 16 * 8;
 constexpr int TOTAL = SLOT + 16;
-enum { B_Q = 0, B_RDY = 1, B_AVE = 2, B_YFREE = 4, B_CF = 5, B_CE = 7, B_DRAIN = 9 };
+// RDY / YFREE per half: the rows write the next window's half A while the
+// tensor core still reads half B of the current one
+enum { B_Q = 0, B_RDY = 1, B_AVE = 3, B_YFREE = 5, B_CF = 7, B_CE = 9, B_DRAIN = 11 };
 // tensor memory: buffer b at 256 b: C^T half A, C^T half B, dV^T | dK_gate^T
 constexpr uint32_t C0 = 0, C1 = 112, DVK = 224, BUF = 256;
 }  // namespace k2
@@ -1062,9 +1064,9 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
 
   if (tid == 0) {
     mbar_init(&bars[k2::B_Q], 1);
-    mbar_init(&bars[k2::B_RDY], 256);
-    mbar_init(&bars[k2::B_YFREE], 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[k2::B_RDY + i], 256);
+      mbar_init(&bars[k2::B_YFREE + i], 1);
       mbar_init(&bars[k2::B_AVE + i], 1);
       mbar_init(&bars[k2::B_CF + i], 1);
       mbar_init(&bars[k2::B_CE + i], 128);
@@ -1107,31 +1109,32 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
       bool ok = mbar_wait(&bars[k2::B_Q], 0, err, kErrQ);
       for (int w = 0; ok && w <= WL; ++w) {
         const int bf = w & 1;
-        if (!(ok = mbar_wait(&bars[k2::B_RDY], w & 1, err, kErrY))) break;
-        if (w >= 2 && !(ok = mbar_wait(&bars[k2::B_CE + bf], ((w >> 1) - 1) & 1, err, kErrCEmpty)))
-          break;
-        tc_fence_after();
         const uint32_t acc = tmem + k2::BUF * bf;
         const uint32_t av = sAV + 32768 * bf;
-        // K = the 128 query rows, 16 per step
+        // half A: C^T = v^T Y_A and dV^T = dO^T P (P of both halves rides in
+        // the Y_A rows); then half B: C^T = v^T Y_B and dK_gate^T = Q^T dS.
+        // K = the 128 query rows, 16 per step.
+        for (int hh = 0; hh < 2 && ok; ++hh) {
+          if (!(ok = mbar_wait(&bars[k2::B_RDY + hh], w & 1, err, kErrY))) break;
+          if (hh == 0 && w >= 2 &&
+              !(ok = mbar_wait(&bars[k2::B_CE + bf], ((w >> 1) - 1) & 1, err, kErrCEmpty)))
+            break;
+          tc_fence_after();
+          const uint32_t yr = hh ? sYB : sYA;
+          const uint32_t other = hh ? sQ : sDO;
 #pragma unroll 1
-        for (int s = 0; s < 8; ++s)
-          mma_ss(acc + k2::C0, sdesc_mnmajor(av + 2048 * s, 16384),
-                 sdesc_mnmajor(sYA + 2048 * s, 16384), id_c, s > 0);
-#pragma unroll 1
-        for (int s = 0; s < 8; ++s)
-          mma_ss(acc + k2::C1, sdesc_mnmajor(av + 2048 * s, 16384),
-                 sdesc_mnmajor(sYB + 2048 * s, 16384), id_c, s > 0);
-#pragma unroll 1
-        for (int s = 0; s < 8; ++s) {
-          mma_ss(acc + k2::DVK, sdesc_mnmajor(sDO + 2048 * s, 16384),
-                 sdesc_mnmajor(sYA + 16384 + 2048 * s + 96, 16384), id_s, s > 0);
-          mma_ss(acc + k2::DVK + 16, sdesc_mnmajor(sQ + 2048 * s, 16384),
-                 sdesc_mnmajor(sYB + 16384 + 2048 * s + 96, 16384), id_s, s > 0);
+          for (int s = 0; s < 8; ++s) {
+            mma_ss(acc + (hh ? k2::C1 : k2::C0), sdesc_mnmajor(av + 2048 * s, 16384),
+                   sdesc_mnmajor(yr + 2048 * s, 16384), id_c, s > 0);
+            mma_ss(acc + k2::DVK + 16 * hh, sdesc_mnmajor(other + 2048 * s, 16384),
+                   sdesc_mnmajor(yr + 16384 + 2048 * s + 96, 16384), id_s, s > 0);
+          }
+          if (hh == 1) {
+            mma_commit(&bars[k2::B_CF + bf]);
+            mma_commit(&bars[k2::B_AVE + bf]);
+          }
+          mma_commit(&bars[k2::B_YFREE + hh]);
         }
-        mma_commit(&bars[k2::B_CF + bf]);
-        mma_commit(&bars[k2::B_AVE + bf]);
-        mma_commit(&bars[k2::B_YFREE]);
       }
       mma_commit(&bars[k2::B_DRAIN]);
       mbar_wait(&bars[k2::B_DRAIN], 0, err, kErrDrain);
@@ -1274,10 +1277,11 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
           }
         }
       }
-      // ---- Y | P rows and Y | dS rows (the previous window's GEMMs are done with them)
-      if (w >= 1 && !(ok = wwait(bars[k2::B_YFREE], (w - 1) & 1, err, kErrY))) break;
+      // ---- Y | P rows, then Y | dS rows, each once the previous window's
+      // GEMMs of that half are done with them
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
+        if (w >= 1 && !(ok = wwait(bars[k2::B_YFREE + hh], (w - 1) & 1, err, kErrY))) break;
         const uint32_t yrow = hh ? sYB : sYA;
         const float dl[4] = {cur.dl[hh].x, cur.dl[hh].y, cur.dl[hh].z, cur.dl[hh].w};
         const float uj[4] = {u_decode(cur.u[hh].x & 0xffffu), u_decode(cur.u[hh].x >> 16),
@@ -1300,12 +1304,18 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
 #pragma unroll
         for (int m = 0; m < kM; ++m)
           sts64(yrow + (m >> 3) * 16384 + sw128_offset(r, m & 7) + 8 * rg, y[m][0], y[m][1]);
-        // P of the half -> chunk 6 + hh of the Y | P rows; dS -> the Y | dS rows
-        sts64(sYA + 16384 + sw128_offset(r, 6 + hh) + 8 * rg, cur.pd[hh].x, cur.pd[hh].y);
-        sts64(sYB + 16384 + sw128_offset(r, 6 + hh) + 8 * rg, cur.pd[hh].z, cur.pd[hh].w);
+        // P of both halves -> chunks 6, 7 of the Y | P rows; dS -> the Y | dS rows
+#pragma unroll
+        for (int q2 = 0; q2 < 2; ++q2) {
+          if (hh == 0)
+            sts64(sYA + 16384 + sw128_offset(r, 6 + q2) + 8 * rg, cur.pd[q2].x, cur.pd[q2].y);
+          else
+            sts64(sYB + 16384 + sw128_offset(r, 6 + q2) + 8 * rg, cur.pd[q2].z, cur.pd[q2].w);
+        }
+        fence_async_smem();
+        mbar_arrive(&bars[k2::B_RDY + hh]);
       }
-      fence_async_smem();
-      mbar_arrive(&bars[k2::B_RDY]);
+      if (!ok) break;
       cur = nxt;
     }
   }

@@ -18,14 +18,21 @@
 // operands; coefficients below 2e-6 are pruned, which shortens the K extent
 // of the high-m terms.
 //
-// Roles per CTA (128 query rows of one (b, h), 384 threads):
-//   warps 0-3  row warps: gates, carries, A operand, Chebyshev (Clenshaw)
-//              combine, online softmax (stale-max rescaling), P, epilogue
-//   warp 4     TMA: Q once, K/V tiles of 64 keys (2 stages)
-//   warp 5     UMMA issue of the G GEMM (A operand from tensor memory)
-//   warp 6     UMMA issue of the gate GEMM Q K^T and of P V
-//   warps 8-11 build the K^(m) operand of each window in shared memory
+// Roles per CTA (128 query rows of one (b, h), 512 threads):
+//   warps 0-7  two row warpgroups sharing every row (group g: keys 4g..4g+3
+//              of each 8-key half, rotation pairs g*D/4 .. and output
+//              columns g*D/2 ..): gates, carries, A operand, Chebyshev
+//              (Clenshaw) combine, online softmax (stale-max rescaling; the
+//              groups agree on each window's row max through shared memory),
+//              P, epilogue (row sums combined at the end)
+//   warp 8     TMA: Q once, K/V tiles of 64 keys (2 stages)
+//   warp 9     UMMA issue of the G GEMM (A operand from tensor memory)
+//   warp 10    UMMA issue of the gate GEMM Q K^T and of P V
+//   warps 12-15 build the K^(m) operand of each window in shared memory
 //              (double-buffered when it fits)
+// Registers are re-balanced with setmaxnreg (rows 176, builders 104, the
+// TMA/UMMA warpgroup 56), then a CTA barrier so that no warp returns
+// registers to the pool before every warp holds its share.
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -56,7 +63,9 @@ using tcx::kW;
 using tcx::kM;
 constexpr int kBM = 128;     // query rows per CTA
 constexpr int kKT = 64;      // keys per K/V tile
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
+constexpr int kRowRegs = 176, kBldRegs = 104, kCtlRegs = 56;
+static_assert(2 * kRowRegs + kBldRegs + kCtlRegs == 4 * 128, "register split");
 using tcx::kC0;
 using tcx::kLog2e;
 constexpr float kRescale = 8.0f;  // stale-max headroom (log2 units)
@@ -64,7 +73,7 @@ constexpr float kRescale = 8.0f;  // stale-max headroom (log2 units)
 // error codes recorded by bounded waits
 enum : int {
   kErrQ = 101, kErrKvEmpty, kErrKvFull, kErrSg, kErrG, kErrGEmpty, kErrB, kErrBEmpty, kErrAv,
-  kErrP, kErrO, kErrDrain
+  kErrP, kErrO, kErrDrain, kErrX
 };
 
 struct Params {
@@ -95,9 +104,11 @@ struct Layout {
   static constexpr int BAR = TH + (D / 2) * 4;
   static constexpr int NBAR = 32;
   static constexpr int SLOT = BAR + NBAR * 8;
+  // row-group exchange: [2 groups][128 rows] row max, then [2][128] row sums
+  static constexpr int XCH = (SLOT + 16 + 15) & ~15;
   // builder work items: [kMaxItems][128 threads] x (uint2)
   static constexpr int MAX_ITEMS = (2 * 8 * 8 * kM + 127) / 128;
-  static constexpr int ITEMS = (SLOT + 16 + 15) & ~15;
+  static constexpr int ITEMS = XCH + 4 * 128 * 4;
   // K^(m) buffers [2 halves][nb][b_buf_bytes] follow, 1024-aligned
   static constexpr int BOP = (ITEMS + MAX_ITEMS * 128 * 8 + 1023) & ~1023;
   // tensor-memory columns
@@ -119,7 +130,8 @@ enum {
   B_Q = 0, B_KVF = 1, B_KVE = 3, B_SG = 5, B_GF = 7, B_GE = 9,
   B_BF = 11,  // [half][buffer] -> B_BF + 2 * half + buffer
   B_BE = 15,  // [half][buffer]
-  B_AV = 19, B_P = 20, B_O = 21, B_DRAIN = 22, B_DRAIN2 = 23
+  B_AV = 19, B_P = 20, B_O = 21, B_DRAIN = 22, B_DRAIN2 = 23,
+  B_XM = 24, B_XL = 25  // row-group exchanges: window row max, final row sums
 };
 
 using tcx::ElemTraits;
@@ -159,14 +171,16 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       mbar_init(&bars[B_KVE + i], 1 + 128);
       mbar_init(&bars[B_SG + i], 1);
       mbar_init(&bars[B_GF + i], 1);
-      mbar_init(&bars[B_GE + i], 128);
+      mbar_init(&bars[B_GE + i], 256);
     }
     for (int i = 0; i < 4; ++i) {
       mbar_init(&bars[B_BF + i], 128);
       mbar_init(&bars[B_BE + i], 1);
     }
-    mbar_init(&bars[B_AV], 128);
-    mbar_init(&bars[B_P], 128);
+    mbar_init(&bars[B_AV], 256);
+    mbar_init(&bars[B_P], 256);
+    mbar_init(&bars[B_XM], 256);
+    mbar_init(&bars[B_XL], 256);
     mbar_init(&bars[B_O], 1);
     mbar_init(&bars[B_DRAIN], 1);
     mbar_init(&bars[B_DRAIN2], 1);
@@ -190,99 +204,107 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
   const uint32_t s_coef_u = smem_u32(s_coef);
   const int nb = P.nb;
 
-  if (warp == 4) {
-    // ------------------------------------------------------------ TMA
-    if (lane == 0) {
-      prefetch_tmap(&P.tm_q);
-      prefetch_tmap(&P.tm_k);
-      prefetch_tmap(&P.tm_v);
-      mbar_expect_tx(&bars[B_Q], NS * 16384);
-      for (int s = 0; s < NS; ++s)
-        tma_load_4d(smem + L::Q + s * 16384, &P.tm_q, &bars[B_Q], 64 * s, q0, h, b);
-      int last_use[2] = {-1, -1};
-      for (int n = 0; T0 - n >= 0; ++n) {
-        const int tile = T0 - n, st = n & 1, u = n >> 1;
-        if (n >= 2 && !mbar_wait(&bars[B_KVE + st], (u - 1) & 1, err, kErrKvEmpty)) break;
-        mbar_expect_tx(&bars[B_KVF + st], 2 * NS * 8192);
-        for (int s = 0; s < NS; ++s) {
-          tma_load_4d(smem + L::K + (st * NS + s) * 8192, &P.tm_k, &bars[B_KVF + st], 64 * s,
-                      kKT * tile, hk, b);
-          tma_load_4d(smem + L::V + (st * NS + s) * 8192, &P.tm_v, &bars[B_KVF + st], 64 * s,
-                      kKT * tile, hk, b);
-        }
-        last_use[st] = u;
-      }
-      // no copy may still be in flight when the CTA exits
-      for (int st = 0; st < 2; ++st)
-        if (last_use[st] >= 0) mbar_wait(&bars[B_KVF + st], last_use[st] & 1, err, kErrDrain);
-    }
-  } else if (warp == 5) {
-    // ------------------------------------------------------ UMMA: G GEMM
-    if (lane == 0) {
-      bool ok = true;
-      for (int w = W0; ok && w >= 0; --w) {
-        const int k = W0 - w, buf = k % nb, use = k / nb;
-        if (!(ok = mbar_wait(&bars[B_AV], k & 1, err, kErrAv))) break;
-        for (int hh = 0; hh < 2 && ok; ++hh) {
-          ok = mbar_wait(&bars[B_BF + 2 * hh + buf], use & 1, err, kErrB);
-          if (ok && k > 0) ok = mbar_wait(&bars[B_GE + hh], (k - 1) & 1, err, kErrGEmpty);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t dst = tmem + (hh ? L::T_G1 : L::T_G0);
-          const uint32_t bb = sB + (hh * nb + buf) * P.b_buf_bytes;
-#pragma unroll
-          for (int s = 0; s < KSTEPS; ++s) {
-            const int nr = P.nrow[s];
-            if (nr == 0) break;
-            mma_ts(dst, tmem + ((w & 1) ? L::T_AV1 : L::T_AV0) + 8 * s,
-                   sdesc_kmajor(bb + P.b_slab_off[s >> 2] + 32 * (s & 3)),
-                   idesc_f16(128, nr, E::kBf16, false), s > 0);
+  if (warp >= 8 && warp < 12) {
+    regs_dec<kCtlRegs>();
+    named_bar(1, kThreads);
+    if (warp == 8) {
+      // ------------------------------------------------------------ TMA
+      if (lane == 0) {
+        prefetch_tmap(&P.tm_q);
+        prefetch_tmap(&P.tm_k);
+        prefetch_tmap(&P.tm_v);
+        mbar_expect_tx(&bars[B_Q], NS * 16384);
+        for (int s = 0; s < NS; ++s)
+          tma_load_4d(smem + L::Q + s * 16384, &P.tm_q, &bars[B_Q], 64 * s, q0, h, b);
+        int last_use[2] = {-1, -1};
+        for (int n = 0; T0 - n >= 0; ++n) {
+          const int tile = T0 - n, st = n & 1, u = n >> 1;
+          if (n >= 2 && !mbar_wait(&bars[B_KVE + st], (u - 1) & 1, err, kErrKvEmpty)) break;
+          mbar_expect_tx(&bars[B_KVF + st], 2 * NS * 8192);
+          for (int s = 0; s < NS; ++s) {
+            tma_load_4d(smem + L::K + (st * NS + s) * 8192, &P.tm_k, &bars[B_KVF + st], 64 * s,
+                        kKT * tile, hk, b);
+            tma_load_4d(smem + L::V + (st * NS + s) * 8192, &P.tm_v, &bars[B_KVF + st], 64 * s,
+                        kKT * tile, hk, b);
           }
-          mma_commit(&bars[B_GF + hh]);
-          mma_commit(&bars[B_BE + 2 * hh + buf]);
+          last_use[st] = u;
         }
+        // no copy may still be in flight when the CTA exits
+        for (int st = 0; st < 2; ++st)
+          if (last_use[st] >= 0) mbar_wait(&bars[B_KVF + st], last_use[st] & 1, err, kErrDrain);
       }
-      mma_commit(&bars[B_DRAIN]);
-      mbar_wait(&bars[B_DRAIN], 0, err, kErrDrain);
-    }
-  } else if (warp == 6) {
-    // ------------------------------------------- UMMA: gate GEMM and P V
-    if (lane == 0) {
-      const uint32_t id_gate = idesc_f16(128, 16, E::kBf16, false);
-      const uint32_t id_pv = idesc_f16(128, D, E::kBf16, true);
-      bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
-      tc_fence_after();
-      auto gate = [&](int w) -> bool {
-        const int n = T0 - w / 4, st = n & 1;
-        if (!mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) return false;
-        tc_fence_after();
-        const uint32_t kt = sK + st * NS * 8192 + (w & 3) * kW * 128;
-        const uint32_t dst = tmem + ((w & 1) ? L::T_SG1 : L::T_SG0);
-#pragma unroll
-        for (int s = 0; s < KSTEPS; ++s)
-          mma_ss(dst, sdesc_kmajor(sQ + (s >> 2) * 16384 + 32 * (s & 3)),
-                 sdesc_kmajor(kt + (s >> 2) * 8192 + 32 * (s & 3)), id_gate, s > 0);
-        mma_commit(&bars[B_SG + (w & 1)]);
-        return true;
-      };
-      if (ok) ok = gate(W0);
-      if (ok && W0 >= 1) ok = gate(W0 - 1);
-      for (int w = W0; ok && w >= 0; --w) {
-        if (!(ok = mbar_wait(&bars[B_P], (W0 - w) & 1, err, kErrP))) break;
-        tc_fence_after();
-        const int n = T0 - w / 4, st = n & 1;
-        const uint32_t vt = sV + st * NS * 8192 + (w & 3) * kW * 128;
-        const uint32_t pa = tmem + ((w & 1) ? L::T_SG1 : L::T_SG0);
-        mma_ts(tmem + L::T_O, pa, sdesc_mnmajor(vt, 8192), id_pv, w != W0);
-        mma_commit(&bars[B_O]);
-        if ((w & 3) == 0) mma_commit(&bars[B_KVE + st]);
-        // P(w) has been consumed (in issue order) -> its buffer takes gate(w-2)
-        if (w >= 2) ok = gate(w - 2);
+    } else if (warp == 9) {
+      // ------------------------------------------------------ UMMA: G GEMM
+      if (lane == 0) {
+        bool ok = true;
+        for (int w = W0; ok && w >= 0; --w) {
+          const int k = W0 - w, buf = k % nb, use = k / nb;
+          if (!(ok = mbar_wait(&bars[B_AV], k & 1, err, kErrAv))) break;
+          for (int hh = 0; hh < 2 && ok; ++hh) {
+            ok = mbar_wait(&bars[B_BF + 2 * hh + buf], use & 1, err, kErrB);
+            if (ok && k > 0) ok = mbar_wait(&bars[B_GE + hh], (k - 1) & 1, err, kErrGEmpty);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t dst = tmem + (hh ? L::T_G1 : L::T_G0);
+            const uint32_t bb = sB + (hh * nb + buf) * P.b_buf_bytes;
+  #pragma unroll
+            for (int s = 0; s < KSTEPS; ++s) {
+              const int nr = P.nrow[s];
+              if (nr == 0) break;
+              mma_ts(dst, tmem + ((w & 1) ? L::T_AV1 : L::T_AV0) + 8 * s,
+                     sdesc_kmajor(bb + P.b_slab_off[s >> 2] + 32 * (s & 3)),
+                     idesc_f16(128, nr, E::kBf16, false), s > 0);
+            }
+            mma_commit(&bars[B_GF + hh]);
+            mma_commit(&bars[B_BE + 2 * hh + buf]);
+          }
+        }
+        mma_commit(&bars[B_DRAIN]);
+        mbar_wait(&bars[B_DRAIN], 0, err, kErrDrain);
       }
-      mma_commit(&bars[B_DRAIN2]);
-      mbar_wait(&bars[B_DRAIN2], 0, err, kErrDrain);
+    } else if (warp == 10) {
+      // ------------------------------------------- UMMA: gate GEMM and P V
+      if (lane == 0) {
+        const uint32_t id_gate = idesc_f16(128, 16, E::kBf16, false);
+        const uint32_t id_pv = idesc_f16(128, D, E::kBf16, true);
+        bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
+        tc_fence_after();
+        auto gate = [&](int w) -> bool {
+          const int n = T0 - w / 4, st = n & 1;
+          if (!mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) return false;
+          tc_fence_after();
+          const uint32_t kt = sK + st * NS * 8192 + (w & 3) * kW * 128;
+          const uint32_t dst = tmem + ((w & 1) ? L::T_SG1 : L::T_SG0);
+  #pragma unroll
+          for (int s = 0; s < KSTEPS; ++s)
+            mma_ss(dst, sdesc_kmajor(sQ + (s >> 2) * 16384 + 32 * (s & 3)),
+                   sdesc_kmajor(kt + (s >> 2) * 8192 + 32 * (s & 3)), id_gate, s > 0);
+          mma_commit(&bars[B_SG + (w & 1)]);
+          return true;
+        };
+        if (ok) ok = gate(W0);
+        if (ok && W0 >= 1) ok = gate(W0 - 1);
+        for (int w = W0; ok && w >= 0; --w) {
+          if (!(ok = mbar_wait(&bars[B_P], (W0 - w) & 1, err, kErrP))) break;
+          tc_fence_after();
+          const int n = T0 - w / 4, st = n & 1;
+          const uint32_t vt = sV + st * NS * 8192 + (w & 3) * kW * 128;
+          const uint32_t pa = tmem + ((w & 1) ? L::T_SG1 : L::T_SG0);
+          mma_ts(tmem + L::T_O, pa, sdesc_mnmajor(vt, 8192), id_pv, w != W0);
+          mma_commit(&bars[B_O]);
+          if ((w & 3) == 0) mma_commit(&bars[B_KVE + st]);
+          // P(w) has been consumed (in issue order) -> its buffer takes gate(w-2)
+          if (w >= 2) ok = gate(w - 2);
+        }
+        mma_commit(&bars[B_DRAIN2]);
+        mbar_wait(&bars[B_DRAIN2], 0, err, kErrDrain);
+      }
     }
-  } else if (warp >= 8) {
+    __syncwarp();
+    regs_inc<128>();
+  } else if (warp >= 12) {
+    regs_dec<kBldRegs>();
+    named_bar(1, kThreads);
     // ------------------------------------------------- K^(m) operand builder
     // Work items are the (K-step s, row, 16-byte chunk) triples the G GEMM
     // reads: rows [0, nrow[s]) x 2 chunks of K-step s, numbered s-major and
@@ -291,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
     // (without the window/half row offset), the coefficient quad, the
     // destination chunk, and the (-i)^m swap/sign flags.
     constexpr int kMaxItems = L::MAX_ITEMS;
-    const int gt = tid - 256;
+    const int gt = tid - 384;
     uint2* items = reinterpret_cast<uint2*>(smem + L::ITEMS);
     int my_n = 0;
     {
@@ -326,12 +348,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
     for (int w = W0; w >= 0; --w) {
       const int k = W0 - w, buf = k % nb, use = k / nb;
       const int n = T0 - w / 4, st = n & 1;
-      if (!mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) break;
+      if (!wwait(bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) break;
       bool ok = true;
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
         if (use > 0 &&
-            !(ok = mbar_wait(&bars[B_BE + 2 * hh + buf], (use - 1) & 1, err, kErrBEmpty)))
+            !(ok = wwait(bars[B_BE + 2 * hh + buf], (use - 1) & 1, err, kErrBEmpty)))
           break;
         const uint32_t kt = sK + st * NS * 8192 + (2 * (w & 3) + hh) * 1024;
         const uint32_t bt = sB + (hh * nb + buf) * P.b_buf_bytes;
@@ -372,29 +394,37 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       if (!ok) break;
       if ((w & 3) == 0) mbar_arrive(&bars[B_KVE + st]);
     }
-  } else if (warp < 4) {
+    __syncwarp();
+    regs_inc<128>();
+  } else {
     // ------------------------------------------------------------ row warps
-    const int r = tid;
+    regs_inc<kRowRegs>();
+    named_bar(1, kThreads);
+    const int rg = warp >> 2;  // row group
+    const int r = tid & 127;
     const int t = q0 + r;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-    const uint8_t* qrow = smem + L::Q;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t s_xch = smem_u32(smem + L::XCH);
     float carry = 0.f;                     // gate sum of keys after the window
-    float m_used = -1e30f, m_true = -INFINITY, lsum = 0.f;
-    bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
+    float m_used = -1e30f, m_true = -INFINITY;
+    float lsum = 0.f;                      // this group's keys
+    bool ok = wwait(bars[B_Q], 0, err, kErrQ);
 
-    // A operand of one window: v = R((carry + c0) theta) q_t in tensor memory
-    // (angles reduced to [-pi, pi] on the FMA pipe, sine/cosine on MUFU).
+    // This group's half of the A operand of one window, v = R((carry + c0)
+    // theta) q_t, into tensor memory (angles reduced to [-pi, pi] on the FMA
+    // pipe, sine/cosine on MUFU).
     auto build_a = [&](float cw, uint32_t av_col) {
       const float base = cw + kC0;
 #pragma unroll 1
-      for (int g = 0; g < NP / 16; ++g) {
+      for (int g = 0; g < NP / 32; ++g) {
         // 16 independent pairs, advanced stage by stage (instruction-level
         // parallelism across pairs instead of one long chain per pair)
+        const int p0 = rg * (NP / 2) + 16 * g;
         uint4 qv[4];
         float th[16];
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
-          const int c = g * 4 + cc;  // 16-byte chunk of the row (4 pairs)
+          const int c = p0 / 4 + cc;  // 16-byte chunk of the row (4 pairs)
           qv[cc] = lds128(sQ + (c >> 3) * 16384 + sw128_offset(r, c & 7));
           const float4 t4 = lds128f(s_th_u + 16 * c);
           th[4 * cc] = t4.x; th[4 * cc + 1] = t4.y; th[4 * cc + 2] = t4.z; th[4 * cc + 3] = t4.w;
@@ -412,26 +442,29 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
           const float qe = E::lo(w32), qo = E::hi(w32);
           regs[i] = E::pack(qe * cs[i] - qo * sn[i], qe * sn[i] + qo * cs[i]);
         }
-        tmem_st16(lane_base + av_col + 16 * g, regs);
+        tmem_st16(lane_base + av_col + p0, regs);
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars[B_AV]);
     };
 
-    // Clenshaw combine of 8 keys from one G half: f_j = sum_m T_m(u_j) G_m.
-    // Columns m*8 + j; one 16-column load brings terms 2c and 2c+1.
-    auto combine = [&](uint32_t gcol, const float* uj, float* f, int ge_bar) {
-      constexpr int NC = kM / 2;  // 16-column loads
-      float b1[8], b2[8];
+    // Clenshaw combine of this group's 4 keys of one G half:
+    // f_j = sum_m T_m(u_j) G_m, G columns 16 c + 8 (m & 1) + key (m = 2c + (m & 1)).
+    auto combine = [&](uint32_t gcol, const float (&uj)[4], float (&f)[4], int ge_bar) {
+      constexpr int NC = kM / 2;
+      float b1[4], b2[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) { b1[j] = 0.f; b2[j] = 0.f; }
+      for (int j = 0; j < 4; ++j) { b1[j] = 0.f; b2[j] = 0.f; }
 #pragma unroll
       for (int c0 = NC - 1; c0 >= 0; c0 -= 2) {
-        uint32_t g[2][16];
+        uint32_t g[2][2][4];
 #pragma unroll
         for (int i = 0; i < 2; ++i)
-          if (c0 - i >= 0) tmem_ld16(lane_base + gcol + 16 * (c0 - i), g[i]);
+          if (c0 - i >= 0) {
+            tmem_ld4(lane_base + gcol + 16 * (c0 - i) + 4 * rg, g[i][0]);
+            tmem_ld4(lane_base + gcol + 16 * (c0 - i) + 8 + 4 * rg, g[i][1]);
+          }
         tmem_wait_ld();
         if (c0 <= 1) {
           tc_fence_before();
@@ -445,8 +478,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
           for (int mm = 1; mm >= 0; --mm) {
             const int m = 2 * c + mm;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float a = __uint_as_float(g[i][mm * 8 + j]);
+            for (int j = 0; j < 4; ++j) {
+              const float a = __uint_as_float(g[i][mm][j]);
               if (m > 0) {
                 const float bn = fmaf(2.0f * uj[j], b1[j], a - b2[j]);
                 b2[j] = b1[j];
@@ -469,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       const int j0 = w * kW;
       const uint32_t sg = (w & 1) ? L::T_SG1 : L::T_SG0;
       // gates of the window
-      if (!(ok = mbar_wait(&bars[B_SG + (w & 1)], ((W0 - w) >> 1) & 1, err, kErrSg))) break;
+      if (!(ok = wwait(bars[B_SG + (w & 1)], ((W0 - w) >> 1) & 1, err, kErrSg))) break;
       tc_fence_after();
       uint32_t sraw[16];
       tmem_ld16(lane_base + sg, sraw);
@@ -482,39 +515,52 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         uu[jj] = fmaf(acc, 1.0f / kC0, -1.0f);
         acc += z;
       }
+      // this group's keys: i -> key 8 (i >> 2) + 4 rg + (i & 3)
+      float uo[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int kk = 8 * (i >> 2) + (i & 3);
+        uo[i] = rg ? uu[kk + 4] : uu[kk];
+      }
       const float carry_next = carry + acc;
       // A operand of the next window (its buffer was last read by G(w+1),
       // which completed before this row group loaded G(w+1))
       if (w > 0) build_a(carry_next, ((w - 1) & 1) ? L::T_AV1 : L::T_AV0);
-      float lg[16];
+      float lg[8];
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
-        if (!(ok = mbar_wait(&bars[B_GF + hh], k & 1, err, kErrG))) break;
+        if (!(ok = wwait(bars[B_GF + hh], k & 1, err, kErrG))) break;
         tc_fence_after();
-        float uj[8], f[8];
+        float uj[4], f[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) uj[j] = hh ? uu[8 + j] : uu[j];
+        for (int j = 0; j < 4; ++j) uj[j] = hh ? uo[4 + j] : uo[j];
         combine(hh ? L::T_G1 : L::T_G0, uj, f, B_GE + hh);
         if (hh == 0) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) lg[j] = f[j];
+          for (int j = 0; j < 4; ++j) lg[j] = f[j];
         } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) lg[8 + j] = f[j];
+          for (int j = 0; j < 4; ++j) lg[4 + j] = f[j];
         }
       }
       if (!ok) break;
-      // online softmax (log2 units) with stale-max rescaling
+      // online softmax (log2 units) with stale-max rescaling; the row max
+      // of the window is agreed between the two groups
       float mx = -INFINITY;
 #pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {
-        if (HAS_BIAS && j0 + jj <= t) lg[jj] = fmaf(P.bias[(int64_t)t * P.bias_rs + j0 + jj], kLog2e, lg[jj]);
-        lg[jj] = (j0 + jj <= t) ? lg[jj] : -INFINITY;
-        mx = fmaxf(mx, lg[jj]);
+      for (int i = 0; i < 8; ++i) {
+        const int kj = j0 + 8 * (i >> 2) + 4 * rg + (i & 3);
+        if (HAS_BIAS && kj <= t) lg[i] = fmaf(P.bias[(int64_t)t * P.bias_rs + kj], kLog2e, lg[i]);
+        lg[i] = (kj <= t) ? lg[i] : -INFINITY;
+        mx = fmaxf(mx, lg[i]);
       }
+      sts32f(s_xch + (rg * 128 + r) * 4, mx);
+      mbar_arrive(&bars[B_XM]);
+      if (!(ok = wwait(bars[B_XM], k & 1, err, kErrX))) break;
+      mx = fmaxf(mx, lds32f(s_xch + ((rg ^ 1) * 128 + r) * 4));
       m_true = fmaxf(m_true, mx);
       if (k > 0) {
-        if (!(ok = mbar_wait(&bars[B_O], (k - 1) & 1, err, kErrO))) break;
+        if (!(ok = wwait(bars[B_O], (k - 1) & 1, err, kErrO))) break;
         tc_fence_after();
       }
       const bool resc = mx > m_used + kRescale;
@@ -523,38 +569,46 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       lsum *= alpha;
       if (k > 0 && __any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-        for (int c = 0; c < D / 16; ++c) {
+        for (int c = 0; c < D / 32; ++c) {  // this group's half of the O columns
+          const uint32_t oc = lane_base + L::T_O + rg * (D / 2) + 16 * c;
           uint32_t o[16];
-          tmem_ld16(lane_base + L::T_O + 16 * c, o);
+          tmem_ld16(oc, o);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st16(lane_base + L::T_O + 16 * c, o);
+          tmem_st16(oc, o);
         }
       }
-      uint32_t pk[8];
+      uint32_t pk[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < 4; ++i) {
         const float p0 = exp2f(lg[2 * i] - m_used), p1 = exp2f(lg[2 * i + 1] - m_used);
         lsum += p0 + p1;
         pk[i] = E::pack(p0, p1);
       }
-      tmem_st8(lane_base + sg, pk);
+      // P over the gate columns (keys 2i, 2i+1 in word i)
+      tmem_st2(lane_base + sg + 2 * rg, pk[0], pk[1]);
+      tmem_st2(lane_base + sg + 4 + 2 * rg, pk[2], pk[3]);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars[B_P]);
       carry = carry_next;
     }
-    // epilogue
-    if (ok) ok = mbar_wait(&bars[B_O], W0 & 1, err, kErrO);
+    // epilogue: row sum of both groups, then this group's output columns
+    if (ok) ok = wwait(bars[B_O], W0 & 1, err, kErrO);
+    sts32f(s_xch + (256 + rg * 128 + r) * 4, lsum);
+    mbar_arrive(&bars[B_XL]);
+    if (ok) ok = wwait(bars[B_XL], 0, err, kErrX);
     if (ok) {
       tc_fence_after();
-      const float inv = 1.0f / lsum;
-      T* orow = reinterpret_cast<T*>(P.o) + b * P.os[0] + h * P.os[1] + (int64_t)t * P.os[2];
+      const float ltot = lsum + lds32f(s_xch + (256 + (rg ^ 1) * 128 + r) * 4);
+      const float inv = 1.0f / ltot;
+      T* orow = reinterpret_cast<T*>(P.o) + b * P.os[0] + h * P.os[1] + (int64_t)t * P.os[2] +
+                rg * (D / 2);
 #pragma unroll 1
-      for (int c = 0; c < D / 16; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         uint32_t o[16];
-        tmem_ld16(lane_base + L::T_O + 16 * c, o);
+        tmem_ld16(lane_base + L::T_O + rg * (D / 2) + 16 * c, o);
         tmem_wait_ld();
         uint32_t pk[8];
 #pragma unroll
@@ -566,16 +620,18 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
           dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
       }
-      if (t < S) {
+      if (t < S && rg == 0) {
         const int64_t ri = ((int64_t)b * P.H + h) * S + t;
         const float M = m_true * 0.6931471805599453f;
-        const float Lv = lsum * exp2f(m_used - m_true);
+        const float Lv = ltot * exp2f(m_used - m_true);
         if (P.m) P.m[ri] = M;
         if (P.l) P.l[ri] = Lv;
         if (P.a) P.a[ri] = carry;
         if (P.lse) P.lse[ri] = M + logf(Lv);
       }
     }
+    __syncwarp();
+    regs_dec<128>();
   }
 
   tc_fence_before();
