@@ -763,41 +763,35 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 
     // Clenshaw for this group's 4 keys of a half: logits (log2 units) and
     // their derivative in u.  G columns: 16 c + 8 (m & 1) + key, m = 2 c + (m & 1).
+    // All 14 loads are issued before the single wait, after which the G
+    // region is released to the next half's GEMM.
     auto clenshaw = [&](const float (&uj)[4], float (&f)[4], float (&fd)[4]) {
+      uint32_t g[kM / 2][2][4];
+#pragma unroll
+      for (int c = 0; c < kM / 2; ++c) {
+        tmem_ld4(lane_base + T_G + 16 * c + 4 * rg, g[c][0]);
+        tmem_ld4(lane_base + T_G + 16 * c + 8 + 4 * rg, g[c][1]);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bars[B_GE]);
       float b1[4], b2[4], d1[4], d2[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) { b1[j] = b2[j] = d1[j] = d2[j] = 0.f; }
 #pragma unroll
-      for (int c0 = kM / 2 - 1; c0 >= 0; c0 -= 2) {
-        uint32_t g[2][2][4];
+      for (int m = kM - 1; m >= 0; --m) {
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
-          if (c0 - i >= 0) {
-            tmem_ld4(lane_base + T_G + 16 * (c0 - i) + 4 * rg, g[i][0]);
-            tmem_ld4(lane_base + T_G + 16 * (c0 - i) + 8 + 4 * rg, g[i][1]);
-          }
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int c = c0 - i;
-          if (c < 0) continue;
-#pragma unroll
-          for (int mm = 1; mm >= 0; --mm) {
-            const int m = 2 * c + mm;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float a = __uint_as_float(g[i][mm][j]);
-              const float u2 = 2.0f * uj[j];
-              if (m > 0) {
-                const float dn = fmaf(u2, d1[j], fmaf(2.0f, b1[j], -d2[j]));
-                const float bn = fmaf(u2, b1[j], a - b2[j]);
-                d2[j] = d1[j]; d1[j] = dn;
-                b2[j] = b1[j]; b1[j] = bn;
-              } else {
-                f[j] = fmaf(uj[j], b1[j], a - b2[j]);
-                fd[j] = fmaf(uj[j], d1[j], b1[j] - d2[j]);
-              }
-            }
+        for (int j = 0; j < 4; ++j) {
+          const float a = __uint_as_float(g[m >> 1][m & 1][j]);
+          const float u2 = 2.0f * uj[j];
+          if (m > 0) {
+            const float dn = fmaf(u2, d1[j], fmaf(2.0f, b1[j], -d2[j]));
+            const float bn = fmaf(u2, b1[j], a - b2[j]);
+            d2[j] = d1[j]; d1[j] = dn;
+            b2[j] = b1[j]; b1[j] = bn;
+          } else {
+            f[j] = fmaf(uj[j], b1[j], a - b2[j]);
+            fd[j] = fmaf(uj[j], d1[j], b1[j] - d2[j]);
           }
         }
       }
@@ -842,8 +836,6 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         }
         float f[4], fd[4];
         clenshaw(uj, f, fd);
-        tc_fence_before();
-        mbar_arrive(&bars[B_GE]);
         float dl[4], da[4], pr[4];
         float sum4 = 0.f;
 #pragma unroll

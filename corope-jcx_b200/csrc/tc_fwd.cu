@@ -451,43 +451,31 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
 
     // Clenshaw combine of this group's 4 keys of one G half:
     // f_j = sum_m T_m(u_j) G_m, G columns 16 c + 8 (m & 1) + key (m = 2c + (m & 1)).
+    // All loads go out before one wait; the half's G region is then released.
     auto combine = [&](uint32_t gcol, const float (&uj)[4], float (&f)[4], int ge_bar) {
-      constexpr int NC = kM / 2;
+      uint32_t g[kM / 2][2][4];
+#pragma unroll
+      for (int c = 0; c < kM / 2; ++c) {
+        tmem_ld4(lane_base + gcol + 16 * c + 4 * rg, g[c][0]);
+        tmem_ld4(lane_base + gcol + 16 * c + 8 + 4 * rg, g[c][1]);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bars[ge_bar]);
       float b1[4], b2[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) { b1[j] = 0.f; b2[j] = 0.f; }
 #pragma unroll
-      for (int c0 = NC - 1; c0 >= 0; c0 -= 2) {
-        uint32_t g[2][2][4];
+      for (int m = kM - 1; m >= 0; --m) {
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
-          if (c0 - i >= 0) {
-            tmem_ld4(lane_base + gcol + 16 * (c0 - i) + 4 * rg, g[i][0]);
-            tmem_ld4(lane_base + gcol + 16 * (c0 - i) + 8 + 4 * rg, g[i][1]);
-          }
-        tmem_wait_ld();
-        if (c0 <= 1) {
-          tc_fence_before();
-          mbar_arrive(&bars[ge_bar]);
-        }
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int c = c0 - i;
-          if (c < 0) continue;
-#pragma unroll
-          for (int mm = 1; mm >= 0; --mm) {
-            const int m = 2 * c + mm;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float a = __uint_as_float(g[i][mm][j]);
-              if (m > 0) {
-                const float bn = fmaf(2.0f * uj[j], b1[j], a - b2[j]);
-                b2[j] = b1[j];
-                b1[j] = bn;
-              } else {
-                f[j] = fmaf(uj[j], b1[j], a - b2[j]);
-              }
-            }
+        for (int j = 0; j < 4; ++j) {
+          const float a = __uint_as_float(g[m >> 1][m & 1][j]);
+          if (m > 0) {
+            const float bn = fmaf(2.0f * uj[j], b1[j], a - b2[j]);
+            b2[j] = b1[j];
+            b1[j] = bn;
+          } else {
+            f[j] = fmaf(uj[j], b1[j], a - b2[j]);
           }
         }
       }
