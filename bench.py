@@ -42,11 +42,14 @@ UNIT = "TFLOP/s"
 # full S=4096, D=128 (each row attends to every earlier key), fwd + autograd bwd
 CPU_SAMPLE_ROWS = 48
 
-# DRAM traffic per launch of the dominant kernel from one ncu capture
-# (dram__bytes_read.sum + dram__bytes_write.sum) of B=1,H=8,S=2048,D=128,
-# scaled by the query rows x heads of this workload (x32); see
-# profiles/exact_bwd_b1h8s2048d128.md.
-NCU_TRAFFIC_BYTES = {"exact": 33.78e6 * 32, "tensor": None}
+# DRAM traffic of one backward call (dram__bytes_read.sum + dram__bytes_write.sum
+# summed over its kernels) from ncu captures of B=1,H=8,S=2048,D=128, scaled to
+# this workload.  Exact kernel: by query rows x heads (x32),
+# profiles/exact_bwd_b1h8s2048d128.md.  Tensor-core kernels: dominated by the
+# dQ -> dK hand-off, 364.8 MB over 8 x 1088 (b, h, query tile, window) blocks,
+# i.e. 41.9 KB per block, times the 128 x 4224 blocks of this workload;
+# profiles/tc_bwd_b1h8s2048d128.md.
+NCU_TRAFFIC_BYTES = {"exact": 33.78e6 * 32, "tensor": 364.8e6 / (8 * 1088) * (128 * 4224)}
 
 
 def causal_pairs(B, H, S):
