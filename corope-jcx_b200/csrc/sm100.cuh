@@ -249,6 +249,21 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool b
          ((uint32_t)(M >> 4) << 24);
 }
 
+// Global loads through the non-coherent path, as volatile asm so that the
+// compiler keeps them where they are written (a prefetch issued early stays
+// early instead of being sunk to its first use).
+__device__ __forceinline__ uint4 ldg128_nc(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint2 ldg64_nc(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"

@@ -1014,8 +1014,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 //
 // Roles (512 threads): warps 0-7 two row warpgroups (group g: pairs
 // 32g..32g+31 of the A rows, keys 4g..4g+3 of each half); warp 8 TMA; warp 9
-// UMMA; warps 12-15 combine (one head dim per thread).  The A rows and the
-// tensor-memory accumulators are double-buffered over windows.
+// UMMA; warps 12-15 combine (one head dim per thread); registers re-split as
+// in the dQ launch.  The A rows and the tensor-memory accumulators are
+// double-buffered over windows.
 namespace k2 {
 constexpr int Q = 0, DO = 32768, AV = 65536;  // AV: 2 buffers of [NS][128][128 B]
 constexpr int YA = AV + 2 * 32768;            // Y half A | P (chunks 6-7 of slab 1)
@@ -1081,6 +1082,9 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
   const uint32_t sYA = smem_u32(smem + k2::YA), sYB = smem_u32(smem + k2::YB);
   const uint32_t s_th_u = smem_u32(s_th);
 
+  if (warp >= 8 && warp < 12) {
+  regs_dec<kCtlRegs>();
+  named_bar(1, kThreads);
   if (warp == 8) {
     // ------------------------------------------------------------ TMA
     if (lane == 0) {
@@ -1131,8 +1135,13 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
       mma_commit(&bars[k2::B_DRAIN]);
       mbar_wait(&bars[k2::B_DRAIN], 0, err, kErrDrain);
     }
+  }
+  __syncwarp();
+  regs_inc<128>();
   } else if (warp >= 12) {
     // ------------------------------------------------------------ combine
+    regs_dec<kBldRegs>();
+    named_bar(1, kThreads);
     const int gt = tid - 384;  // head dim
     float cm[kM];
     {
@@ -1161,8 +1170,13 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const uint32_t creg = acc + (hh ? k2::C1 : k2::C0);
+        // even terms use this lane's column of C^T; odd terms the partner
+        // component's (d ^ 1), whose coefficient for this lane is minus the
+        // partner's own: each lane sums its odd terms with -cm and the sums
+        // are swapped once per key
+        float ev[8], od[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) dk[8 * hh + j] = 0.f;
+        for (int j = 0; j < 8; ++j) { ev[j] = 0.f; od[j] = 0.f; }
 #pragma unroll
         for (int c0 = 0; c0 < kM / 2; c0 += 2) {  // terms 2c, 2c+1 for the 8 keys
           uint32_t g[2][16];
@@ -1176,13 +1190,13 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
             if (c >= kM / 2) continue;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-              const float own = __uint_as_float(g[i][j]);
-              const float partner = __shfl_xor_sync(0xffffffffu, __uint_as_float(g[i][8 + j]), 1);
-              dk[8 * hh + j] = fmaf(cm[2 * c], own, dk[8 * hh + j]);
-              dk[8 * hh + j] = fmaf(cm[2 * c + 1], partner, dk[8 * hh + j]);
+              ev[j] = fmaf(cm[2 * c], __uint_as_float(g[i][j]), ev[j]);
+              od[j] = fmaf(-cm[2 * c + 1], __uint_as_float(g[i][8 + j]), od[j]);
             }
           }
         }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dk[8 * hh + j] = ev[j] + __shfl_xor_sync(0xffffffffu, od[j], 1);
       }
       {
         uint32_t g[2][16];
@@ -1206,8 +1220,12 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
         }
       }
     }
-  } else if (warp < 8) {
+    __syncwarp();
+    regs_inc<128>();
+  } else {
     // ------------------------------------------------------------ row warps
+    regs_inc<kRowRegs>();
+    named_bar(1, kThreads);
     const int rg = warp >> 2;
     const int r = tid & 127;
     const uint8_t* hb0 = P.handoff + ((int64_t)blockIdx.y * P.blocks_bh + tile_block0(qt)) * kHB;
@@ -1222,9 +1240,11 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int qd = 2 * hh + rg;
-        x.dl[hh] = __ldg(reinterpret_cast<const float4*>(hb + HB_DL + (qd * 128 + r) * 16));
-        x.pd[hh] = __ldg(reinterpret_cast<const uint4*>(hb + HB_PD + (qd * 128 + r) * 16));
-        x.u[hh] = __ldg(reinterpret_cast<const uint2*>(hb + HB_U + (qd * 128 + r) * 8));
+        const uint4 dl = ldg128_nc(hb + HB_DL + (qd * 128 + r) * 16);
+        x.dl[hh] = make_float4(__uint_as_float(dl.x), __uint_as_float(dl.y),
+                               __uint_as_float(dl.z), __uint_as_float(dl.w));
+        x.pd[hh] = ldg128_nc(hb + HB_PD + (qd * 128 + r) * 16);
+        x.u[hh] = ldg64_nc(hb + HB_U + (qd * 128 + r) * 8);
       }
       x.carry = __ldg(reinterpret_cast<const float*>(hb + HB_C + 4 * r));
     };
@@ -1310,6 +1330,8 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
       if (!ok) break;
       cur = nxt;
     }
+    __syncwarp();
+    regs_dec<128>();
   }
 
   tc_fence_before();
