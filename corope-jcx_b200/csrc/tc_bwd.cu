@@ -152,8 +152,11 @@ constexpr int kHB = HB_C + 128 * 4;
 // first block of query tile qt within its (b, h): tiles before it are full
 // (8 (q + 1) windows each)
 __host__ __device__ constexpr int64_t tile_block0(int qt) { return 4ll * qt * (qt + 1); }
+// u in [-1, 1] -> 16-bit fixed point, rounded, saturating at both ends
 __device__ __forceinline__ uint32_t u_encode(float u) {
-  return __float2uint_rn(fminf(fmaxf((u + 1.0f) * 32767.5f, 0.0f), 65535.0f));
+  unsigned short q;
+  asm("cvt.rni.sat.u16.f32 %0, %1;" : "=h"(q) : "f"(fmaf(u, 32767.5f, 32767.5f)));
+  return q;
 }
 __device__ __forceinline__ float u_decode(uint32_t q) { return fmaf((float)q, 1.0f / 32767.5f, -1.0f); }
 
@@ -655,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     float da_run = 0.f;  // gate-gradient prefix before the current half
     // this group's keys of the window: i -> key 8 (i >> 2) + 4 rg + (i & 3)
     float zo[8], uo[8], dpo[8];
-    uint32_t csc[32];    // dQ: (cos, sin) halves of this group's 32 pairs
+    uint32_t csc[32];    // dQ: ln2 (cos, sin) as f16 pairs for this group's 32 pairs
     bool ok = wwait(bars[B_Q], 0, err, kErrQ);
 
     // gates and positions of window w; reads the gate scores and dP
@@ -735,10 +738,12 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             const int c = 4 * g + cc;
             sts128(sAV + rg * 16384 + sw128_offset(r, c),
                    make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]));
+            // staged for the dQ update, already scaled by ln 2
             sts128(s_cs + c * 4096,
-                   make_uint4(pack_cs(cs[4 * cc], sn[4 * cc]), pack_cs(cs[4 * cc + 1], sn[4 * cc + 1]),
-                              pack_cs(cs[4 * cc + 2], sn[4 * cc + 2]),
-                              pack_cs(cs[4 * cc + 3], sn[4 * cc + 3])));
+                   make_uint4(pack_cs(kLn2 * cs[4 * cc], kLn2 * sn[4 * cc]),
+                              pack_cs(kLn2 * cs[4 * cc + 1], kLn2 * sn[4 * cc + 1]),
+                              pack_cs(kLn2 * cs[4 * cc + 2], kLn2 * sn[4 * cc + 2]),
+                              pack_cs(kLn2 * cs[4 * cc + 3], kLn2 * sn[4 * cc + 3])));
           }
         } else {
           tmem_st16(lane_base + tk::AVT + 32 * rg + 16 * g, o);
@@ -945,12 +950,12 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         tmem_wait_ld();
 #pragma unroll
         for (int e2 = 0; e2 < 8; ++e2) {
-          const float2 cs = unpack_cs(csc[8 * g + e2]);
-          const float c_ = cs.x * kLn2, s_ = cs.y * kLn2;
+          const float2 cs = unpack_cs(csc[8 * g + e2]);  // ln2 cos, ln2 sin
           const float xe = __uint_as_float(xv[2 * e2]), xo = __uint_as_float(xv[2 * e2 + 1]);
-          qv2[2 * e2] = __float_as_uint(__uint_as_float(qv2[2 * e2]) + fmaf(c_, xe, s_ * xo));
-          qv2[2 * e2 + 1] =
-              __float_as_uint(__uint_as_float(qv2[2 * e2 + 1]) + fmaf(c_, xo, -s_ * xe));
+          qv2[2 * e2] = __float_as_uint(
+              fmaf(cs.y, xo, fmaf(cs.x, xe, __uint_as_float(qv2[2 * e2]))));
+          qv2[2 * e2 + 1] = __float_as_uint(
+              fmaf(-cs.y, xe, fmaf(cs.x, xo, __uint_as_float(qv2[2 * e2 + 1]))));
         }
         tmem_st16(lane_base + tq::DQ + 64 * rg + 16 * g, qv2);
       }
