@@ -861,16 +861,18 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         uint32_t y[kM][2];
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
-          float ta0 = 1.f, tb0 = 1.f;
-          float ta1 = uj[2 * jp], tb1 = uj[2 * jp + 1];
-          y[0][jp] = E::pack(dl[2 * jp], dl[2 * jp + 1]);
-          y[1][jp] = E::pack(dl[2 * jp] * ta1, dl[2 * jp + 1] * tb1);
+          // Y_m = dl T_m(u) obeys the Chebyshev recurrence itself:
+          // Y_{m+1} = 2u Y_m - Y_{m-1}, Y_0 = dl, Y_1 = dl u
+          const float ua = 2.f * uj[2 * jp], ub = 2.f * uj[2 * jp + 1];
+          float ya0 = dl[2 * jp], yb0 = dl[2 * jp + 1];
+          float ya1 = ya0 * uj[2 * jp], yb1 = yb0 * uj[2 * jp + 1];
+          y[0][jp] = E::pack(ya0, yb0);
+          y[1][jp] = E::pack(ya1, yb1);
 #pragma unroll
           for (int m = 2; m < kM; ++m) {
-            const float ta2 = fmaf(2.f * uj[2 * jp], ta1, -ta0);
-            const float tb2 = fmaf(2.f * uj[2 * jp + 1], tb1, -tb0);
-            ta0 = ta1; ta1 = ta2; tb0 = tb1; tb1 = tb2;
-            y[m][jp] = E::pack(dl[2 * jp] * ta2, dl[2 * jp + 1] * tb2);
+            const float ya2 = fmaf(ua, ya1, -ya0), yb2 = fmaf(ub, yb1, -yb0);
+            ya0 = ya1; ya1 = ya2; yb0 = yb1; yb1 = yb2;
+            y[m][jp] = E::pack(ya2, yb2);
           }
         }
         if (MODE == MODE_DQ) {
@@ -943,21 +945,27 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       if (!wwait(bars[B_XF], w & 1, err, kErrX)) return false;
       tc_fence_after();
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {  // 8 pairs (16 columns) per step
-        uint32_t xv[16], qv2[16];
-        tmem_ld16(lane_base + tq::X + 64 * rg + 16 * g, xv);
-        tmem_ld16(lane_base + tq::DQ + 64 * rg + 16 * g, qv2);
+      for (int g0 = 0; g0 < 4; g0 += 2) {  // 16 pairs (32 columns) per load round trip
+        uint32_t xv[2][16], qv2[2][16];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          tmem_ld16(lane_base + tq::X + 64 * rg + 16 * (g0 + i), xv[i]);
+          tmem_ld16(lane_base + tq::DQ + 64 * rg + 16 * (g0 + i), qv2[i]);
+        }
         tmem_wait_ld();
 #pragma unroll
-        for (int e2 = 0; e2 < 8; ++e2) {
-          const float2 cs = unpack_cs(csc[8 * g + e2]);  // ln2 cos, ln2 sin
-          const float xe = __uint_as_float(xv[2 * e2]), xo = __uint_as_float(xv[2 * e2 + 1]);
-          qv2[2 * e2] = __float_as_uint(
-              fmaf(cs.y, xo, fmaf(cs.x, xe, __uint_as_float(qv2[2 * e2]))));
-          qv2[2 * e2 + 1] = __float_as_uint(
-              fmaf(-cs.y, xe, fmaf(cs.x, xo, __uint_as_float(qv2[2 * e2 + 1]))));
+        for (int i = 0; i < 2; ++i) {
+#pragma unroll
+          for (int e2 = 0; e2 < 8; ++e2) {
+            const float2 cs = unpack_cs(csc[8 * (g0 + i) + e2]);  // ln2 cos, ln2 sin
+            const float xe = __uint_as_float(xv[i][2 * e2]), xo = __uint_as_float(xv[i][2 * e2 + 1]);
+            qv2[i][2 * e2] = __float_as_uint(
+                fmaf(cs.y, xo, fmaf(cs.x, xe, __uint_as_float(qv2[i][2 * e2]))));
+            qv2[i][2 * e2 + 1] = __float_as_uint(
+                fmaf(-cs.y, xe, fmaf(cs.x, xo, __uint_as_float(qv2[i][2 * e2 + 1]))));
+          }
+          tmem_st16(lane_base + tq::DQ + 64 * rg + 16 * (g0 + i), qv2[i]);
         }
-        tmem_st16(lane_base + tq::DQ + 64 * rg + 16 * g, qv2);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -1306,16 +1314,18 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
         uint32_t y[kM][2];
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
-          float ta0 = 1.f, tb0 = 1.f;
-          float ta1 = uj[2 * jp], tb1 = uj[2 * jp + 1];
-          y[0][jp] = E::pack(dl[2 * jp], dl[2 * jp + 1]);
-          y[1][jp] = E::pack(dl[2 * jp] * ta1, dl[2 * jp + 1] * tb1);
+          // Y_m = dl T_m(u) obeys the Chebyshev recurrence itself:
+          // Y_{m+1} = 2u Y_m - Y_{m-1}, Y_0 = dl, Y_1 = dl u
+          const float ua = 2.f * uj[2 * jp], ub = 2.f * uj[2 * jp + 1];
+          float ya0 = dl[2 * jp], yb0 = dl[2 * jp + 1];
+          float ya1 = ya0 * uj[2 * jp], yb1 = yb0 * uj[2 * jp + 1];
+          y[0][jp] = E::pack(ya0, yb0);
+          y[1][jp] = E::pack(ya1, yb1);
 #pragma unroll
           for (int m = 2; m < kM; ++m) {
-            const float ta2 = fmaf(2.f * uj[2 * jp], ta1, -ta0);
-            const float tb2 = fmaf(2.f * uj[2 * jp + 1], tb1, -tb0);
-            ta0 = ta1; ta1 = ta2; tb0 = tb1; tb1 = tb2;
-            y[m][jp] = E::pack(dl[2 * jp] * ta2, dl[2 * jp + 1] * tb2);
+            const float ya2 = fmaf(ua, ya1, -ya0), yb2 = fmaf(ub, yb1, -yb0);
+            ya0 = ya1; ya1 = ya2; yb0 = yb1; yb1 = yb2;
+            y[m][jp] = E::pack(ya2, yb2);
           }
         }
 #pragma unroll
