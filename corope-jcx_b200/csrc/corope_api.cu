@@ -158,7 +158,7 @@ static size_t bwd_ws(const corope_bwd_params_t* p) {
 // rows x 16 keys; with less, the (b, h) slices go through it in chunks, or the
 // dK kernel recomputes them.
 static size_t bwd_handoff_ws(const corope_bwd_params_t* p) {
-  if (p->head_dim != 128 || p->algo == COROPE_ALGO_EXACT ||
+  if ((p->head_dim != 64 && p->head_dim != 128) || p->algo == COROPE_ALGO_EXACT ||
       (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16))
     return 0;
   return align256((size_t)p->batch * p->heads * (size_t)tc_bwd_handoff_bytes_per_bh(p->seq_len));
@@ -236,7 +236,7 @@ int corope_bwd(const corope_bwd_params_t* p, corope_stream_t stream) {
   const bool tc_ok = tc_bwd_supported(a, p->dtype);
   if (p->algo == COROPE_ALGO_TENSOR && !tc_ok)
     return fail(COROPE_ERR_UNSUPPORTED,
-                "tensor-core backward needs bf16/f16, head_dim 128 and 16-byte aligned rows");
+                "tensor-core backward needs bf16/f16, head_dim 64 or 128 and 16-byte aligned rows");
   cudaError_t e = cudaMemsetAsync(a.dk32, 0, 2 * align256(kv * 4), st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
   if (p->algo != COROPE_ALGO_EXACT && tc_ok) {

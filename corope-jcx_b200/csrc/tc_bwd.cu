@@ -1,4 +1,4 @@
-// Tensor-core (tcgen05) CoRoPE backward for sm_100a, head_dim 128.
+// Tensor-core (tcgen05) CoRoPE backward for sm_100a, head_dim 64 and 128.
 //
 // Gradients of  logit_tj = sm <R(a_tj theta) q_t, k_j>  with the contextual
 // position a_tj = sum_{i=j+1..t} sigmoid(q_t . k_i).  As in the forward, keys
@@ -71,10 +71,11 @@ using tcx::kSmemLimit;
 using tcx::kW;
 using tcx::sigmoid_f;
 
-constexpr int D = 128;
-constexpr int NS = 2;        // 64-element slabs of the head dim
-constexpr int NP = 64;       // rotation pairs
-constexpr int KSTEPS = 8;    // 16-element K steps over the head dim
+// Head dims 64 and 128.  Shared-memory tiles are always laid out for 128
+// (two 64-element slabs); with 64 the second slab of Q, dO and the A rows is
+// zero, which keeps the transposed GEMMs (M = head dim) at M = 128.
+constexpr int NS = 2;        // 64-element slabs in the shared-memory layout
+constexpr int NPX = 64;      // rotation pairs of the widest head dim (table width)
 constexpr int kBM = 128;     // query rows per CTA
 constexpr int kKT = 32;      // keys per K/V tile (2 windows)
 constexpr int kThreads = 512;
@@ -121,8 +122,8 @@ constexpr int S_Y = S_AV + NS * 16384;       // dK: Y | P rows [NS][128][128 B];
 constexpr int S_DS = S_Y + NS * 16384;       // dK: dS rows [128][128 B] (bytes 96..127 used)
 template <int MODE> struct SmemTail {
   static constexpr int COEF = S_DS + (MODE == MODE_DK ? 16384 : 0);
-  static constexpr int TH = COEF + kM * NP * 4;
-  static constexpr int BAR = TH + NP * 4;
+  static constexpr int TH = COEF + kM * NPX * 4;
+  static constexpr int BAR = TH + NPX * 4;
   static constexpr int NBAR = 40;
   static constexpr int SLOT = BAR + NBAR * 8;
   static constexpr int XCH = (SLOT + 16 + 15) & ~15;  // gate-gradient sums [half][group][128]
@@ -188,11 +189,15 @@ __device__ __forceinline__ float2 unpack_cs(uint32_t v) {
   return __half22float2(*reinterpret_cast<const __half2*>(&v));
 }
 
-template <typename T, int MODE, bool HAS_BIAS>
+template <typename T, int D, int MODE, bool HAS_BIAS>
 __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant__ Params P) {
   using E = ElemTraits<T>;
   using L = SmemTail<MODE>;
   using namespace sm100;
+  constexpr int NP = D / 2;        // rotation pairs
+  constexpr int KSTEPS = D / 16;   // 16-element K steps over the head dim
+  constexpr int DSL = D / 64;      // slabs holding data
+  constexpr int PW = NP / 2;       // rotation pairs per row warpgroup
   // gate/dP accumulators: double-buffered in the dQ launch, single in the dK
   // launch (its tensor memory holds the A operand and two C regions)
   constexpr int NSD = MODE == MODE_DQ ? 2 : 1;
@@ -248,14 +253,23 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     mbar_init(&bars[B_DRAIN6], 1);
     fence_mbar_init();
   }
-  for (int i = tid; i < kM * NP; i += kThreads) s_coef[i] = P.coef[i / NP][i % NP];
+  for (int i = tid; i < kM * NPX; i += kThreads) s_coef[i] = P.coef[i / NPX][i % NPX];
   for (int p = tid; p < NP; p += kThreads) s_th[p] = theta_at(P.thetas, P.theta, p, D);
   // The K^(m) buffers start at zero: the builders skip the pruned (term,
   // head-dim) entries, which the dQ launch's X GEMM still reads densely.
+  // With D = 64 the unused second slab of Q, dO and the A rows is zero too
+  // (the dK launch's transposed GEMMs read it).
   {
     uint4* kb = reinterpret_cast<uint4*>(smem + P.bop);
     const int n16 = (2 * P.nb * P.b_buf_bytes) / 16;
     for (int i = tid; i < n16; i += kThreads) kb[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (DSL == 1) {
+      for (int i = tid; i < 1024; i += kThreads) {
+        reinterpret_cast<uint4*>(smem + S_Q + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
+        reinterpret_cast<uint4*>(smem + S_DO + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
+        reinterpret_cast<uint4*>(smem + S_AV + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
     fence_async_smem();
   }
   if (warp == 0) {
@@ -289,8 +303,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         prefetch_tmap(&P.tm_k);
         prefetch_tmap(&P.tm_v);
         prefetch_tmap(&P.tm_do);
-        mbar_expect_tx(&bars[B_Q], 2 * NS * 16384);
-        for (int s = 0; s < NS; ++s) {
+        mbar_expect_tx(&bars[B_Q], 2 * DSL * 16384);
+        for (int s = 0; s < DSL; ++s) {
           tma_load_4d(smem + S_Q + s * 16384, &P.tm_q, &bars[B_Q], 64 * s, q0, h, b);
           tma_load_4d(smem + S_DO + s * 16384, &P.tm_do, &bars[B_Q], 64 * s, q0, h, b);
         }
@@ -299,8 +313,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         for (int n = 0; n <= TL; ++n) {
           const int st = n & 1, u = n >> 1;
           if (n >= 2 && !mbar_wait(&bars[B_KVE + st], (u - 1) & 1, err, kErrKvEmpty)) break;
-          mbar_expect_tx(&bars[B_KVF + st], 2 * NS * 4096);
-          for (int s = 0; s < NS; ++s) {
+          mbar_expect_tx(&bars[B_KVF + st], 2 * DSL * 4096);
+          for (int s = 0; s < DSL; ++s) {
             tma_load_4d(smem + S_K + (st * NS + s) * 4096, &P.tm_k, &bars[B_KVF + st], 64 * s,
                         kKT * n, hk, b);
             tma_load_4d(smem + S_V + (st * NS + s) * 4096, &P.tm_v, &bars[B_KVF + st], 64 * s,
@@ -492,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           const int local = it - base;
           const int r = local >> 1, c = 2 * s2 + (local & 1), m = r >> 3, j = r & 7;
           const uint32_t kofs = (c >> 3) * 4096 + j * 128 + (((c & 7) ^ j) << 4);
-          const uint32_t cofs = (m * NP + 4 * c) * 4;
+          const uint32_t cofs = (m * NPX + 4 * c) * 4;
           const uint32_t bofs = P.b_slab_off[c >> 3] + sw128_offset(r, c & 7);
           const uint32_t flags = (m & 1) | ((m & 2) ? 2u : 0u) | (((m + 1) & 2) ? 4u : 0u);
           d = make_uint2(kofs | (cofs << 16), bofs | (flags << 16));
@@ -516,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           case 2: sgn = -1.f; break;
           default: sgn = e ? -1.f : 1.f; break;
         }
-        cm[m] = kLn2 * s_coef[m * NP + p] * sgn;
+        cm[m] = kLn2 * s_coef[m * NPX + p] * sgn;  // zero for p >= D / 2
       }
     }
     const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
@@ -623,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = w * kW + j;
-        if (key < S) {
+        if (key < S && d < D) {
           atomicAdd(dk32 + (int64_t)key * D + d, dk[j]);
           atomicAdd(dv32 + (int64_t)key * D + d, dv[j]);
         }
@@ -658,7 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     float da_run = 0.f;  // gate-gradient prefix before the current half
     // this group's keys of the window: i -> key 8 (i >> 2) + 4 rg + (i & 3)
     float zo[8], uo[8], dpo[8];
-    uint32_t csc[32];    // dQ: ln2 (cos, sin) as f16 pairs for this group's 32 pairs
+    uint32_t csc[PW];    // dQ: ln2 (cos, sin) as f16 pairs for this group's pairs
     bool ok = wwait(bars[B_Q], 0, err, kErrQ);
 
     // gates and positions of window w; reads the gate scores and dP
@@ -709,14 +723,14 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     auto build_a = [&]() {
       const float bse = carry + kC0;
 #pragma unroll 1
-      for (int g = 0; g < 2; ++g) {
+      for (int g = 0; g < PW / 16; ++g) {
         uint4 qv[4];
         float th[16];
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
-          const int c = 4 * g + cc;  // chunk within the slab (4 pairs)
-          qv[cc] = lds128(sQ + rg * 16384 + sw128_offset(r, c));
-          const float4 t4 = lds128f(s_th_u + 16 * (8 * rg + c));
+          const int c = rg * (PW / 4) + 4 * g + cc;  // chunk of the row (4 pairs)
+          qv[cc] = lds128(sQ + (c >> 3) * 16384 + sw128_offset(r, c & 7));
+          const float4 t4 = lds128f(s_th_u + 16 * c);
           th[4 * cc] = t4.x; th[4 * cc + 1] = t4.y; th[4 * cc + 2] = t4.z; th[4 * cc + 3] = t4.w;
         }
         float rr[16], sn[16], cs[16];
@@ -735,18 +749,18 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         if (MODE == MODE_DQ) {
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
-            const int c = 4 * g + cc;
-            sts128(sAV + rg * 16384 + sw128_offset(r, c),
+            const int c = rg * (PW / 4) + 4 * g + cc;
+            sts128(sAV + (c >> 3) * 16384 + sw128_offset(r, c & 7),
                    make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]));
             // staged for the dQ update, already scaled by ln 2
-            sts128(s_cs + c * 4096,
+            sts128(s_cs + (4 * g + cc) * 4096,
                    make_uint4(pack_cs(kLn2 * cs[4 * cc], kLn2 * sn[4 * cc]),
                               pack_cs(kLn2 * cs[4 * cc + 1], kLn2 * sn[4 * cc + 1]),
                               pack_cs(kLn2 * cs[4 * cc + 2], kLn2 * sn[4 * cc + 2]),
                               pack_cs(kLn2 * cs[4 * cc + 3], kLn2 * sn[4 * cc + 3])));
           }
         } else {
-          tmem_st16(lane_base + tk::AVT + 32 * rg + 16 * g, o);
+          tmem_st16(lane_base + tk::AVT + rg * PW + 16 * g, o);
         }
       }
       if (MODE == MODE_DQ) {
@@ -760,7 +774,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 
     auto load_cs = [&]() {
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < PW / 4; ++c) {
         const uint4 v = lds128(s_cs + c * 4096);
         csc[4 * c] = v.x; csc[4 * c + 1] = v.y; csc[4 * c + 2] = v.z; csc[4 * c + 3] = v.w;
       }
@@ -817,14 +831,16 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         if (w > 0 && !wwait(bars[B_YFREE], (w - 1) & 1, err, kErrY)) return false;
         tc_fence_after();
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {
+        for (int g = 0; g < PW / 16; ++g) {
           uint32_t o[16];
-          tmem_ld16(lane_base + tk::AVT + 32 * rg + 16 * g, o);
+          tmem_ld16(lane_base + tk::AVT + rg * PW + 16 * g, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
-            sts128(sAV + rg * 16384 + sw128_offset(r, 4 * g + cc),
+          for (int cc = 0; cc < 4; ++cc) {
+            const int c = rg * (PW / 4) + 4 * g + cc;
+            sts128(sAV + (c >> 3) * 16384 + sw128_offset(r, c & 7),
                    make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]));
+          }
         }
       }
       uint32_t dsa0 = 0u, dsa1 = 0u;  // dS of half A (packed), written with half B
@@ -945,12 +961,12 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       if (!wwait(bars[B_XF], w & 1, err, kErrX)) return false;
       tc_fence_after();
 #pragma unroll
-      for (int g0 = 0; g0 < 4; g0 += 2) {  // 16 pairs (32 columns) per load round trip
+      for (int g0 = 0; g0 < PW / 8; g0 += 2) {  // 16 pairs (32 columns) per load round trip
         uint32_t xv[2][16], qv2[2][16];
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
-          tmem_ld16(lane_base + tq::X + 64 * rg + 16 * (g0 + i), xv[i]);
-          tmem_ld16(lane_base + tq::DQ + 64 * rg + 16 * (g0 + i), qv2[i]);
+          tmem_ld16(lane_base + tq::X + 2 * PW * rg + 16 * (g0 + i), xv[i]);
+          tmem_ld16(lane_base + tq::DQ + 2 * PW * rg + 16 * (g0 + i), qv2[i]);
         }
         tmem_wait_ld();
 #pragma unroll
@@ -964,7 +980,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             qv2[i][2 * e2 + 1] = __float_as_uint(
                 fmaf(-cs.y, xe, fmaf(cs.x, xo, __uint_as_float(qv2[i][2 * e2 + 1]))));
           }
-          tmem_st16(lane_base + tq::DQ + 64 * rg + 16 * (g0 + i), qv2[i]);
+          tmem_st16(lane_base + tq::DQ + 2 * PW * rg + 16 * (g0 + i), qv2[i]);
         }
       }
       tmem_wait_st();
@@ -994,15 +1010,15 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       // all GEMMs into DQ are done (the last window's B_XF was waited above)
       T* dqrow = reinterpret_cast<T*>(P.dq) + b * P.dqs[0] + h * P.dqs[1] + (int64_t)t * P.dqs[2];
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < PW / 8; ++c) {
         uint32_t o[16];
-        tmem_ld16(lane_base + tq::DQ + 64 * rg + 16 * c, o);
+        tmem_ld16(lane_base + tq::DQ + 2 * PW * rg + 16 * c, o);
         tmem_wait_ld();
         uint32_t pk[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) pk[i] = E::pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
         if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(dqrow + 64 * rg + 16 * c);
+          uint4* dst = reinterpret_cast<uint4*>(dqrow + 2 * PW * rg + 16 * c);
           dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
@@ -1035,8 +1051,8 @@ constexpr int Q = 0, DO = 32768, AV = 65536;  // AV: 2 buffers of [NS][128][128 
 constexpr int YA = AV + 2 * 32768;            // Y half A | P (chunks 6-7 of slab 1)
 constexpr int YB = YA + 32768;                // Y half B | dS (chunks 6-7 of slab 1)
 constexpr int COEF = YB + 32768;
-constexpr int TH = COEF + kM * NP * 4;
-constexpr int BAR = TH + NP * 4;
+constexpr int TH = COEF + kM * NPX * 4;
+constexpr int BAR = TH + NPX * 4;
 constexpr int SLOT = BAR + 16 * 8;
 constexpr int TOTAL = SLOT + 16;
 // RDY / YFREE per half: the rows write the next window's half A while the
@@ -1046,10 +1062,11 @@ enum { B_Q = 0, B_RDY = 1, B_AVE = 3, B_YFREE = 5, B_CF = 7, B_CE = 9, B_DRAIN =
 constexpr uint32_t C0 = 0, C1 = 112, DVK = 224, BUF = 256;
 }  // namespace k2
 
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant__ Params P) {
   using E = ElemTraits<T>;
   using namespace sm100;
+  constexpr int NP = D / 2, DSL = D / 64, PW = NP / 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -1080,8 +1097,17 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
     mbar_init(&bars[k2::B_DRAIN], 1);
     fence_mbar_init();
   }
-  for (int i = tid; i < kM * NP; i += kThreads) s_coef[i] = P.coef[i / NP][i % NP];
+  for (int i = tid; i < kM * NPX; i += kThreads) s_coef[i] = P.coef[i / NPX][i % NPX];
   for (int p = tid; p < NP; p += kThreads) s_th[p] = theta_at(P.thetas, P.theta, p, D);
+  if (DSL == 1) {  // D = 64: the second slab of Q, dO and both A buffers is zero
+    for (int i = tid; i < 1024; i += kThreads) {
+      reinterpret_cast<uint4*>(smem + k2::Q + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
+      reinterpret_cast<uint4*>(smem + k2::DO + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
+      reinterpret_cast<uint4*>(smem + k2::AV + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
+      reinterpret_cast<uint4*>(smem + k2::AV + 32768 + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_async_smem();
+  }
   if (warp == 0) {
     tmem_alloc(tslot, 512);
     tmem_relinquish();
@@ -1103,8 +1129,8 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
     if (lane == 0) {
       prefetch_tmap(&P.tm_q);
       prefetch_tmap(&P.tm_do);
-      mbar_expect_tx(&bars[k2::B_Q], 2 * NS * 16384);
-      for (int s = 0; s < NS; ++s) {
+      mbar_expect_tx(&bars[k2::B_Q], 2 * DSL * 16384);
+      for (int s = 0; s < DSL; ++s) {
         tma_load_4d(smem + k2::Q + s * 16384, &P.tm_q, &bars[k2::B_Q], 64 * s, q0, h, b);
         tma_load_4d(smem + k2::DO + s * 16384, &P.tm_do, &bars[k2::B_Q], 64 * s, q0, h, b);
       }
@@ -1168,7 +1194,7 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
           case 2: sgn = -1.f; break;
           default: sgn = e ? -1.f : 1.f; break;
         }
-        cm[m] = kLn2 * s_coef[m * NP + p] * sgn;
+        cm[m] = kLn2 * s_coef[m * NPX + p] * sgn;  // zero for p >= D / 2
       }
     }
     const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
@@ -1227,7 +1253,7 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = w * kW + j;
-        if (key < S) {
+        if (key < S && gt < D) {
           atomicAdd(dk32 + (int64_t)key * D, dk[j]);
           atomicAdd(dv32 + (int64_t)key * D, dv[j]);
         }
@@ -1271,16 +1297,16 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
         break;
       {
         const float bse = cur.carry + kC0;
-        const uint32_t av = sAV + 32768 * (w & 1) + rg * 16384;
+        const uint32_t av = sAV + 32768 * (w & 1);
 #pragma unroll 1
-        for (int g = 0; g < 2; ++g) {
+        for (int g = 0; g < PW / 16; ++g) {
           uint4 qv[4];
           float th[16];
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
-            const int c = 4 * g + cc;
-            qv[cc] = lds128(sQ + rg * 16384 + sw128_offset(r, c));
-            const float4 t4 = lds128f(s_th_u + 16 * (8 * rg + c));
+            const int c = rg * (PW / 4) + 4 * g + cc;  // chunk of the row (4 pairs)
+            qv[cc] = lds128(sQ + (c >> 3) * 16384 + sw128_offset(r, c & 7));
+            const float4 t4 = lds128f(s_th_u + 16 * c);
             th[4 * cc] = t4.x; th[4 * cc + 1] = t4.y; th[4 * cc + 2] = t4.z; th[4 * cc + 3] = t4.w;
           }
           float rr[16], sn[16], cs[16];
@@ -1298,7 +1324,8 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
               const float s_ = sn[4 * cc + i], c_ = cs[4 * cc + i];
               o[i] = E::pack(qe * c_ - qo * s_, qe * s_ + qo * c_);
             }
-            sts128(av + sw128_offset(r, 4 * g + cc), make_uint4(o[0], o[1], o[2], o[3]));
+            const int c = rg * (PW / 4) + 4 * g + cc;
+            sts128(av + (c >> 3) * 16384 + sw128_offset(r, c & 7), make_uint4(o[0], o[1], o[2], o[3]));
           }
         }
       }
@@ -1365,7 +1392,7 @@ static int plan(Params& p) {
     p.b_slab_off[s] = off;
     off += p.nrow[4 * s] * 128;
   }
-  for (int s = 0; s < KSTEPS; ++s) rows += p.nrow[s];
+  for (int s = 0; s < 8; ++s) rows += p.nrow[s];  // zero beyond the head dim's K steps
   p.max_items = (2 * rows + 127) / 128;  // (term x key row, 8-element chunk) items per builder
   p.bop = (L::ITEMS + p.max_items * 128 * 8 + 1023) & ~1023;
   p.b_buf_bytes = (off + 1023) & ~1023;
@@ -1373,19 +1400,19 @@ static int plan(Params& p) {
   return p.bop + 2 * p.nb * p.b_buf_bytes + 1024;
 }
 
-template <typename T, int MODE>
+template <typename T, int D, int MODE>
 static cudaError_t launch_mode(Params& p, bool bias, int S, int nbh, cudaStream_t st) {
   const int smem = plan<MODE>(p);
   if (smem > kSmemLimit) return cudaErrorInvalidValue;
   dim3 grid((S + kBM - 1) / kBM, nbh);
   cudaError_t e;
   if (bias) {
-    auto kern = bwd_kernel<T, MODE, true>;
+    auto kern = bwd_kernel<T, D, MODE, true>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return e;
     kern<<<grid, kThreads, smem, st>>>(p);
   } else {
-    auto kern = bwd_kernel<T, MODE, false>;
+    auto kern = bwd_kernel<T, D, MODE, false>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return e;
     kern<<<grid, kThreads, smem, st>>>(p);
@@ -1393,11 +1420,11 @@ static cudaError_t launch_mode(Params& p, bool bias, int S, int nbh, cudaStream_
   return cudaGetLastError();
 }
 
-template <typename T>
+template <typename T, int D>
 static cudaError_t launch_dk2(Params& p, int S, int nbh, cudaStream_t st) {
   const int smem = k2::TOTAL + 1024;
   dim3 grid((S + kBM - 1) / kBM, nbh);
-  auto kern = dk2_kernel<T>;
+  auto kern = dk2_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, smem, st>>>(p);
@@ -1411,7 +1438,7 @@ static int64_t blocks_per_bh(int S) {
   return n;
 }
 
-template <typename T>
+template <typename T, int D>
 static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* handoff,
                               size_t handoff_bytes, cudaStream_t st) {
   const int64_t per_bh = blocks_per_bh(S) * kHB;
@@ -1421,8 +1448,8 @@ static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* hand
   if (chunk == 0) {
     p.handoff = nullptr;
     p.bh0 = 0;
-    e = launch_mode<T, MODE_DQ>(p, bias, S, BH, st);
-    if (e == cudaSuccess) e = launch_mode<T, MODE_DK>(p, bias, S, BH, st);
+    e = launch_mode<T, D, MODE_DQ>(p, bias, S, BH, st);
+    if (e == cudaSuccess) e = launch_mode<T, D, MODE_DK>(p, bias, S, BH, st);
     return e;
   }
   p.handoff = handoff;
@@ -1430,8 +1457,8 @@ static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* hand
   for (int bh0 = 0; bh0 < BH && e == cudaSuccess; bh0 += chunk) {
     p.bh0 = bh0;
     const int nbh = std::min(chunk, BH - bh0);
-    e = launch_mode<T, MODE_DQ>(p, bias, S, nbh, st);
-    if (e == cudaSuccess) e = launch_dk2<T>(p, S, nbh, st);
+    e = launch_mode<T, D, MODE_DQ>(p, bias, S, nbh, st);
+    if (e == cudaSuccess) e = launch_dk2<T, D>(p, S, nbh, st);
   }
   return e;
 }
@@ -1447,7 +1474,7 @@ static bool rows16(const void* ptr, const int64_t* st) {
 
 bool tc_bwd_supported(const BwdArgs& a, int dtype) {
   if (dtype != COROPE_DTYPE_BF16 && dtype != COROPE_DTYPE_F16) return false;
-  if (a.D != 128) return false;
+  if (a.D != 64 && a.D != 128) return false;
   if (!rows16(a.q, a.qs) || !rows16(a.k, a.ks) || !rows16(a.v, a.vs) ||
       !rows16(a.dout, a.dos) || !rows16(a.dq, a.dqs))
     return false;
@@ -1491,9 +1518,12 @@ cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* ha
   tcx::fill_coefficients(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
   const bool bias = a.bias != nullptr;
   uint8_t* hp = static_cast<uint8_t*>(handoff);
+  const int BH = a.B * a.H;
   if (dtype == COROPE_DTYPE_BF16)
-    return launch_all<__nv_bfloat16>(p, bias, a.B * a.H, a.S, hp, handoff_bytes, st);
-  return launch_all<__half>(p, bias, a.B * a.H, a.S, hp, handoff_bytes, st);
+    return a.D == 64 ? launch_all<__nv_bfloat16, 64>(p, bias, BH, a.S, hp, handoff_bytes, st)
+                     : launch_all<__nv_bfloat16, 128>(p, bias, BH, a.S, hp, handoff_bytes, st);
+  return a.D == 64 ? launch_all<__half, 64>(p, bias, BH, a.S, hp, handoff_bytes, st)
+                   : launch_all<__half, 128>(p, bias, BH, a.S, hp, handoff_bytes, st);
 }
 
 }  // namespace corope

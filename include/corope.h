@@ -108,7 +108,7 @@ int corope_fwd(const corope_fwd_params_t *p, corope_stream_t stream);
 int corope_mqa_fwd(const corope_fwd_params_t *p, corope_stream_t stream);
 
 /* Bytes of workspace corope_bwd uses at its fastest for these parameters:
- * the minimum below plus, for the tensor-core path (head_dim 128, bf16/f16),
+ * the minimum below plus, for the tensor-core path (head_dim 64 or 128, bf16/f16),
  * a hand-off region of 20,992 bytes per 128 query rows x 16 keys through
  * which the dQ kernel passes its per-(row, key) results to the dK kernel.
  * Any size between the two works (smaller hand-off regions are used slice by

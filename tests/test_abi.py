@@ -84,9 +84,12 @@ def test_backward_workspace_checks():
         setattr(p, n, st)
     p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = 1, 2, 2, 128, 64
     p.sm_scale, p.theta, p.causal, p.dtype = 0.125, 1e4, 1, 2
-    need = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
-    # delta + lse rows, fp32 dk/dv accumulators
+    need = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
+    full = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
+    # delta + lse rows, fp32 dk/dv accumulators; the full size adds the
+    # tensor-core hand-off region (bf16, head_dim 64)
     assert need >= 2 * 2 * 128 * 4 + 2 * 2 * 128 * 64 * 4
+    assert full > need
     assert lib.corope_bwd(ctypes.byref(p), None) == _lib.ERR_WORKSPACE
     p.workspace, p.workspace_bytes = fake, need - 1
     assert lib.corope_bwd(ctypes.byref(p), None) == _lib.ERR_WORKSPACE

@@ -144,10 +144,12 @@ def test_mqa_reference_bias_draw_is_reproducible():
 
 
 # ------------------------------------------------------ full fwd + bwd ----
-@pytest.mark.parametrize("algo", ["exact"])
+@pytest.mark.parametrize("algo", ["exact", "tensor"])
 def test_config3_forward_backward_bf16(algo):
     """B=8, H=16, S=2048, D=64 bf16, seed 2, theta 1e4: dq, dk, dv of two
-    (b, h) slices against the closed-form oracle gradients."""
+    (b, h) slices against the closed-form oracle gradients, on both kernel
+    families (the tensor-core backward at D=64 keeps its transposed GEMMs
+    at M=128 with a zero second slab)."""
     (q, k, v, do), cpu = inputs(8, 16, 2048, 64, 2, torch.bfloat16)
     sm = 1 / math.sqrt(64)
     saved, o = co_rope_forward(q, k, v, sm, theta=1e4, algo=algo)
@@ -284,11 +286,12 @@ def test_tensor_forward_strided_module_layout():
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("S,theta,hkv", [(1, 1e4, 3), (40, 1e4, 3), (300, 1e4, 3), (513, 5e5, 3),
                                          (300, 1e4, 1)])
-def test_tensor_backward_small_shapes(dtype, S, theta, hkv):
-    """Tensor-core backward (D=128) against the closed-form oracle gradients:
-    ragged S (partial windows and query tiles), both half types, MQA grouping
-    (k/v gradients summed over the heads that share a K/V head)."""
-    D, H = 128, 3
+@pytest.mark.parametrize("D", [64, 128])
+def test_tensor_backward_small_shapes(dtype, S, theta, hkv, D):
+    """Tensor-core backward (D=64 and 128) against the closed-form oracle
+    gradients: ragged S (partial windows and query tiles), both half types, MQA
+    grouping (k/v gradients summed over the heads that share a K/V head)."""
+    H = 3
     (q, k, v, do), cpu = inputs(2, H, S, D, 31, dtype, hkv=hkv)
     sm = 1 / math.sqrt(D)
     from CoROPE import _lib
