@@ -356,3 +356,27 @@ def test_tensor_backward_workspace_paths(mode):
         assert torch.isfinite(mine).all(), name
         assert maxabs(mine, r) < G_MAXABS, name
         assert rel_l2(mine, r) < REL_L2, name
+
+
+@pytest.mark.parametrize("algo", ["exact", "tensor"])
+@pytest.mark.parametrize("D", [64, 128])
+def test_backward_with_contextual_bias(algo, D):
+    """MQA forward and backward with an additive [S, S] bias (the reference MQA
+    kernel's extra term), gradients against the closed-form oracle."""
+    B, H, S = 1, 4, 200
+    (q, k, v, do), cpu = inputs(B, H, S, D, 71, torch.bfloat16, hkv=1)
+    g = torch.Generator().manual_seed(72)
+    bias = (torch.randn(S, S, generator=g) * 0.5).tril()
+    sm = 1 / math.sqrt(D)
+    saved, o = co_rope_mqa_forward(q, k, v, sm, contextual_bias=bias.to(DEV), algo=algo)
+    dq, dk, dv = co_rope_backward(saved, do, sm, 1e4, algo=algo, contextual_bias=bias.to(DEV))
+    torch.cuda.synchronize()
+    from CoROPE import _lib
+    assert _lib.take_device_error() == 0
+    ref = O.forward_dense(*[t.double() for t in cpu[:3]], sm, 1e4, bias=bias.double())
+    assert maxabs(o, ref["o"]) < O_MAXABS
+    rq, rk, rv = O.backward_dense(*[t.double() for t in cpu], sm, 1e4, bias=bias.double())
+    for name, mine, r in (("dq", dq, rq), ("dk", dk, rk), ("dv", dv, rv)):
+        assert torch.isfinite(mine).all(), name
+        assert maxabs(mine, r) < G_MAXABS, name
+        assert rel_l2(mine, r) < REL_L2, name
