@@ -259,6 +259,11 @@ __device__ __forceinline__ uint4 ldg128_nc(const void* p) {
                : "l"(p));
   return v;
 }
+__device__ __forceinline__ float ldg32f_nc(const void* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
 __device__ __forceinline__ uint2 ldg64_nc(const void* p) {
   uint2 v;
   asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));

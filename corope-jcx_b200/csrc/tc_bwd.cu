@@ -66,7 +66,6 @@ using tcx::ElemTraits;
 using tcx::kC0;
 using tcx::kLn2;
 using tcx::kLog2e;
-using tcx::kM;
 using tcx::kSmemLimit;
 using tcx::kW;
 using tcx::sigmoid_f;
@@ -74,6 +73,10 @@ using tcx::sigmoid_f;
 // Head dims 64 and 128.  Shared-memory tiles are always laid out for 128
 // (two 64-element slabs); with 64 the second slab of Q, dO and the A rows is
 // zero, which keeps the transposed GEMMs (M = head dim) at M = 128.
+// Chebyshev terms: 16 in the backward (the position derivative of a 14-term
+// expansion errs by up to 2.4% at the highest frequency, 0.2% with 16); the
+// recompute dK kernel at head dim 128 keeps 14 to fit its shared memory.
+constexpr int kMB = 16;      // most terms any backward kernel uses
 constexpr int NS = 2;        // 64-element slabs in the shared-memory layout
 constexpr int NPX = 64;      // rotation pairs of the widest head dim (table width)
 constexpr int kBM = 128;     // query rows per CTA
@@ -108,7 +111,7 @@ struct Params {
   uint8_t* handoff;     // dQ launch -> dK launch, per (b, h, query tile, window) block
   int64_t blocks_bh;    // hand-off blocks per (b, h)
   int bh0;              // first (b, h) of this launch (blockIdx.y counts from it)
-  float coef[kM][64];
+  float coef[kMB][64];
 };
 
 // shared memory (bytes from the 1024-aligned base)
@@ -119,10 +122,10 @@ constexpr int S_V = S_K + 2 * NS * 4096;
 constexpr int S_AV = S_V + 2 * NS * 4096;    // A operand rows [NS][128][128 B]
 constexpr int S_Y = S_AV + NS * 16384;       // dK: Y | P rows [NS][128][128 B];
                                              // dQ: staged (cos, sin) [8 chunks][256 threads][16 B]
-constexpr int S_DS = S_Y + NS * 16384;       // dK: dS rows [128][128 B] (bytes 96..127 used)
-template <int MODE> struct SmemTail {
+constexpr int S_DS = S_Y + NS * 16384;       // dK: P | dS rows [128][128 B] (bytes 64..127)
+template <int MODE, int KM> struct SmemTail {
   static constexpr int COEF = S_DS + (MODE == MODE_DK ? 16384 : 0);
-  static constexpr int TH = COEF + kM * NPX * 4;
+  static constexpr int TH = COEF + KM * NPX * 4;
   static constexpr int BAR = TH + NPX * 4;
   static constexpr int NBAR = 40;
   static constexpr int SLOT = BAR + NBAR * 8;
@@ -130,17 +133,21 @@ template <int MODE> struct SmemTail {
   static constexpr int ITEMS = XCH + 2 * 2 * 128 * 4;  // then the K^(m) buffers at Params::bop
 };
 
-// tensor memory columns
-namespace tq {  // dQ launch
-constexpr uint32_t X = 0, DQ = 128, G = 256, SG0 = 368, DP0 = 400,
-                   YT = 432;  // Y (56 cols) | dS (8 cols)
-static_assert(YT + 64 <= 512, "tmem");
-}  // namespace tq
-namespace tk {  // dK launch
-// C0 / C1: C^T of the window's halves (terms x keys); DVK: dV^T (16 keys) | dK_gate^T (16 keys)
-constexpr uint32_t G = 0, SG0 = 112, DP0 = 128, AVT = 144, C0 = 208, C1 = 320, DVK = 432;
-static_assert(DVK + 32 <= 512, "tmem");
-}  // namespace tk
+// tensor memory columns (GW = 8 KM: one G half, terms x keys)
+template <int KM> struct TQ {  // dQ launch
+  static constexpr uint32_t GW = 8 * KM;
+  static constexpr int NSD = KM > 14 ? 1 : 2;  // gate / dP buffers
+  static constexpr uint32_t X = 0, DQ = 128, G = 256, SG0 = G + GW, DP0 = SG0 + 16 * NSD,
+                            YT = DP0 + 16 * NSD;  // Y (4 KM cols) | dS (8 cols)
+  static_assert(YT + 4 * KM + 8 <= 512, "tmem");
+};
+template <int KM> struct TK {  // recompute dK launch
+  // C0 / C1: C^T of the window's halves; DVK: dV^T (16 keys) | dK_gate^T (16 keys)
+  static constexpr uint32_t GW = 8 * KM;
+  static constexpr uint32_t G = 0, SG0 = GW, DP0 = GW + 16, AVT = GW + 32, C0 = AVT + 64,
+                            C1 = C0 + GW, DVK = C1 + GW;
+  static_assert(DVK + 32 <= 512, "tmem");
+};
 
 // Hand-off block (one per (b, h, query tile, window), 128 rows): what the dK
 // launch needs to rebuild Y without the gates, the G GEMM or the Clenshaw
@@ -189,18 +196,21 @@ __device__ __forceinline__ float2 unpack_cs(uint32_t v) {
   return __half22float2(*reinterpret_cast<const __half2*>(&v));
 }
 
-template <typename T, int D, int MODE, bool HAS_BIAS>
+template <typename T, int D, int MODE, bool HAS_BIAS, int KM>
 __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant__ Params P) {
   using E = ElemTraits<T>;
-  using L = SmemTail<MODE>;
+  using L = SmemTail<MODE, KM>;
+  using tq = TQ<KM>;
+  using tk = TK<KM>;
   using namespace sm100;
+  constexpr int kM = KM;           // Chebyshev terms
   constexpr int NP = D / 2;        // rotation pairs
   constexpr int KSTEPS = D / 16;   // 16-element K steps over the head dim
   constexpr int DSL = D / 64;      // slabs holding data
   constexpr int PW = NP / 2;       // rotation pairs per row warpgroup
   // gate/dP accumulators: double-buffered in the dQ launch, single in the dK
   // launch (its tensor memory holds the A operand and two C regions)
-  constexpr int NSD = MODE == MODE_DQ ? 2 : 1;
+  constexpr int NSD = MODE == MODE_DQ ? tq::NSD : 1;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -429,14 +439,14 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             if (!ok) break;
             // gate part: dq += dS K_w  (A = dS from tensor memory, B = K tile)
             if (!(ok = mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull))) break;
-            mma_ts(tmem + tq::DQ, tmem + tq::YT + 56,
+            mma_ts(tmem + tq::DQ, tmem + tq::YT + 4 * kM,
                    sdesc_mnmajor(sK + st * NS * 4096 + (w & 1) * kW * 128, 4096), id_g, w > 0);
             mma_commit(&bars[B_XF]);
             mma_commit(&bars[B_YTFREE]);
             if (w & 1) mma_commit(&bars[B_KVE + st]);
           }
         } else {
-          const uint32_t id_c = idesc_f16(128, 112, E::kBf16, true) | (1u << 15);  // A, B MN-major
+          const uint32_t id_c = idesc_f16(128, 8 * kM, E::kBf16, true) | (1u << 15);  // A, B MN-major
           const uint32_t id_s = idesc_f16(128, 16, E::kBf16, true) | (1u << 15);
           for (int w = 0; ok && w <= WL; ++w) {
             for (int hh = 0; hh < 2 && ok; ++hh) {
@@ -463,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             for (int s = 0; s < 8; ++s) {
               const uint32_t ko = 2048 * s;
               mma_ss(tmem + tk::DVK, sdesc_mnmajor(sDO + ko, 16384),
-                     sdesc_mnmajor(sY + 16384 + ko + 96, 16384), id_s, s > 0);
+                     sdesc_mnmajor(sDS + ko + 64, 16384), id_s, s > 0);
               mma_ss(tmem + tk::DVK + 16, sdesc_mnmajor(sQ + ko, 16384),
                      sdesc_mnmajor(sDS + ko + 96, 16384), id_s, s > 0);
             }
@@ -911,7 +921,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 #pragma unroll
           for (int m = 0; m < kM; ++m)  // element 8 m + key: chunk m of the row
             sts64(sY + (m >> 3) * 16384 + sw128_offset(r, m & 7) + 8 * rg, y[m][0], y[m][1]);
-          sts64(sY + 16384 + sw128_offset(r, 6 + hh) + 8 * rg, E::pack(pr[0], pr[1]),
+          sts64(sDS + sw128_offset(r, 4 + hh) + 8 * rg, E::pack(pr[0], pr[1]),
                 E::pack(pr[2], pr[3]));
         }
         // gate-gradient prefix: group 0's keys precede group 1's in the half
@@ -941,8 +951,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             dsa0 = ds0;
             dsa1 = ds1;
           } else {
-            tmem_st2(lane_base + tq::YT + 56 + 2 * rg, dsa0, dsa1);
-            tmem_st2(lane_base + tq::YT + 60 + 2 * rg, ds0, ds1);
+            tmem_st2(lane_base + tq::YT + 4 * kM + 2 * rg, dsa0, dsa1);
+            tmem_st2(lane_base + tq::YT + 4 * kM + 4 + 2 * rg, ds0, ds1);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&bars[B_YB]);
@@ -1048,18 +1058,22 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 // double-buffered over windows.
 namespace k2 {
 constexpr int Q = 0, DO = 32768, AV = 65536;  // AV: 2 buffers of [NS][128][128 B]
-constexpr int YA = AV + 2 * 32768;            // Y half A | P (chunks 6-7 of slab 1)
-constexpr int YB = YA + 32768;                // Y half B | dS (chunks 6-7 of slab 1)
-constexpr int COEF = YB + 32768;
-constexpr int TH = COEF + kM * NPX * 4;
+constexpr int YA = AV + 2 * 32768;            // Y half A rows (16 terms x 8 keys)
+constexpr int YB = YA + 32768;                // Y half B rows
+constexpr int PD = YB + 32768;                // P (chunks 4-5) | dS (chunks 6-7) rows
+constexpr int COEF = PD + 16384;
+constexpr int TH = COEF + kMB * NPX * 4;
 constexpr int BAR = TH + NPX * 4;
 constexpr int SLOT = BAR + 16 * 8;
 constexpr int TOTAL = SLOT + 16;
 // RDY / YFREE per half: the rows write the next window's half A while the
 // tensor core still reads half B of the current one
-enum { B_Q = 0, B_RDY = 1, B_AVE = 3, B_YFREE = 5, B_CF = 7, B_CE = 9, B_DRAIN = 11 };
-// tensor memory: buffer b at 256 b: C^T half A, C^T half B, dV^T | dK_gate^T
-constexpr uint32_t C0 = 0, C1 = 112, DVK = 224, BUF = 256;
+enum { B_Q = 0, B_RDY = 1, B_AVE = 3, B_YFREE = 5, B_CF = 7, B_CE = 9, B_DRAIN = 11,
+       B_CE1 = 12 };
+// tensor memory: C^T of half A double-buffered (window parity b at 128 b),
+// C^T of half B single (its GEMM waits until the combine has read it), and
+// dV^T | dK_gate^T double-buffered
+constexpr uint32_t C0 = 0, C1 = 256, DVK = 384;
 }  // namespace k2
 
 template <typename T, int D>
@@ -1067,6 +1081,7 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
   using E = ElemTraits<T>;
   using namespace sm100;
   constexpr int NP = D / 2, DSL = D / 64, PW = NP / 2;
+  constexpr int kM = kMB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -1095,6 +1110,7 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
       mbar_init(&bars[k2::B_CE + i], 128);
     }
     mbar_init(&bars[k2::B_DRAIN], 1);
+    mbar_init(&bars[k2::B_CE1], 128);
     fence_mbar_init();
   }
   for (int i = tid; i < kM * NPX; i += kThreads) s_coef[i] = P.coef[i / NPX][i % NPX];
@@ -1119,6 +1135,7 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
   const uint32_t sQ = smem_u32(smem + k2::Q), sDO = smem_u32(smem + k2::DO);
   const uint32_t sAV = smem_u32(smem + k2::AV);
   const uint32_t sYA = smem_u32(smem + k2::YA), sYB = smem_u32(smem + k2::YB);
+  const uint32_t sPD = smem_u32(smem + k2::PD);
   const uint32_t s_th_u = smem_u32(s_th);
 
   if (warp >= 8 && warp < 12) {
@@ -1139,30 +1156,32 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
   } else if (warp == 9) {
     // ------------------------------------------------------------ UMMA
     if (lane == 0) {
-      const uint32_t id_c = idesc_f16(128, 112, E::kBf16, true) | (1u << 15);  // A, B MN-major
+      const uint32_t id_c = idesc_f16(128, 8 * kM, E::kBf16, true) | (1u << 15);  // A, B MN-major
       const uint32_t id_s = idesc_f16(128, 16, E::kBf16, true) | (1u << 15);
       bool ok = mbar_wait(&bars[k2::B_Q], 0, err, kErrQ);
       for (int w = 0; ok && w <= WL; ++w) {
         const int bf = w & 1;
-        const uint32_t acc = tmem + k2::BUF * bf;
         const uint32_t av = sAV + 32768 * bf;
-        // half A: C^T = v^T Y_A and dV^T = dO^T P (P of both halves rides in
-        // the Y_A rows); then half B: C^T = v^T Y_B and dK_gate^T = Q^T dS.
-        // K = the 128 query rows, 16 per step.
+        // half A: C^T = v^T Y_A and dV^T = dO^T P; then half B: C^T = v^T Y_B
+        // and dK_gate^T = Q^T dS.  K = the 128 query rows, 16 per step.
         for (int hh = 0; hh < 2 && ok; ++hh) {
           if (!(ok = mbar_wait(&bars[k2::B_RDY + hh], w & 1, err, kErrY))) break;
           if (hh == 0 && w >= 2 &&
               !(ok = mbar_wait(&bars[k2::B_CE + bf], ((w >> 1) - 1) & 1, err, kErrCEmpty)))
             break;
+          if (hh == 1 && w >= 1 &&
+              !(ok = mbar_wait(&bars[k2::B_CE1], (w - 1) & 1, err, kErrCEmpty)))
+            break;
           tc_fence_after();
           const uint32_t yr = hh ? sYB : sYA;
           const uint32_t other = hh ? sQ : sDO;
+          const uint32_t cacc = tmem + (hh ? k2::C1 : k2::C0 + 128 * bf);
 #pragma unroll 1
           for (int s = 0; s < 8; ++s) {
-            mma_ss(acc + (hh ? k2::C1 : k2::C0), sdesc_mnmajor(av + 2048 * s, 16384),
-                   sdesc_mnmajor(yr + 2048 * s, 16384), id_c, s > 0);
-            mma_ss(acc + k2::DVK + 16 * hh, sdesc_mnmajor(other + 2048 * s, 16384),
-                   sdesc_mnmajor(yr + 16384 + 2048 * s + 96, 16384), id_s, s > 0);
+            mma_ss(cacc, sdesc_mnmajor(av + 2048 * s, 16384), sdesc_mnmajor(yr + 2048 * s, 16384),
+                   id_c, s > 0);
+            mma_ss(tmem + k2::DVK + 32 * bf + 16 * hh, sdesc_mnmajor(other + 2048 * s, 16384),
+                   sdesc_mnmajor(sPD + 2048 * s + 64 + 32 * hh, 16384), id_s, s > 0);
           }
           if (hh == 1) {
             mma_commit(&bars[k2::B_CF + bf]);
@@ -1204,11 +1223,10 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
       const int bf = w & 1;
       if (!wwait(bars[k2::B_CF + bf], (w >> 1) & 1, err, kErrC)) break;
       tc_fence_after();
-      const uint32_t acc = lane_base + k2::BUF * bf;
       float dk[16], dv[16];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        const uint32_t creg = acc + (hh ? k2::C1 : k2::C0);
+        const uint32_t creg = lane_base + (hh ? k2::C1 : k2::C0 + 128 * bf);
         // even terms use this lane's column of C^T; odd terms the partner
         // component's (d ^ 1), whose coefficient for this lane is minus the
         // partner's own: each lane sums its odd terms with -cm and the sums
@@ -1234,13 +1252,17 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
             }
           }
         }
+        if (hh == 1) {  // the single half-B region is free for the next window
+          tc_fence_before();
+          mbar_arrive(&bars[k2::B_CE1]);
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) dk[8 * hh + j] = ev[j] + __shfl_xor_sync(0xffffffffu, od[j], 1);
       }
       {
         uint32_t g[2][16];
-        tmem_ld16(acc + k2::DVK, g[0]);       // dO^T P  (16 keys)
-        tmem_ld16(acc + k2::DVK + 16, g[1]);  // Q^T dS  (16 keys)
+        tmem_ld16(lane_base + k2::DVK + 32 * bf, g[0]);       // dO^T P  (16 keys)
+        tmem_ld16(lane_base + k2::DVK + 32 * bf + 16, g[1]);  // Q^T dS  (16 keys)
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -1285,7 +1307,7 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
         x.pd[hh] = ldg128_nc(hb + HB_PD + (qd * 128 + r) * 16);
         x.u[hh] = ldg64_nc(hb + HB_U + (qd * 128 + r) * 8);
       }
-      x.carry = __ldg(reinterpret_cast<const float*>(hb + HB_C + 4 * r));
+      x.carry = ldg32f_nc(hb + HB_C + 4 * r);
     };
     bool ok = wwait(bars[k2::B_Q], 0, err, kErrQ);
     Rec cur, nxt;
@@ -1329,8 +1351,8 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
           }
         }
       }
-      // ---- Y | P rows, then Y | dS rows, each once the previous window's
-      // GEMMs of that half are done with them
+      // ---- Y_A and P rows, then Y_B and dS rows, each once the previous
+      // window's GEMMs of that half are done with them
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         if (w >= 1 && !(ok = wwait(bars[k2::B_YFREE + hh], (w - 1) & 1, err, kErrY))) break;
@@ -1358,13 +1380,13 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
 #pragma unroll
         for (int m = 0; m < kM; ++m)
           sts64(yrow + (m >> 3) * 16384 + sw128_offset(r, m & 7) + 8 * rg, y[m][0], y[m][1]);
-        // P of both halves -> chunks 6, 7 of the Y | P rows; dS -> the Y | dS rows
+        // P of both halves -> chunks 4, 5 of the P | dS rows; dS -> chunks 6, 7
 #pragma unroll
         for (int q2 = 0; q2 < 2; ++q2) {
           if (hh == 0)
-            sts64(sYA + 16384 + sw128_offset(r, 6 + q2) + 8 * rg, cur.pd[q2].x, cur.pd[q2].y);
+            sts64(sPD + sw128_offset(r, 4 + q2) + 8 * rg, cur.pd[q2].x, cur.pd[q2].y);
           else
-            sts64(sYB + 16384 + sw128_offset(r, 6 + q2) + 8 * rg, cur.pd[q2].z, cur.pd[q2].w);
+            sts64(sPD + sw128_offset(r, 6 + q2) + 8 * rg, cur.pd[q2].z, cur.pd[q2].w);
         }
         fence_async_smem();
         mbar_arrive(&bars[k2::B_RDY + hh]);
@@ -1384,9 +1406,9 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
 
 // ------------------------------------------------------------------ host
 // K^(m) buffer layout and count; returns the dynamic shared memory needed
-template <int MODE>
+template <int MODE, int KM>
 static int plan(Params& p) {
-  using L = SmemTail<MODE>;
+  using L = SmemTail<MODE, KM>;
   int off = 0, rows = 0;
   for (int s = 0; s < NS; ++s) {
     p.b_slab_off[s] = off;
@@ -1400,19 +1422,31 @@ static int plan(Params& p) {
   return p.bop + 2 * p.nb * p.b_buf_bytes + 1024;
 }
 
+// Chebyshev terms of each backward kernel.  The derivative of the truncated
+// series converges one order slower than its value, so the backward keeps 16
+// terms where shared memory allows; the recompute dK kernel at head dim 128
+// holds 14 (its K^(m), Y and P | dS buffers do not fit with 16).
+template <int D, int MODE>
+struct Terms {
+  static constexpr int value = (MODE == MODE_DK && D == 128) ? 14 : kMB;
+};
+
 template <typename T, int D, int MODE>
-static cudaError_t launch_mode(Params& p, bool bias, int S, int nbh, cudaStream_t st) {
-  const int smem = plan<MODE>(p);
+static cudaError_t launch_mode(Params& p, bool bias, int S, int nbh, cudaStream_t st,
+                               float theta, float sm_scale) {
+  constexpr int KM = Terms<D, MODE>::value;
+  tcx::fill_coefficients<KM>(p.coef, p.nrow, D, theta, sm_scale);
+  const int smem = plan<MODE, KM>(p);
   if (smem > kSmemLimit) return cudaErrorInvalidValue;
   dim3 grid((S + kBM - 1) / kBM, nbh);
   cudaError_t e;
   if (bias) {
-    auto kern = bwd_kernel<T, D, MODE, true>;
+    auto kern = bwd_kernel<T, D, MODE, true, KM>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return e;
     kern<<<grid, kThreads, smem, st>>>(p);
   } else {
-    auto kern = bwd_kernel<T, D, MODE, false>;
+    auto kern = bwd_kernel<T, D, MODE, false, KM>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return e;
     kern<<<grid, kThreads, smem, st>>>(p);
@@ -1421,7 +1455,9 @@ static cudaError_t launch_mode(Params& p, bool bias, int S, int nbh, cudaStream_
 }
 
 template <typename T, int D>
-static cudaError_t launch_dk2(Params& p, int S, int nbh, cudaStream_t st) {
+static cudaError_t launch_dk2(Params& p, int S, int nbh, cudaStream_t st, float theta,
+                              float sm_scale) {
+  tcx::fill_coefficients<kMB>(p.coef, p.nrow, D, theta, sm_scale);
   const int smem = k2::TOTAL + 1024;
   dim3 grid((S + kBM - 1) / kBM, nbh);
   auto kern = dk2_kernel<T, D>;
@@ -1440,7 +1476,8 @@ static int64_t blocks_per_bh(int S) {
 
 template <typename T, int D>
 static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* handoff,
-                              size_t handoff_bytes, cudaStream_t st) {
+                              size_t handoff_bytes, cudaStream_t st, float theta,
+                              float sm_scale) {
   const int64_t per_bh = blocks_per_bh(S) * kHB;
   int chunk = handoff ? (int)std::min<int64_t>(BH, (int64_t)(handoff_bytes / per_bh)) : 0;
   if (chunk < std::min(BH, 16)) chunk = 0;  // too few (b, h) per launch: recompute instead
@@ -1448,8 +1485,8 @@ static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* hand
   if (chunk == 0) {
     p.handoff = nullptr;
     p.bh0 = 0;
-    e = launch_mode<T, D, MODE_DQ>(p, bias, S, BH, st);
-    if (e == cudaSuccess) e = launch_mode<T, D, MODE_DK>(p, bias, S, BH, st);
+    e = launch_mode<T, D, MODE_DQ>(p, bias, S, BH, st, theta, sm_scale);
+    if (e == cudaSuccess) e = launch_mode<T, D, MODE_DK>(p, bias, S, BH, st, theta, sm_scale);
     return e;
   }
   p.handoff = handoff;
@@ -1457,8 +1494,8 @@ static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* hand
   for (int bh0 = 0; bh0 < BH && e == cudaSuccess; bh0 += chunk) {
     p.bh0 = bh0;
     const int nbh = std::min(chunk, BH - bh0);
-    e = launch_mode<T, D, MODE_DQ>(p, bias, S, nbh, st);
-    if (e == cudaSuccess) e = launch_dk2<T, D>(p, S, nbh, st);
+    e = launch_mode<T, D, MODE_DQ>(p, bias, S, nbh, st, theta, sm_scale);
+    if (e == cudaSuccess) e = launch_dk2<T, D>(p, S, nbh, st, theta, sm_scale);
   }
   return e;
 }
@@ -1479,10 +1516,18 @@ bool tc_bwd_supported(const BwdArgs& a, int dtype) {
       !rows16(a.dout, a.dos) || !rows16(a.dq, a.dqs))
     return false;
   // small theta keeps more Chebyshev terms: the K^(m) buffers must still fit
-  tcb::Params p;
-  tcx::fill_coefficients(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
-  if (tcb::plan<tcb::MODE_DQ>(p) > tcx::kSmemLimit || tcb::plan<tcb::MODE_DK>(p) > tcx::kSmemLimit)
-    return false;
+  using namespace tcb;
+  Params p;
+  constexpr int kDK128 = Terms<128, MODE_DK>::value, kDK64 = Terms<64, MODE_DK>::value;
+  tcx::fill_coefficients<kMB>(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
+  if (plan<MODE_DQ, kMB>(p) > tcx::kSmemLimit) return false;
+  if (a.D == 128) {
+    tcx::fill_coefficients<kDK128>(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
+    if (plan<MODE_DK, kDK128>(p) > tcx::kSmemLimit) return false;
+  } else {
+    tcx::fill_coefficients<kDK64>(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
+    if (plan<MODE_DK, kDK64>(p) > tcx::kSmemLimit) return false;
+  }
   return tcx::get_encoder() != nullptr;
 }
 
@@ -1515,15 +1560,19 @@ cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* ha
   p.bias_rs = a.bias_rs;
   for (int i = 0; i < 3; ++i) p.dqs[i] = a.dqs[i];
   p.B = a.B; p.H = a.H; p.Hkv = a.Hkv; p.S = a.S;
-  tcx::fill_coefficients(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
   const bool bias = a.bias != nullptr;
   uint8_t* hp = static_cast<uint8_t*>(handoff);
   const int BH = a.B * a.H;
   if (dtype == COROPE_DTYPE_BF16)
-    return a.D == 64 ? launch_all<__nv_bfloat16, 64>(p, bias, BH, a.S, hp, handoff_bytes, st)
-                     : launch_all<__nv_bfloat16, 128>(p, bias, BH, a.S, hp, handoff_bytes, st);
-  return a.D == 64 ? launch_all<__half, 64>(p, bias, BH, a.S, hp, handoff_bytes, st)
-                   : launch_all<__half, 128>(p, bias, BH, a.S, hp, handoff_bytes, st);
+    return a.D == 64
+               ? launch_all<__nv_bfloat16, 64>(p, bias, BH, a.S, hp, handoff_bytes, st, a.theta,
+                                                a.sm_scale)
+               : launch_all<__nv_bfloat16, 128>(p, bias, BH, a.S, hp, handoff_bytes, st, a.theta,
+                                                 a.sm_scale);
+  return a.D == 64 ? launch_all<__half, 64>(p, bias, BH, a.S, hp, handoff_bytes, st, a.theta,
+                                            a.sm_scale)
+                   : launch_all<__half, 128>(p, bias, BH, a.S, hp, handoff_bytes, st, a.theta,
+                                             a.sm_scale);
 }
 
 }  // namespace corope

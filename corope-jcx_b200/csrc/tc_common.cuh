@@ -95,13 +95,14 @@ inline double bessel_j(int m, double x) {
   return sum;
 }
 
-// Chebyshev coefficients eps_m J_m(c0 theta_p) * sm_scale * log2(e) and the
-// pruned K extent of each term: nrow[s] = rows of the K^(m) operand that
+// Chebyshev coefficients eps_m J_m(c0 theta_p) * sm_scale * log2(e) of the
+// first KM terms and the pruned K extent of each term: nrow[s] = rows of the K^(m) operand that
 // K-step s (16 head dims) reads (8 keys per term, rounded to 16 rows).
+template <int KM = kM>
 inline void fill_coefficients(float (*coef)[64], int* nrow, int D, float theta, float sm_scale) {
   const int NP = D / 2;
-  int kd[kM];
-  for (int m = 0; m < kM; ++m) {
+  int kd[KM];
+  for (int m = 0; m < KM; ++m) {
     int need = 0;
     for (int q = 0; q < NP; ++q) {
       const double th = 1.0 / std::pow((double)theta, (double)(2 * q) / (double)D);
@@ -112,10 +113,10 @@ inline void fill_coefficients(float (*coef)[64], int* nrow, int D, float theta, 
     for (int q = NP; q < 64; ++q) coef[m][q] = 0.f;
     kd[m] = std::max(1, (2 * need + 15) / 16);
   }
-  for (int m = kM - 2; m >= 0; --m) kd[m] = std::max(kd[m], kd[m + 1]);
+  for (int m = KM - 2; m >= 0; --m) kd[m] = std::max(kd[m], kd[m + 1]);
   for (int s = 0; s < 8; ++s) {
     int nm = 0;
-    for (int m = 0; m < kM; ++m) nm += kd[m] > s;
+    for (int m = 0; m < KM; ++m) nm += kd[m] > s;
     nm = (nm + 1) & ~1;
     nrow[s] = (s < D / 16) ? 8 * nm : 0;
   }

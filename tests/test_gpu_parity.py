@@ -322,14 +322,15 @@ def test_tensor_backward_s2048_d128():
         assert rel_l2(mine, r) < REL_L2, name
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("mode", ["full", "chunked", "min"])
-def test_tensor_backward_workspace_paths(mode):
+def test_tensor_backward_workspace_paths(mode, D):
     """The three ways the tensor-core backward uses its workspace give the
     oracle's gradients: a full hand-off region (the dK kernel reads the dQ
     kernel's per-pair results), a region for 17 of the 24 (b, h) slices
     (two rounds of both kernels), and the minimum (the dK kernel recomputes)."""
     from CoROPE import _lib
-    B, H, S, D = 2, 12, 300, 128
+    B, H, S = 2, 12, 300
     (q, k, v, do), cpu = inputs(B, H, S, D, 57, torch.bfloat16)
     sm = 1 / math.sqrt(D)
     saved, o = co_rope_forward(q, k, v, sm, algo="tensor")
