@@ -199,11 +199,38 @@ def fwd(q, k, v, o, m, l, a, lse, sm_scale, theta, bias=None, algo="auto", theta
     _check(rc, "corope_mqa_fwd" if mqa else "corope_fwd")
 
 
+def auto_workspace_bytes(lib, p, device):
+    """The workspace "auto" gives corope_bwd: the full size when it fits in a
+    quarter of the memory the device and torch's cache have free, else the
+    minimum plus as many whole (b, h) hand-off slices as fit there (long
+    sequences: the hand-off region grows with S^2, 5.5 GB per (b, h) at
+    S=32768; from 2 slices on a launch already has 512 CTAs), else the
+    minimum.  A quarter leaves the caller's own tensors room and keeps the
+    request the same from call to call, so torch's cache can serve it again."""
+    full = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
+    least = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
+    free, _ = torch.cuda.mem_get_info(device)
+    budget = (free + torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)) // 4
+    return fit_workspace(full, least, p.batch * p.heads, budget)
+
+
+def fit_workspace(full, least, units, budget):
+    """Largest of full / least + k whole hand-off slices / least within
+    `budget` bytes (least even when it does not fit: the call then fails in
+    the allocator, as the caller's own allocation would)."""
+    if full <= budget or full == least:
+        return full
+    per = (full - least) // units  # >= one slice's bytes (the region is 256-aligned)
+    slices = max(0, (budget - least) // per) if per > 0 else 0
+    return least + min(slices, units) * per
+
+
 def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="auto",
-        thetas=None, workspace="full"):
+        thetas=None, workspace="auto"):
     """Launch corope_bwd on the current stream of q with a torch-allocated
-    workspace: "full" (corope_bwd_workspace_bytes, the fastest), "min"
-    (corope_bwd_min_workspace_bytes) or a byte count in between."""
+    workspace: "auto" (the full size when it fits in free memory, else as many
+    hand-off slices as fit), "full" (corope_bwd_workspace_bytes, the fastest),
+    "min" (corope_bwd_min_workspace_bytes) or a byte count in between."""
     lib = load_library()
     B, H, S, D = q.shape
     p = BwdParams()
@@ -222,7 +249,9 @@ def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="a
     p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, k.shape[1], S, D
     p.sm_scale, p.theta = float(sm_scale), float(theta)
     p.causal, p.dtype, p.algo = 1, _dtype_code(q), algo_code(algo)
-    if workspace == "full":
+    if workspace == "auto":
+        nbytes = auto_workspace_bytes(lib, p, q.device)
+    elif workspace == "full":
         nbytes = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
     elif workspace == "min":
         nbytes = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))

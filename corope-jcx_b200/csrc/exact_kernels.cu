@@ -78,7 +78,10 @@ exact_fwd_kernel(FwdArgs args) {
     qp[i] = (t < S) ? load_pair<T>(qb, (int64_t)t * args.qs[2] + 2 * p) : make_float2(0.f, 0.f);
     op[i] = make_float2(0.f, 0.f);
   }
-  float m_run = -1e30f, l_run = 0.f, a_run = 0.f;
+  float m_run = -1e30f, l_run = 0.f;
+  // suffix gate sum, compensated (Kahan; a_run - a_cmp is the sum to ~1 ulp):
+  // a plain fp32 running sum over tens of thousands of keys drifts by ~1e-2
+  float a_run = 0.f, a_cmp = 0.f;
   float lg[CH];
   const float sm = args.sm_scale;
 
@@ -104,12 +107,13 @@ exact_fwd_kernel(FwdArgs args) {
         }
         g = group_sum<TPR>(g);
         const float z = valid ? sigmoidf_fast(g) : 0.f;
+        const float a_tj = a_run - a_cmp;
         float acc = 0.f;
 #pragma unroll
         for (int i = 0; i < NP; ++i) {
           float2 kk = kr[i * TPR + sub];
           float s, c;
-          sincos_reduced(a_run * th_s[i * TPR + sub], &s, &c);
+          sincos_reduced(a_tj * th_s[i * TPR + sub], &s, &c);
           float Cp = fmaf(qp[i].x, kk.x, qp[i].y * kk.y);
           float Sp = fmaf(qp[i].x, kk.y, -qp[i].y * kk.x);
           acc = fmaf(c, Cp, fmaf(s, Sp, acc));
@@ -118,7 +122,12 @@ exact_fwd_kernel(FwdArgs args) {
         float logit = acc * sm;
         if (HAS_BIAS && valid) logit += args.bias[(int64_t)t * args.bias_rs + j];
         lg[u] = valid ? logit : -INFINITY;
-        a_run += z;
+        {
+          const float y = z - a_cmp;
+          const float s2 = a_run + y;
+          a_cmp = (s2 - a_run) - y;
+          a_run = s2;
+        }
       }
       // online softmax over the CH keys just scored
       float mx = m_run;
@@ -157,7 +166,7 @@ exact_fwd_kernel(FwdArgs args) {
       const int64_t r = ((int64_t)b * args.H + h) * S + t;
       if (args.m) args.m[r] = m_run;
       if (args.l) args.l[r] = l_run;
-      if (args.a) args.a[r] = a_run;
+      if (args.a) args.a[r] = a_run - a_cmp;
       if (args.lse) args.lse[r] = m_run + logf(l_run);
     }
   }
@@ -249,7 +258,8 @@ exact_bwd_kernel(BwdArgs args) {
   const float A_t = (t < S) ? args.a[rix] : 0.f;
   const float lse_t = (t < S) ? args.lse[rix] : 0.f;
   const float dlt_t = (t < S) ? args.delta[rix] : 0.f;
-  float c_run = 0.f, da_run = 0.f;
+  // gate prefix, compensated (Kahan; c_run - c_cmp is the prefix to ~1 ulp)
+  float c_run = 0.f, c_cmp = 0.f, da_run = 0.f;
 
   // phase-2 mapping
   const int kj = threadIdx.x / TPK, sub2 = threadIdx.x % TPK;
@@ -277,8 +287,13 @@ exact_bwd_kernel(BwdArgs args) {
       }
       g = group_sum<TPR>(g);
       const float z = valid ? sigmoidf_fast(g) : 0.f;
-      c_run += z;
-      const float a = valid ? (A_t - c_run) : 0.f;
+      {
+        const float y = z - c_cmp;
+        const float s2 = c_run + y;
+        c_cmp = (s2 - c_run) - y;
+        c_run = s2;
+      }
+      const float a = valid ? ((A_t - c_run) + c_cmp) : 0.f;
       float cs[NP], sn[NP];
       float acc = 0.f, dacc = 0.f, dpp = 0.f;
 #pragma unroll

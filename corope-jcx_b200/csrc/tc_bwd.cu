@@ -677,7 +677,11 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     const float delta = P.delta[ri];
     const uint32_t s_xch = smem_u32(smem + L::XCH);
     const uint32_t s_cs = sY + (rg * 128 + r) * 16;  // dQ: staged (cos, sin), chunk q at + 4096 q
-    float base = 0.f;    // gate prefix through the current window
+    // gate prefix through the current window, compensated (Kahan): the prefix
+    // reaches ~S/2, where fp32 steps are 2^-10 at S = 32768, and a plain
+    // running sum over S/16 windows drifts by ~1e-2 -- an angle error of that
+    // size in the fastest rotation.  base - base_c is the prefix to ~1 ulp.
+    float base = 0.f, base_c = 0.f;
     float carry = 0.f;   // gate sum of the keys after the current window
     float da_run = 0.f;  // gate-gradient prefix before the current half
     // this group's keys of the window: i -> key 8 (i >> 2) + 4 rg + (i & 3)
@@ -722,8 +726,13 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         dpo[i] = __uint_as_float(d4a[i]);
         dpo[4 + i] = __uint_as_float(d4b[i]);
       }
-      base += zsum;
-      carry = A_t - base;
+      {
+        const float y = zsum - base_c;
+        const float s2 = base + y;
+        base_c = (s2 - base) - y;
+        base = s2;
+      }
+      carry = (A_t - base) + base_c;
       return true;
     };
 
@@ -1467,6 +1476,14 @@ static cudaError_t launch_dk2(Params& p, int S, int nbh, cudaStream_t st, float 
   return cudaGetLastError();
 }
 
+// Fewest (b, h) slices per launch of the hand-off pair: 16, or fewer when
+// they already make 512 CTAs (about 3.5 waves of 148 SMs; long sequences),
+// or all of them.
+static int min_slices(int BH, int S) {
+  const int qtiles = (S + kBM - 1) / kBM;
+  return std::min(std::min(BH, 16), (512 + qtiles - 1) / qtiles);
+}
+
 // hand-off blocks of one (b, h): one per (query tile, window)
 static int64_t blocks_per_bh(int S) {
   int64_t n = 0;
@@ -1480,7 +1497,7 @@ static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* hand
                               float sm_scale) {
   const int64_t per_bh = blocks_per_bh(S) * kHB;
   int chunk = handoff ? (int)std::min<int64_t>(BH, (int64_t)(handoff_bytes / per_bh)) : 0;
-  if (chunk < std::min(BH, 16)) chunk = 0;  // too few (b, h) per launch: recompute instead
+  if (chunk < min_slices(BH, S)) chunk = 0;  // too few CTAs per launch: recompute instead
   cudaError_t e = cudaSuccess;
   if (chunk == 0) {
     p.handoff = nullptr;
@@ -1533,9 +1550,9 @@ bool tc_bwd_supported(const BwdArgs& a, int dtype) {
 
 // Launches the dQ and dK kernels; the caller runs the delta/lse pre-kernel
 // before and the fp32 -> dtype conversion of dk/dv after.  With a hand-off
-// region large enough for at least min(B H, 16) (b, h) slices the dK launch
-// reads the dQ launch's per-pair results (slice by slice through the region);
-// otherwise it recomputes them.
+// region large enough for min_slices (b, h) slices the dK launch reads the
+// dQ launch's per-pair results (slice by slice through the region); otherwise
+// it recomputes them.
 cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* handoff,
                           size_t handoff_bytes) {
   using namespace tcb;

@@ -405,7 +405,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
     const int t = q0 + r;
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const uint32_t s_xch = smem_u32(smem + L::XCH);
-    float carry = 0.f;                     // gate sum of keys after the window
+    // gate sum of keys after the window, compensated (Kahan): it reaches ~S/2,
+    // where fp32 steps are 2^-10 at S = 32768, and a plain running sum over
+    // S/16 windows drifts by ~1e-2 (an angle error of that size in the fastest
+    // rotation).  carry - carry_c is the sum to ~1 ulp.
+    float carry = 0.f, carry_c = 0.f;
     float m_used = -1e30f, m_true = -INFINITY;
     float lsum = 0.f;                      // this group's keys
     bool ok = wwait(bars[B_Q], 0, err, kErrQ);
@@ -510,10 +514,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         const int kk = 8 * (i >> 2) + (i & 3);
         uo[i] = rg ? uu[kk + 4] : uu[kk];
       }
-      const float carry_next = carry + acc;
+      const float y = acc - carry_c;
+      const float carry_next = carry + y;
+      const float carry_c_next = (carry_next - carry) - y;
       // A operand of the next window (its buffer was last read by G(w+1),
       // which completed before this row group loaded G(w+1))
-      if (w > 0) build_a(carry_next, ((w - 1) & 1) ? L::T_AV1 : L::T_AV0);
+      if (w > 0) build_a(carry_next - carry_c_next, ((w - 1) & 1) ? L::T_AV1 : L::T_AV0);
       float lg[8];
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
@@ -581,6 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       tc_fence_before();
       mbar_arrive(&bars[B_P]);
       carry = carry_next;
+      carry_c = carry_c_next;
     }
     // epilogue: row sum of both groups, then this group's output columns
     if (ok) ok = wwait(bars[B_O], W0 & 1, err, kErrO);
@@ -614,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         const float Lv = ltot * exp2f(m_used - m_true);
         if (P.m) P.m[ri] = M;
         if (P.l) P.l[ri] = Lv;
-        if (P.a) P.a[ri] = carry;
+        if (P.a) P.a[ri] = carry - carry_c;
         if (P.lse) P.lse[ri] = M + logf(Lv);
       }
     }

@@ -261,6 +261,54 @@ def backward_dense(q, k, v, do, sm_scale, theta=10000.0, bias=None, row_chunk=64
     return dq, dk, dv
 
 
+def backward_rows(q, k, v, do, rows, sm_scale, theta=10000.0, row_chunk=16):
+    """The part of ``backward_dense`` that query rows ``rows`` of one (b, h)
+    slice contribute, for long sequences.  q, k, v, do: [S, D].
+
+    Row t only involves keys 0..t, so this costs O(T S D).  Returns
+    ``dq`` of those rows [T, D] (complete: a row's dq depends on that row
+    alone) and their summed contributions ``dk_part``, ``dv_part`` [S, D] to
+    every key.  The gradient of key j is complete once every row t >= j is
+    among ``rows``: with rows = S-n..S-1 the last n keys' dk, dv are exact."""
+    S, D = q.shape
+    th = thetas_for(D, theta, q.dtype)
+    rows = rows.to(torch.long)
+    dq = torch.zeros(len(rows), D, dtype=q.dtype)
+    dk = torch.zeros(S, D, dtype=q.dtype)
+    dv = torch.zeros(S, D, dtype=q.dtype)
+    for r0 in range(0, len(rows), row_chunk):
+        rr = rows[r0:r0 + row_chunk]
+        n = int(rr.max()) + 1                             # keys any of these rows sees
+        kk, vv = k[:n], v[:n]
+        qt, dot = q[rr], do[rr]                           # [T, D]
+        cm = torch.arange(n)[None, :] <= rr[:, None]      # causal mask [T, n]
+        z = torch.sigmoid(qt @ kk.T).masked_fill(~cm, 0)
+        c = torch.cumsum(z, 1)
+        ctt = c.gather(1, rr[:, None])                    # c[t, t]
+        phi = ((ctt - c).masked_fill(~cm, 0))[:, :, None] * th   # [T, n, P]
+        cs, sn = torch.cos(phi), torch.sin(phi)
+        qe, qo = qt[:, None, 0::2], qt[:, None, 1::2]
+        ke, ko = kk[None, :, 0::2], kk[None, :, 1::2]
+        Cp = qe * ke + qo * ko
+        Sp = qe * ko - qo * ke
+        lg = ((cs * Cp + sn * Sp).sum(-1) * sm_scale).masked_fill(~cm, float("-inf"))
+        P = torch.softmax(lg, 1)
+        o = P @ vv
+        dv[:n] += P.T @ dot
+        dl = P * (dot @ vv.T - (dot * o).sum(-1, keepdim=True))
+        da = (dl * sm_scale * (th * (cs * Sp - sn * Cp)).sum(-1)).masked_fill(~cm, 0)
+        dz = torch.cumsum(da, 1) - da                     # sum_{j<i} da_tj
+        ds = (dz * z * (1 - z)).masked_fill(~cm, 0)
+        w = (dl * sm_scale)[:, :, None]
+        dq[r0:r0 + len(rr), 0::2] = (w * (ke * cs + ko * sn)).sum(1)
+        dq[r0:r0 + len(rr), 1::2] = (w * (-ke * sn + ko * cs)).sum(1)
+        dq[r0:r0 + len(rr)] += ds @ kk
+        dk[:n, 0::2] += (w * (qe * cs - qo * sn)).sum(0)
+        dk[:n, 1::2] += (w * (qe * sn + qo * cs)).sum(0)
+        dk[:n] += ds.T @ qt
+    return dq, dk, dv
+
+
 def autograd_reference(q, k, v, do, sm_scale, theta=10000.0, bias=None):
     """Gradients by autograd through ``forward_dense`` (small shapes only)."""
     qq = q.detach().clone().requires_grad_(True)

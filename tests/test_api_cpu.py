@@ -67,3 +67,19 @@ def test_theta_table_matches_reference_expression():
     ref = 1.0 / (theta ** (torch.arange(0, D, 2).float() / D))
     assert torch.equal(_lib.theta_table(D, theta, "cpu"), ref)
     assert _lib.default_scale(64, None) == pytest.approx(1 / math.sqrt(64))
+
+
+def test_auto_workspace_fits_whole_slices():
+    """The "auto" backward workspace: the full hand-off region when it fits,
+    else the minimum plus whole (b, h) slices (long sequences), else the
+    minimum."""
+    from CoROPE._lib import fit_workspace
+    least, per, units = 1000, 256 * 40, 8
+    full = least + per * units
+    assert fit_workspace(full, least, units, budget=full) == full
+    assert fit_workspace(full, least, units, budget=10 ** 12) == full
+    assert fit_workspace(full, least, units, budget=least + 3 * per + 5) == least + 3 * per
+    assert fit_workspace(full, least, units, budget=least + per - 1) == least
+    assert fit_workspace(full, least, units, budget=0) == least
+    # no hand-off region at all (exact path, or head dims without one)
+    assert fit_workspace(least, least, units, budget=0) == least

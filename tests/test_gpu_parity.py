@@ -359,6 +359,44 @@ def test_tensor_backward_workspace_paths(mode, D):
         assert rel_l2(mine, r) < REL_L2, name
 
 
+@pytest.mark.parametrize("mode", ["auto", "two-slices", "min"])
+def test_long_context_s32768(mode):
+    """The long-context shape of one GPU's share (S=32768, D=128 bf16, theta
+    5e5, seed 4) on 4 heads: forward rows and the backward against the
+    per-row oracle -- dq of sampled rows, dk and dv of the last 32 keys (whose
+    contributing rows are all sampled) -- with the hand-off region in full
+    (22 GB), two (b, h) slices at a time, or not at all."""
+    from CoROPE import _lib
+    B, H, S, D, theta = 1, 4, 32768, 128, 5e5
+    (q, k, v, do), cpu = inputs(B, H, S, D, 4, torch.bfloat16)
+    sm = 1 / math.sqrt(D)
+    saved, o = co_rope_forward(q, k, v, sm, theta=theta, algo="tensor")
+    q_, k_, v_, o_, m_, l_, a_ = saved
+    p = _lib.BwdParams()
+    p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, H, S, D
+    p.dtype, p.algo = _lib._dtype_code(q), _lib.algo_code("tensor")
+    lib = _lib.load_library()
+    lo = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
+    hi = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
+    ws = {"auto": "auto", "min": "min", "two-slices": lo + 2 * ((hi - lo) // (B * H))}[mode]
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    _lib.bwd(q_, k_, v_, o_, do, m_, l_, a_, dq, dk, dv, sm, theta, algo="tensor", workspace=ws)
+    torch.cuda.synchronize()
+    assert _lib.take_device_error() == 0
+    n = 32
+    rows = torch.cat([torch.tensor([0, 1, 777, 9000, 20000]), torch.arange(S - n, S)])
+    for h in (0, 3):
+        if mode == "auto":
+            check_rows(o, m_, a_, cpu, 0, h, rows, sm, theta)
+        rq, rk, rv = O.backward_rows(cpu[0][0, h], cpu[1][0, h], cpu[2][0, h], cpu[3][0, h],
+                                     rows, sm, theta)
+        for name, mine, r in (("dq", dq[0, h, rows], rq), ("dk", dk[0, h, S - n:], rk[S - n:]),
+                              ("dv", dv[0, h, S - n:], rv[S - n:])):
+            assert torch.isfinite(mine).all(), name
+            assert maxabs(mine, r) < G_MAXABS, name
+            assert rel_l2(mine, r) < REL_L2, name
+
+
 @pytest.mark.parametrize("algo", ["exact", "tensor"])
 @pytest.mark.parametrize("D", [64, 128])
 def test_backward_with_contextual_bias(algo, D):

@@ -69,6 +69,23 @@ def test_forward_rows_equals_dense():
     assert (a - r["a"][1, 0, rows]).abs().max() < 1e-6
 
 
+def test_backward_rows_equals_dense_fp64():
+    """Per-row backward (long sequences): dq of the sampled rows, and dk, dv of
+    the keys whose every contributing row is sampled, equal backward_dense."""
+    g = torch.Generator().manual_seed(5)
+    S, D = 40, 8
+    q, k, v, do = (torch.randn(1, 1, S, D, generator=g, dtype=torch.float64) for _ in range(4))
+    rq, rk, rv = O.backward_dense(q, k, v, do, 0.35, 500.0)
+    rows = torch.arange(S - 6, S)
+    dq, dk, dv = O.backward_rows(q[0, 0], k[0, 0], v[0, 0], do[0, 0], rows, 0.35, 500.0)
+    assert (dq - rq[0, 0, rows]).abs().max() < 1e-12
+    assert (dk[S - 6:] - rk[0, 0, S - 6:]).abs().max() < 1e-12
+    assert (dv[S - 6:] - rv[0, 0, S - 6:]).abs().max() < 1e-12
+    every = torch.arange(S)
+    dq, dk, dv = O.backward_rows(q[0, 0], k[0, 0], v[0, 0], do[0, 0], every, 0.35, 500.0)
+    assert (dk - rk[0, 0]).abs().max() < 1e-12 and (dv - rv[0, 0]).abs().max() < 1e-12
+
+
 def test_planted_error_is_detected():
     """A mistake planted in the oracle's inputs (one flipped gate sign) must
     move the output well past the tolerances used by the GPU tests."""
