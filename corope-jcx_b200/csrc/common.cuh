@@ -42,6 +42,20 @@ __device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
   __sincosf(r, s, c);
 }
 
+// Below this many radians MUFU's own range reduction keeps sin/cos within
+// 5.5e-4 of the fp32 angle's (measured maximum up to 4096 rad), under half a
+// bf16 ulp of a unit-scale rotated value: the tensor-core kernels, whose
+// rotated operands are rounded to 16-bit floats, skip the explicit reduction
+// when a whole warp's angles are below it.
+constexpr float kMufuReduceMax = 4096.f;
+
+// Largest |theta_p| of a frequency table of n entries in shared memory.
+__device__ __forceinline__ float theta_max(const float* th, int n) {
+  float m = 0.f;
+  for (int p = 0; p < n; ++p) m = fmaxf(m, fabsf(th[p]));
+  return m;
+}
+
 // Reduce x (radians) to r in [-pi, pi]: k = nearest integer to x / 2pi by
 // the round-to-nearest of adding 1.5 * 2^23 (|x| / 2pi < 2^22), then the same
 // two-constant Cody-Waite subtraction as sincos_reduced.  FMA pipe only.

@@ -739,8 +739,10 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     // this group's half of the A operand v = R((carry + c0) theta) q_t:
     // dQ launch -> shared memory (and the (cos, sin) staging); dK launch ->
     // tensor memory (the G GEMM's A; copied to shared memory later for C)
+    const float th_max = theta_max(s_th, NP);
     auto build_a = [&]() {
       const float bse = carry + kC0;
+      const bool mufu_reduce = __all_sync(0xffffffffu, bse * th_max < kMufuReduceMax);
 #pragma unroll 1
       for (int g = 0; g < PW / 16; ++g) {
         uint4 qv[4];
@@ -753,8 +755,13 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           th[4 * cc] = t4.x; th[4 * cc + 1] = t4.y; th[4 * cc + 2] = t4.z; th[4 * cc + 3] = t4.w;
         }
         float rr[16], sn[16], cs[16];
+        if (mufu_reduce) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) rr[i] = reduce_2pi(bse * th[i]);
+          for (int i = 0; i < 16; ++i) rr[i] = bse * th[i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) rr[i] = reduce_2pi(bse * th[i]);
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) __sincosf(rr[i], &sn[i], &cs[i]);
         uint32_t o[16];
@@ -1318,6 +1325,7 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
       }
       x.carry = ldg32f_nc(hb + HB_C + 4 * r);
     };
+    const float th_max = theta_max(s_th, NP);
     bool ok = wwait(bars[k2::B_Q], 0, err, kErrQ);
     Rec cur, nxt;
     load(0, cur);
@@ -1328,6 +1336,7 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
         break;
       {
         const float bse = cur.carry + kC0;
+        const bool mufu_reduce = __all_sync(0xffffffffu, bse * th_max < kMufuReduceMax);
         const uint32_t av = sAV + 32768 * (w & 1);
 #pragma unroll 1
         for (int g = 0; g < PW / 16; ++g) {
@@ -1341,8 +1350,13 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
             th[4 * cc] = t4.x; th[4 * cc + 1] = t4.y; th[4 * cc + 2] = t4.z; th[4 * cc + 3] = t4.w;
           }
           float rr[16], sn[16], cs[16];
+          if (mufu_reduce) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) rr[i] = reduce_2pi(bse * th[i]);
+            for (int i = 0; i < 16; ++i) rr[i] = bse * th[i];
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) rr[i] = reduce_2pi(bse * th[i]);
+          }
 #pragma unroll
           for (int i = 0; i < 16; ++i) __sincosf(rr[i], &sn[i], &cs[i]);
 #pragma unroll

@@ -417,8 +417,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
     // This group's half of the A operand of one window, v = R((carry + c0)
     // theta) q_t, into tensor memory (angles reduced to [-pi, pi] on the FMA
     // pipe, sine/cosine on MUFU).
+    const float th_max = theta_max(s_th, NP);
     auto build_a = [&](float cw, uint32_t av_col) {
       const float base = cw + kC0;
+      const bool mufu_reduce = __all_sync(0xffffffffu, base * th_max < kMufuReduceMax);
 #pragma unroll 1
       for (int g = 0; g < NP / 32; ++g) {
         // 16 independent pairs, advanced stage by stage (instruction-level
@@ -434,8 +436,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
           th[4 * cc] = t4.x; th[4 * cc + 1] = t4.y; th[4 * cc + 2] = t4.z; th[4 * cc + 3] = t4.w;
         }
         float rr[16], sn[16], cs[16];
+        if (mufu_reduce) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) rr[i] = reduce_2pi(base * th[i]);
+          for (int i = 0; i < 16; ++i) rr[i] = base * th[i];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) rr[i] = reduce_2pi(base * th[i]);
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) __sincosf(rr[i], &sn[i], &cs[i]);
         uint32_t regs[16];
