@@ -46,10 +46,10 @@ CPU_SAMPLE_ROWS = 48
 # summed over its kernels) from ncu captures of B=1,H=8,S=2048,D=128, scaled to
 # this workload.  Exact kernel: by query rows x heads (x32),
 # profiles/exact_bwd_b1h8s2048d128.md.  Tensor-core kernels: dominated by the
-# dQ -> dK hand-off, 364.8 MB over 8 x 1088 (b, h, query tile, window) blocks,
-# i.e. 41.9 KB per block, times the 128 x 4224 blocks of this workload;
+# dQ -> dK hand-off, 362.5 MB over 8 x 1088 (b, h, query tile, window) blocks,
+# i.e. 41.6 KB per block, times the 128 x 4224 blocks of this workload;
 # profiles/tc_bwd_b1h8s2048d128.md.
-NCU_TRAFFIC_BYTES = {"exact": 33.78e6 * 32, "tensor": 364.8e6 / (8 * 1088) * (128 * 4224)}
+NCU_TRAFFIC_BYTES = {"exact": 33.78e6 * 32, "tensor": 362.5e6 / (8 * 1088) * (128 * 4224)}
 
 
 def causal_pairs(B, H, S):
