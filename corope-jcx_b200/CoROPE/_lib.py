@@ -62,6 +62,15 @@ class BwdParams(ctypes.Structure):
     ]
 
 
+class ChunkParams(ctypes.Structure):
+    """corope_chunk_t: a query chunk at sequence position q_row0 against
+    kv_len key rows (sequence-sharded callers)."""
+    _fields_ = [
+        ("q_row0", ctypes.c_int64), ("kv_len", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("dk_accum", ctypes.c_void_p), ("dv_accum", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -100,6 +109,14 @@ def load_library():
             lib.corope_params_size.restype = ctypes.c_size_t
             lib.corope_abi_version.argtypes = []
             lib.corope_abi_version.restype = ctypes.c_int
+            chunk_p = ctypes.POINTER(ChunkParams)
+            lib.corope_fwd_chunk.argtypes = [ctypes.POINTER(FwdParams), chunk_p, ctypes.c_void_p]
+            lib.corope_fwd_chunk.restype = ctypes.c_int
+            lib.corope_bwd_chunk.argtypes = [ctypes.POINTER(BwdParams), chunk_p, ctypes.c_void_p]
+            lib.corope_bwd_chunk.restype = ctypes.c_int
+            for name in ("corope_bwd_chunk_workspace_bytes", "corope_bwd_chunk_min_workspace_bytes"):
+                getattr(lib, name).argtypes = [ctypes.POINTER(BwdParams), chunk_p]
+                getattr(lib, name).restype = ctypes.c_size_t
             _lib = lib
     return _lib
 
@@ -175,8 +192,10 @@ def default_scale(head_dim: int, sm_scale) -> float:
 
 
 def fwd(q, k, v, o, m, l, a, lse, sm_scale, theta, bias=None, algo="auto", thetas=None,
-        mqa=False):
-    """Launch corope_fwd / corope_mqa_fwd on the current stream of q."""
+        mqa=False, q_row0=None):
+    """Launch corope_fwd / corope_mqa_fwd on the current stream of q.  With
+    ``q_row0`` (corope_fwd_chunk) q, o, m, l, a, lse are the query rows at
+    sequence positions q_row0.. and k, v hold every key row from 0."""
     lib = load_library()
     B, H, S, D = q.shape
     p = FwdParams()
@@ -193,13 +212,20 @@ def fwd(q, k, v, o, m, l, a, lse, sm_scale, theta, bias=None, algo="auto", theta
     p.sm_scale, p.theta = float(sm_scale), float(theta)
     p.causal, p.dtype, p.algo = 1, _dtype_code(q), algo_code(algo)
     stream = torch.cuda.current_stream(q.device).cuda_stream
+    if q_row0 is not None:
+        c = ChunkParams()
+        c.q_row0, c.kv_len = int(q_row0), k.shape[2]
+        with torch.cuda.device(q.device):
+            rc = lib.corope_fwd_chunk(ctypes.byref(p), ctypes.byref(c), ctypes.c_void_p(stream))
+        _check(rc, "corope_fwd_chunk")
+        return
     fn = lib.corope_mqa_fwd if mqa else lib.corope_fwd
     with torch.cuda.device(q.device):
         rc = fn(ctypes.byref(p), ctypes.c_void_p(stream))
     _check(rc, "corope_mqa_fwd" if mqa else "corope_fwd")
 
 
-def auto_workspace_bytes(lib, p, device):
+def auto_workspace_bytes(lib, p, device, chunk=None):
     """The workspace "auto" gives corope_bwd: the full size when it fits in a
     quarter of the memory the device and torch's cache have free, else the
     minimum plus as many whole (b, h) hand-off slices as fit there (long
@@ -207,8 +233,12 @@ def auto_workspace_bytes(lib, p, device):
     S=32768; from 2 slices on a launch already has 512 CTAs), else the
     minimum.  A quarter leaves the caller's own tensors room and keeps the
     request the same from call to call, so torch's cache can serve it again."""
-    full = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
-    least = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
+    if chunk is None:
+        full = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
+        least = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
+    else:
+        full = lib.corope_bwd_chunk_workspace_bytes(ctypes.byref(p), ctypes.byref(chunk))
+        least = lib.corope_bwd_chunk_min_workspace_bytes(ctypes.byref(p), ctypes.byref(chunk))
     free, _ = torch.cuda.mem_get_info(device)
     budget = (free + torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)) // 4
     return fit_workspace(full, least, p.batch * p.heads, budget)
@@ -226,11 +256,16 @@ def fit_workspace(full, least, units, budget):
 
 
 def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="auto",
-        thetas=None, workspace="auto"):
+        thetas=None, workspace="auto", q_row0=None, dk_accum=None, dv_accum=None):
     """Launch corope_bwd on the current stream of q with a torch-allocated
     workspace: "auto" (the full size when it fits in free memory, else as many
     hand-off slices as fit), "full" (corope_bwd_workspace_bytes, the fastest),
-    "min" (corope_bwd_min_workspace_bytes) or a byte count in between."""
+    "min" (corope_bwd_min_workspace_bytes) or a byte count in between.
+
+    With ``q_row0`` (corope_bwd_chunk) q, o, do, m, l, a, dq are the query rows
+    at sequence positions q_row0.., k, v hold every key row, ``dk``/``dv`` are
+    ignored and this chunk's key gradients are added to the contiguous fp32
+    ``dk_accum``/``dv_accum`` [B, Hkv, kv_len, D]."""
     lib = load_library()
     B, H, S, D = q.shape
     p = BwdParams()
@@ -242,25 +277,40 @@ def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="a
     if bias is not None:
         p.bias = bias.data_ptr()
         p.bias_row_stride = bias.stride(0)
-    p.dq, p.dk, p.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    p.dq = dq.data_ptr()
     p.q_stride, p.k_stride, p.v_stride = _strides(q), _strides(k), _strides(v)
-    p.o_stride, p.do_stride = _strides(o), _strides(do)
-    p.dq_stride, p.dk_stride, p.dv_stride = _strides(dq), _strides(dk), _strides(dv)
+    p.o_stride, p.do_stride, p.dq_stride = _strides(o), _strides(do), _strides(dq)
+    chunk = None
+    if q_row0 is None:
+        p.dk, p.dv = dk.data_ptr(), dv.data_ptr()
+        p.dk_stride, p.dv_stride = _strides(dk), _strides(dv)
+    else:
+        for t in (dk_accum, dv_accum):
+            assert t is not None and t.dtype == torch.float32 and t.is_contiguous()
+            assert t.shape == k.shape
+        chunk = ChunkParams()
+        chunk.q_row0, chunk.kv_len = int(q_row0), k.shape[2]
+        chunk.dk_accum, chunk.dv_accum = dk_accum.data_ptr(), dv_accum.data_ptr()
     p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, k.shape[1], S, D
     p.sm_scale, p.theta = float(sm_scale), float(theta)
     p.causal, p.dtype, p.algo = 1, _dtype_code(q), algo_code(algo)
     if workspace == "auto":
-        nbytes = auto_workspace_bytes(lib, p, q.device)
+        nbytes = auto_workspace_bytes(lib, p, q.device, chunk)
     elif workspace == "full":
-        nbytes = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
+        nbytes = (lib.corope_bwd_workspace_bytes(ctypes.byref(p)) if chunk is None else
+                  lib.corope_bwd_chunk_workspace_bytes(ctypes.byref(p), ctypes.byref(chunk)))
     elif workspace == "min":
-        nbytes = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
+        nbytes = (lib.corope_bwd_min_workspace_bytes(ctypes.byref(p)) if chunk is None else
+                  lib.corope_bwd_chunk_min_workspace_bytes(ctypes.byref(p), ctypes.byref(chunk)))
     else:
         nbytes = int(workspace)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
     p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
     stream = torch.cuda.current_stream(q.device).cuda_stream
     with torch.cuda.device(q.device):
-        rc = lib.corope_bwd(ctypes.byref(p), ctypes.c_void_p(stream))
-    _check(rc, "corope_bwd")
+        if chunk is None:
+            rc = lib.corope_bwd(ctypes.byref(p), ctypes.c_void_p(stream))
+        else:
+            rc = lib.corope_bwd_chunk(ctypes.byref(p), ctypes.byref(chunk), ctypes.c_void_p(stream))
+    _check(rc, "corope_bwd" if chunk is None else "corope_bwd_chunk")
     return ws

@@ -110,6 +110,10 @@ struct FwdArgs {
   int64_t qs[3], ks[3], vs[3], os[3];
   int B, H, Hkv, S, D;
   float sm_scale, theta;
+  // query chunk: q, o, m, l, a, lse hold the S rows at sequence positions
+  // r0 .. r0 + S - 1 (r0 a multiple of 128); k, v hold Sk >= r0 + S rows
+  // from position 0.  A whole sequence is r0 = 0, Sk = S.
+  int r0, Sk;
 };
 
 struct BwdArgs {
@@ -122,11 +126,14 @@ struct BwdArgs {
   int64_t qs[3], ks[3], vs[3], os[3], dos[3], dqs[3], dks[3], dvs[3];
   int B, H, Hkv, S, D;
   float sm_scale, theta;
+  // query chunk, as in FwdArgs: q, o, dO, dq, m, l, a, delta, lse hold rows
+  // r0 .. r0 + S - 1; k, v, dk32, dv32 (and dk, dv) hold Sk rows
+  int r0, Sk;
   // workspace views
   float* delta;  // [B,H,S]  rowsum(dO * O)
   float* lse;    // [B,H,S]  m + log(l)
-  float* dk32;   // [B,Hkv,S,D] fp32 accumulators
-  float* dv32;   // [B,Hkv,S,D]
+  float* dk32;   // [B,Hkv,Sk,D] fp32 accumulators
+  float* dv32;   // [B,Hkv,Sk,D]
 };
 
 }  // namespace corope

@@ -19,7 +19,7 @@ int tc_take_device_error();
 bool tc_bwd_supported(const BwdArgs& a, int dtype);
 cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* handoff,
                           size_t handoff_bytes);
-int64_t tc_bwd_handoff_bytes_per_bh(int S);
+int64_t tc_bwd_handoff_bytes_per_bh(int S, int r0);
 int tcb_take_device_error();
 cudaError_t bwd_pre_launch(const BwdArgs& a, int dtype, cudaStream_t st);
 cudaError_t bwd_post_launch(const BwdArgs& a, int dtype, cudaStream_t st);
@@ -107,19 +107,35 @@ static int check_tensor(const void* p, const int64_t* st, const char* name, int 
 
 static void copy3(int64_t* d, const int64_t* s) { d[0] = s[0]; d[1] = s[1]; d[2] = s[2]; }
 
-static int fwd_common(const corope_fwd_params_t* p, corope_stream_t stream, bool mqa) {
+// A query chunk: row offset tile-aligned, k / v long enough for every row.
+static int check_chunk(const corope_chunk_t* c, int seq_len) {
+  if (!c) return fail(COROPE_ERR_INVALID, "chunk is NULL");
+  if (c->q_row0 < 0 || c->q_row0 % 128 != 0)
+    return fail(COROPE_ERR_INVALID, "q_row0 must be a non-negative multiple of 128 (got %lld)",
+                (long long)c->q_row0);
+  if (c->q_row0 + seq_len > (int64_t)c->kv_len || c->q_row0 + seq_len > INT32_MAX)
+    return fail(COROPE_ERR_INVALID, "kv_len (%d) must cover q_row0 + seq_len (%lld)", c->kv_len,
+                (long long)(c->q_row0 + seq_len));
+  return COROPE_OK;
+}
+
+static int fwd_common(const corope_fwd_params_t* p, corope_stream_t stream, bool mqa,
+                      const corope_chunk_t* chunk = nullptr) {
   if (!p) return fail(COROPE_ERR_INVALID, "params is NULL");
   int rc = check_common(p->batch, p->heads, p->kv_heads, p->seq_len, p->head_dim, p->causal,
                         p->dtype, p->sm_scale, p->theta);
   if (rc) return rc;
+  if (chunk && (rc = check_chunk(chunk, p->seq_len))) return rc;
+  const int r0 = chunk ? (int)chunk->q_row0 : 0;
+  const int Sk = chunk ? chunk->kv_len : p->seq_len;
   if (!mqa && p->kv_heads != p->heads)
     return fail(COROPE_ERR_INVALID, "corope_fwd needs kv_heads == heads; use corope_mqa_fwd");
   if ((rc = check_tensor(p->q, p->q_stride, "q", p->dtype))) return rc;
   if ((rc = check_tensor(p->k, p->k_stride, "k", p->dtype))) return rc;
   if ((rc = check_tensor(p->v, p->v_stride, "v", p->dtype))) return rc;
   if ((rc = check_tensor(p->o, p->o_stride, "o", p->dtype))) return rc;
-  if (p->bias && p->bias_row_stride < p->seq_len)
-    return fail(COROPE_ERR_INVALID, "bias_row_stride must be >= seq_len");
+  if (p->bias && p->bias_row_stride < r0 + p->seq_len)
+    return fail(COROPE_ERR_INVALID, "bias_row_stride must be >= seq_len (q_row0 + seq_len)");
   if ((rc = check_device())) return rc;
 
   FwdArgs a{};
@@ -130,6 +146,7 @@ static int fwd_common(const corope_fwd_params_t* p, corope_stream_t stream, bool
   copy3(a.os, p->o_stride);
   a.B = p->batch; a.H = p->heads; a.Hkv = p->kv_heads; a.S = p->seq_len; a.D = p->head_dim;
   a.sm_scale = p->sm_scale; a.theta = p->theta;
+  a.r0 = r0; a.Sk = Sk;
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const bool tc_ok = tc_fwd_supported(a, p->dtype);
@@ -146,23 +163,33 @@ static int fwd_common(const corope_fwd_params_t* p, corope_stream_t stream, bool
 
 static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
-// Minimum workspace: delta and lse rows, fp32 dk / dv accumulators.
-static size_t bwd_ws(const corope_bwd_params_t* p) {
+// Minimum workspace: delta and lse rows, fp32 dk / dv accumulators (a query
+// chunk accumulates into the caller's dk_accum / dv_accum instead).
+static size_t bwd_ws(const corope_bwd_params_t* p, bool chunk = false) {
   const size_t rows = (size_t)p->batch * p->heads * p->seq_len;
   const size_t kv = (size_t)p->batch * p->kv_heads * p->seq_len * p->head_dim;
-  return 2 * align256(rows * 4) + 2 * align256(kv * 4);
+  return 2 * align256(rows * 4) + (chunk ? 0 : 2 * align256(kv * 4));
 }
 
 // Optional hand-off region after it (tensor-core backward only): the dQ
 // kernel's per-(row, key) results for the dK kernel, 20,992 bytes per 128 query
 // rows x 16 keys; with less, the (b, h) slices go through it in chunks, or the
 // dK kernel recomputes them.
-static size_t bwd_handoff_ws(const corope_bwd_params_t* p) {
+static size_t bwd_handoff_ws(const corope_bwd_params_t* p, int r0 = 0) {
   if ((p->head_dim != 64 && p->head_dim != 128) || p->algo == COROPE_ALGO_EXACT ||
       (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16))
     return 0;
-  return align256((size_t)p->batch * p->heads * (size_t)tc_bwd_handoff_bytes_per_bh(p->seq_len));
+  return align256((size_t)p->batch * p->heads *
+                  (size_t)tc_bwd_handoff_bytes_per_bh(p->seq_len, r0));
 }
+
+static bool sizes_ok(const corope_bwd_params_t* p) {
+  return p && p->batch > 0 && p->heads > 0 && p->kv_heads > 0 && p->seq_len > 0 &&
+         p->head_dim > 0;
+}
+
+static int bwd_common(const corope_bwd_params_t* p, corope_stream_t stream,
+                      const corope_chunk_t* chunk);
 
 extern "C" {
 
@@ -175,38 +202,73 @@ int corope_mqa_fwd(const corope_fwd_params_t* p, corope_stream_t stream) {
 }
 
 size_t corope_bwd_workspace_bytes(const corope_bwd_params_t* p) {
-  if (!p || p->batch <= 0 || p->heads <= 0 || p->kv_heads <= 0 || p->seq_len <= 0 ||
-      p->head_dim <= 0)
-    return 0;
+  if (!sizes_ok(p)) return 0;
   return bwd_ws(p) + bwd_handoff_ws(p);
 }
 
 size_t corope_bwd_min_workspace_bytes(const corope_bwd_params_t* p) {
-  if (!p || p->batch <= 0 || p->heads <= 0 || p->kv_heads <= 0 || p->seq_len <= 0 ||
-      p->head_dim <= 0)
-    return 0;
+  if (!sizes_ok(p)) return 0;
   return bwd_ws(p);
 }
 
 int corope_bwd(const corope_bwd_params_t* p, corope_stream_t stream) {
+  return bwd_common(p, stream, nullptr);
+}
+
+int corope_fwd_chunk(const corope_fwd_params_t* p, const corope_chunk_t* chunk,
+                     corope_stream_t stream) {
+  if (!chunk) return fail(COROPE_ERR_INVALID, "chunk is NULL");
+  return fwd_common(p, stream, true, chunk);
+}
+
+size_t corope_bwd_chunk_workspace_bytes(const corope_bwd_params_t* p, const corope_chunk_t* c) {
+  if (!sizes_ok(p) || !c || c->q_row0 < 0 || c->q_row0 % 128 != 0) return 0;
+  return bwd_ws(p, true) + bwd_handoff_ws(p, (int)c->q_row0);
+}
+
+size_t corope_bwd_chunk_min_workspace_bytes(const corope_bwd_params_t* p,
+                                            const corope_chunk_t* c) {
+  if (!sizes_ok(p) || !c) return 0;
+  return bwd_ws(p, true);
+}
+
+int corope_bwd_chunk(const corope_bwd_params_t* p, const corope_chunk_t* chunk,
+                     corope_stream_t stream) {
+  if (!chunk) return fail(COROPE_ERR_INVALID, "chunk is NULL");
+  return bwd_common(p, stream, chunk);
+}
+
+}  // extern "C"
+
+static int bwd_common(const corope_bwd_params_t* p, corope_stream_t stream,
+                      const corope_chunk_t* chunk) {
   if (!p) return fail(COROPE_ERR_INVALID, "params is NULL");
   int rc = check_common(p->batch, p->heads, p->kv_heads, p->seq_len, p->head_dim, p->causal,
                         p->dtype, p->sm_scale, p->theta);
   if (rc) return rc;
+  if (chunk && (rc = check_chunk(chunk, p->seq_len))) return rc;
+  const int r0 = chunk ? (int)chunk->q_row0 : 0;
+  const int Sk = chunk ? chunk->kv_len : p->seq_len;
   if ((rc = check_tensor(p->q, p->q_stride, "q", p->dtype))) return rc;
   if ((rc = check_tensor(p->k, p->k_stride, "k", p->dtype))) return rc;
   if ((rc = check_tensor(p->v, p->v_stride, "v", p->dtype))) return rc;
   if ((rc = check_tensor(p->o, p->o_stride, "o", p->dtype))) return rc;
   if ((rc = check_tensor(p->dout, p->do_stride, "dout", p->dtype))) return rc;
   if ((rc = check_tensor(p->dq, p->dq_stride, "dq", p->dtype))) return rc;
-  if ((rc = check_tensor(p->dk, p->dk_stride, "dk", p->dtype))) return rc;
-  if ((rc = check_tensor(p->dv, p->dv_stride, "dv", p->dtype))) return rc;
+  if (chunk) {
+    if (!chunk->dk_accum || !chunk->dv_accum || !aligned(chunk->dk_accum, 4) ||
+        !aligned(chunk->dv_accum, 4))
+      return fail(COROPE_ERR_INVALID, "chunk dk_accum and dv_accum (fp32) are required");
+  } else {
+    if ((rc = check_tensor(p->dk, p->dk_stride, "dk", p->dtype))) return rc;
+    if ((rc = check_tensor(p->dv, p->dv_stride, "dv", p->dtype))) return rc;
+  }
   if (!p->m || !p->l || !p->a) return fail(COROPE_ERR_INVALID, "m, l and a are required");
-  if (p->bias && p->bias_row_stride < p->seq_len)
-    return fail(COROPE_ERR_INVALID, "bias_row_stride must be >= seq_len");
+  if (p->bias && p->bias_row_stride < r0 + p->seq_len)
+    return fail(COROPE_ERR_INVALID, "bias_row_stride must be >= seq_len (q_row0 + seq_len)");
   if (p->algo != COROPE_ALGO_EXACT && p->algo != COROPE_ALGO_AUTO && p->algo != COROPE_ALGO_TENSOR)
     return fail(COROPE_ERR_INVALID, "unknown algo %d", p->algo);
-  const size_t need = bwd_ws(p);
+  const size_t need = bwd_ws(p, chunk != nullptr);
   if (!p->workspace || p->workspace_bytes < need)
     return fail(COROPE_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need,
                 p->workspace ? p->workspace_bytes : (size_t)0);
@@ -217,41 +279,52 @@ int corope_bwd(const corope_bwd_params_t* p, corope_stream_t stream) {
   a.q = p->q; a.k = p->k; a.v = p->v; a.o = p->o; a.dout = p->dout;
   a.m = p->m; a.l = p->l; a.a = p->a;
   a.thetas = p->thetas; a.bias = p->bias; a.bias_rs = p->bias_row_stride;
-  a.dq = p->dq; a.dk = p->dk; a.dv = p->dv;
+  a.dq = p->dq;
+  a.dk = chunk ? nullptr : p->dk;
+  a.dv = chunk ? nullptr : p->dv;
   copy3(a.qs, p->q_stride); copy3(a.ks, p->k_stride); copy3(a.vs, p->v_stride);
   copy3(a.os, p->o_stride); copy3(a.dos, p->do_stride); copy3(a.dqs, p->dq_stride);
   copy3(a.dks, p->dk_stride); copy3(a.dvs, p->dv_stride);
   a.B = p->batch; a.H = p->heads; a.Hkv = p->kv_heads; a.S = p->seq_len; a.D = p->head_dim;
   a.sm_scale = p->sm_scale; a.theta = p->theta;
+  a.r0 = r0; a.Sk = Sk;
 
   const size_t rows = (size_t)p->batch * p->heads * p->seq_len;
   const size_t kv = (size_t)p->batch * p->kv_heads * p->seq_len * p->head_dim;
   char* ws = static_cast<char*>(p->workspace);
   a.delta = reinterpret_cast<float*>(ws);
   a.lse = reinterpret_cast<float*>(ws + align256(rows * 4));
-  a.dk32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4));
-  a.dv32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4) + align256(kv * 4));
+  if (chunk) {
+    a.dk32 = chunk->dk_accum;
+    a.dv32 = chunk->dv_accum;
+  } else {
+    a.dk32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4));
+    a.dv32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4) + align256(kv * 4));
+  }
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const bool tc_ok = tc_bwd_supported(a, p->dtype);
   if (p->algo == COROPE_ALGO_TENSOR && !tc_ok)
     return fail(COROPE_ERR_UNSUPPORTED,
                 "tensor-core backward needs bf16/f16, head_dim 64 or 128 and 16-byte aligned rows");
-  cudaError_t e = cudaMemsetAsync(a.dk32, 0, 2 * align256(kv * 4), st);
+  cudaError_t e = cudaSuccess;
+  if (!chunk) e = cudaMemsetAsync(a.dk32, 0, 2 * align256(kv * 4), st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
   if (p->algo != COROPE_ALGO_EXACT && tc_ok) {
     e = bwd_pre_launch(a, p->dtype, st);
-    const size_t base = bwd_ws(p);
+    const size_t base = need;
     if (e == cudaSuccess)
       e = tc_bwd_launch(a, p->dtype, st, static_cast<char*>(p->workspace) + base,
                         p->workspace_bytes - base);
-    if (e == cudaSuccess) e = bwd_post_launch(a, p->dtype, st);
+    if (e == cudaSuccess && !chunk) e = bwd_post_launch(a, p->dtype, st);
   } else {
     e = exact_bwd_launch(a, p->dtype, st);
   }
   if (e != cudaSuccess) return cuda_fail(e, "backward launch");
   return COROPE_OK;
 }
+
+extern "C" {
 
 const char* corope_last_error(void) { return g_err; }
 

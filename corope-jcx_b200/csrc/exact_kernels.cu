@@ -62,7 +62,8 @@ exact_fwd_kernel(FwdArgs args) {
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (args.H / args.Hkv);
   const int rl = threadIdx.x / TPR, sub = threadIdx.x % TPR;
-  const int t = qtile * kBM + rl;
+  const int tl = qtile * kBM + rl;  // row of q / o
+  const int t = args.r0 + tl;       // its sequence position
   const int S = args.S;
 
   const T* qb = (const T*)args.q + b * args.qs[0] + h * args.qs[1];
@@ -75,7 +76,7 @@ exact_fwd_kernel(FwdArgs args) {
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
     int p = i * TPR + sub;
-    qp[i] = (t < S) ? load_pair<T>(qb, (int64_t)t * args.qs[2] + 2 * p) : make_float2(0.f, 0.f);
+    qp[i] = (tl < S) ? load_pair<T>(qb, (int64_t)tl * args.qs[2] + 2 * p) : make_float2(0.f, 0.f);
     op[i] = make_float2(0.f, 0.f);
   }
   float m_run = -1e30f, l_run = 0.f;
@@ -85,11 +86,11 @@ exact_fwd_kernel(FwdArgs args) {
   float lg[CH];
   const float sm = args.sm_scale;
 
-  const int last_row = min(S - 1, qtile * kBM + kBM - 1);
+  const int last_row = args.r0 + min(S - 1, qtile * kBM + kBM - 1);  // sequence position
   for (int j0 = (last_row / kBN) * kBN; j0 >= 0; j0 -= kBN) {
     __syncthreads();
-    stage_rows<T, D>(Ks, kb, args.ks[2], j0, S, NT);
-    stage_rows<T, D>(Vs, vb, args.vs[2], j0, S, NT);
+    stage_rows<T, D>(Ks, kb, args.ks[2], j0, args.Sk, NT);
+    stage_rows<T, D>(Vs, vb, args.vs[2], j0, args.Sk, NT);
     __syncthreads();
 #pragma unroll 1
     for (int c0 = kBN - CH; c0 >= 0; c0 -= CH) {
@@ -97,7 +98,7 @@ exact_fwd_kernel(FwdArgs args) {
       for (int u = CH - 1; u >= 0; --u) {
         const int jj = c0 + u;
         const int j = j0 + jj;
-        const bool valid = (j <= t) && (t < S);
+        const bool valid = (j <= t) && (tl < S);
         const float2* kr = Ks + jj * P;
         float g = 0.f;
 #pragma unroll
@@ -153,8 +154,8 @@ exact_fwd_kernel(FwdArgs args) {
     }
   }
 
-  if (t < S) {
-    T* ob = (T*)args.o + b * args.os[0] + h * args.os[1] + (int64_t)t * args.os[2];
+  if (tl < S) {
+    T* ob = (T*)args.o + b * args.os[0] + h * args.os[1] + (int64_t)tl * args.os[2];
     const float inv = 1.0f / l_run;
 #pragma unroll
     for (int i = 0; i < NP; ++i) {
@@ -163,7 +164,7 @@ exact_fwd_kernel(FwdArgs args) {
       ob[2 * p + 1] = from_f32<T>(op[i].y * inv);
     }
     if (sub == 0) {
-      const int64_t r = ((int64_t)b * args.H + h) * S + t;
+      const int64_t r = ((int64_t)b * args.H + h) * S + tl;
       if (args.m) args.m[r] = m_run;
       if (args.l) args.l[r] = l_run;
       if (args.a) args.a[r] = a_run - a_cmp;
@@ -228,8 +229,9 @@ exact_bwd_kernel(BwdArgs args) {
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (args.H / args.Hkv);
   const int rl = threadIdx.x / TPR, sub = threadIdx.x % TPR;
-  const int q0 = qtile * kBM;
-  const int t = q0 + rl;
+  const int q0 = qtile * kBM;        // first row of the tile in q / dO / dq
+  const int tl = q0 + rl;
+  const int t = args.r0 + tl;        // sequence position of row tl
   const int S = args.S;
   const float sm = args.sm_scale;
 
@@ -254,29 +256,29 @@ exact_bwd_kernel(BwdArgs args) {
     dop[i] = Ds[rl * P + i * TPR + sub];
     dqp[i] = make_float2(0.f, 0.f);
   }
-  const int64_t rix = ((int64_t)b * args.H + h) * S + t;
-  const float A_t = (t < S) ? args.a[rix] : 0.f;
-  const float lse_t = (t < S) ? args.lse[rix] : 0.f;
-  const float dlt_t = (t < S) ? args.delta[rix] : 0.f;
+  const int64_t rix = ((int64_t)b * args.H + h) * S + tl;
+  const float A_t = (tl < S) ? args.a[rix] : 0.f;
+  const float lse_t = (tl < S) ? args.lse[rix] : 0.f;
+  const float dlt_t = (tl < S) ? args.delta[rix] : 0.f;
   // gate prefix, compensated (Kahan; c_run - c_cmp is the prefix to ~1 ulp)
   float c_run = 0.f, c_cmp = 0.f, da_run = 0.f;
 
   // phase-2 mapping
   const int kj = threadIdx.x / TPK, sub2 = threadIdx.x % TPK;
-  float* dk32 = args.dk32 + ((int64_t)b * args.Hkv + hk) * S * D;
-  float* dv32 = args.dv32 + ((int64_t)b * args.Hkv + hk) * S * D;
+  float* dk32 = args.dk32 + ((int64_t)b * args.Hkv + hk) * args.Sk * D;
+  float* dv32 = args.dv32 + ((int64_t)b * args.Hkv + hk) * args.Sk * D;
 
-  const int last_row = min(S - 1, q0 + kBM - 1);
+  const int last_row = args.r0 + min(S - 1, q0 + kBM - 1);  // sequence position
   for (int j0 = 0; j0 <= last_row; j0 += kBN) {
     __syncthreads();
-    stage_rows<T, D>(Ks, kb, args.ks[2], j0, S, NT);
-    stage_rows<T, D>(Vs, vb, args.vs[2], j0, S, NT);
+    stage_rows<T, D>(Ks, kb, args.ks[2], j0, args.Sk, NT);
+    stage_rows<T, D>(Vs, vb, args.vs[2], j0, args.Sk, NT);
     __syncthreads();
     // ---- phase 1: row owners --------------------------------------------
 #pragma unroll 1
     for (int jj = 0; jj < kBN; ++jj) {
       const int j = j0 + jj;
-      const bool valid = (j <= t) && (t < S);
+      const bool valid = (j <= t) && (tl < S);
       const float2* kr = Ks + jj * P;
       const float2* vr = Vs + jj * P;
       float g = 0.f;
@@ -361,7 +363,7 @@ exact_bwd_kernel(BwdArgs args) {
           }
         }
       }
-      if (j < S) {
+      if (j < args.Sk) {
 #pragma unroll
         for (int i = 0; i < NP2; ++i) {
           const int p = i * TPK + sub2;
@@ -376,8 +378,8 @@ exact_bwd_kernel(BwdArgs args) {
     }
   }
 
-  if (t < S) {
-    T* dqb = (T*)args.dq + b * args.dqs[0] + h * args.dqs[1] + (int64_t)t * args.dqs[2];
+  if (tl < S) {
+    T* dqb = (T*)args.dq + b * args.dqs[0] + h * args.dqs[1] + (int64_t)tl * args.dqs[2];
 #pragma unroll
     for (int i = 0; i < NP; ++i) {
       int p = i * TPR + sub;
@@ -390,13 +392,13 @@ exact_bwd_kernel(BwdArgs args) {
 // fp32 dk/dv accumulators -> output dtype and strides.
 template <typename T>
 __global__ void exact_bwd_post_kernel(BwdArgs args) {
-  const int64_t n = (int64_t)args.B * args.Hkv * args.S * args.D;
+  const int64_t n = (int64_t)args.B * args.Hkv * args.Sk * args.D;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int d = i % args.D;
     int64_t r = i / args.D;
-    const int j = r % args.S;
-    r /= args.S;
+    const int j = r % args.Sk;
+    r /= args.Sk;
     const int hk = r % args.Hkv;
     const int b = r / args.Hkv;
     ((T*)args.dk)[b * args.dks[0] + hk * args.dks[1] + (int64_t)j * args.dks[2] + d] =
@@ -486,6 +488,7 @@ static cudaError_t launch_bwd_t(const BwdArgs& a, cudaStream_t st) {
     default: return cudaErrorInvalidValue;
   }
   if (e != cudaSuccess) return e;
+  if (!a.dk || !a.dv) return cudaSuccess;  // query chunk: the caller keeps the fp32 sums
   exact_bwd_post_kernel<T><<<148 * 8, 256, 0, st>>>(a);
   return cudaGetLastError();
 }

@@ -94,13 +94,14 @@ enum : int {
 struct Params {
   CUtensorMap tm_q, tm_k, tm_v, tm_do;
   void* dq;              // dQ launch output, element type of q
-  float *dk32, *dv32;    // dK launch accumulators [B, Hkv, S, D]
+  float *dk32, *dv32;    // dK launch accumulators [B, Hkv, Sk, D]
   const float *lse, *delta, *a;  // [B, H, S]
   const float* thetas;
   const float* bias;
   int64_t bias_rs;
   int64_t dqs[3];
   int B, H, Hkv, S;
+  int r0, Sk;  // sequence position of row 0 of q / dO / dq (a multiple of kBM); rows of k, v
   float theta;
   int nrow[8];
   int nb;
@@ -160,6 +161,10 @@ constexpr int kHB = HB_C + 128 * 4;
 // first block of query tile qt within its (b, h): tiles before it are full
 // (8 (q + 1) windows each)
 __host__ __device__ constexpr int64_t tile_block0(int qt) { return 4ll * qt * (qt + 1); }
+// the same within a query chunk starting at sequence position r0 (a multiple of 128)
+__host__ __device__ constexpr int64_t chunk_block0(int r0, int qt) {
+  return tile_block0(r0 / 128 + qt) - tile_block0(r0 / 128);
+}
 // u in [-1, 1] -> 16-bit fixed point, rounded, saturating at both ends
 __device__ __forceinline__ uint32_t u_encode(float u) {
   unsigned short q;
@@ -226,8 +231,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
   const int bh = P.bh0 + blockIdx.y;
   const int h = bh % P.H, b = bh / P.H;
   const int hk = h / (P.H / P.Hkv);
-  const int q0 = qt * kBM;
-  const int S = P.S;
+  const int q0 = P.r0 + qt * kBM;  // sequence position of the tile's first row
+  const int S = P.r0 + P.S;        // end of this launch's rows (sequence position)
   const int WL = min(S - 1, q0 + kBM - 1) / kW;  // last (highest) window
   const int nb = P.nb;
 
@@ -315,8 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         prefetch_tmap(&P.tm_do);
         mbar_expect_tx(&bars[B_Q], 2 * DSL * 16384);
         for (int s = 0; s < DSL; ++s) {
-          tma_load_4d(smem + S_Q + s * 16384, &P.tm_q, &bars[B_Q], 64 * s, q0, h, b);
-          tma_load_4d(smem + S_DO + s * 16384, &P.tm_do, &bars[B_Q], 64 * s, q0, h, b);
+          tma_load_4d(smem + S_Q + s * 16384, &P.tm_q, &bars[B_Q], 64 * s, q0 - P.r0, h, b);
+          tma_load_4d(smem + S_DO + s * 16384, &P.tm_do, &bars[B_Q], 64 * s, q0 - P.r0, h, b);
         }
         const int TL = WL / 2;  // last K/V tile
         int last_use[2] = {-1, -1};
@@ -544,8 +549,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       }
     }
     const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
-    float* dk32 = P.dk32 + ((int64_t)b * P.Hkv + hk) * S * D;
-    float* dv32 = P.dv32 + ((int64_t)b * P.Hkv + hk) * S * D;
+    float* dk32 = P.dk32 + ((int64_t)b * P.Hkv + hk) * P.Sk * D;
+    float* dv32 = P.dv32 + ((int64_t)b * P.Hkv + hk) * P.Sk * D;
 
     auto build = [&](int w) -> bool {
       const int buf = w % nb, use = w / nb;
@@ -647,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = w * kW + j;
-        if (key < S && d < D) {
+        if (key < P.Sk && d < D) {
           atomicAdd(dk32 + (int64_t)key * D + d, dk[j]);
           atomicAdd(dv32 + (int64_t)key * D + d, dv[j]);
         }
@@ -671,7 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     const int t = q0 + r;
     const bool row_ok = t < S;
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const int64_t ri = ((int64_t)b * P.H + h) * S + min(t, S - 1);
+    const int64_t ri = ((int64_t)b * P.H + h) * P.S + min(t - P.r0, P.S - 1);
     const float A_t = P.a[ri];
     const float lse2 = P.lse[ri] * kLog2e;
     const float delta = P.delta[ri];
@@ -845,7 +850,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     // the two halves of window w
     uint8_t* const hblk0 =
         (MODE == MODE_DQ && P.handoff)
-            ? P.handoff + ((int64_t)blockIdx.y * P.blocks_bh + tile_block0(qt)) * kHB
+            ? P.handoff + ((int64_t)blockIdx.y * P.blocks_bh + chunk_block0(P.r0, qt)) * kHB
             : nullptr;
     auto halves = [&](int w) -> bool {
       const int j0 = w * kW;
@@ -1034,7 +1039,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     }
     if (MODE == MODE_DQ && ok) {
       // all GEMMs into DQ are done (the last window's B_XF was waited above)
-      T* dqrow = reinterpret_cast<T*>(P.dq) + b * P.dqs[0] + h * P.dqs[1] + (int64_t)t * P.dqs[2];
+      T* dqrow = reinterpret_cast<T*>(P.dq) + b * P.dqs[0] + h * P.dqs[1] +
+                 (int64_t)(t - P.r0) * P.dqs[2];
 #pragma unroll 1
       for (int c = 0; c < PW / 8; ++c) {
         uint32_t o[16];
@@ -1112,8 +1118,8 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
   const int bh = P.bh0 + blockIdx.y;
   const int h = bh % P.H, b = bh / P.H;
   const int hk = h / (P.H / P.Hkv);
-  const int q0 = qt * kBM;
-  const int S = P.S;
+  const int q0 = P.r0 + qt * kBM;  // sequence position of the tile's first row
+  const int S = P.r0 + P.S;        // end of this launch's rows (sequence position)
   const int WL = min(S - 1, q0 + kBM - 1) / kW;
 
   if (tid == 0) {
@@ -1164,8 +1170,8 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
       prefetch_tmap(&P.tm_do);
       mbar_expect_tx(&bars[k2::B_Q], 2 * DSL * 16384);
       for (int s = 0; s < DSL; ++s) {
-        tma_load_4d(smem + k2::Q + s * 16384, &P.tm_q, &bars[k2::B_Q], 64 * s, q0, h, b);
-        tma_load_4d(smem + k2::DO + s * 16384, &P.tm_do, &bars[k2::B_Q], 64 * s, q0, h, b);
+        tma_load_4d(smem + k2::Q + s * 16384, &P.tm_q, &bars[k2::B_Q], 64 * s, q0 - P.r0, h, b);
+        tma_load_4d(smem + k2::DO + s * 16384, &P.tm_do, &bars[k2::B_Q], 64 * s, q0 - P.r0, h, b);
       }
       mbar_wait(&bars[k2::B_Q], 0, err, kErrDrain);
     }
@@ -1233,8 +1239,8 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
       }
     }
     const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
-    float* dk32 = P.dk32 + ((int64_t)b * P.Hkv + hk) * S * D + gt;
-    float* dv32 = P.dv32 + ((int64_t)b * P.Hkv + hk) * S * D + gt;
+    float* dk32 = P.dk32 + ((int64_t)b * P.Hkv + hk) * P.Sk * D + gt;
+    float* dv32 = P.dv32 + ((int64_t)b * P.Hkv + hk) * P.Sk * D + gt;
     for (int w = 0; w <= WL; ++w) {
       const int bf = w & 1;
       if (!wwait(bars[k2::B_CF + bf], (w >> 1) & 1, err, kErrC)) break;
@@ -1291,7 +1297,7 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = w * kW + j;
-        if (key < S && gt < D) {
+        if (key < P.Sk && gt < D) {
           atomicAdd(dk32 + (int64_t)key * D, dk[j]);
           atomicAdd(dv32 + (int64_t)key * D, dv[j]);
         }
@@ -1305,7 +1311,8 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
     named_bar(1, kThreads);
     const int rg = warp >> 2;
     const int r = tid & 127;
-    const uint8_t* hb0 = P.handoff + ((int64_t)blockIdx.y * P.blocks_bh + tile_block0(qt)) * kHB;
+    const uint8_t* hb0 =
+        P.handoff + ((int64_t)blockIdx.y * P.blocks_bh + chunk_block0(P.r0, qt)) * kHB;
     struct Rec {
       float4 dl[2];
       uint2 u[2];
@@ -1499,9 +1506,9 @@ static int min_slices(int BH, int S) {
 }
 
 // hand-off blocks of one (b, h): one per (query tile, window)
-static int64_t blocks_per_bh(int S) {
+static int64_t blocks_per_bh(int S, int r0 = 0) {
   int64_t n = 0;
-  for (int qt = 0; qt * kBM < S; ++qt) n += min(S - 1, qt * kBM + kBM - 1) / kW + 1;
+  for (int qt = 0; qt * kBM < S; ++qt) n += (r0 + min(S - 1, qt * kBM + kBM - 1)) / kW + 1;
   return n;
 }
 
@@ -1509,7 +1516,7 @@ template <typename T, int D>
 static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* handoff,
                               size_t handoff_bytes, cudaStream_t st, float theta,
                               float sm_scale) {
-  const int64_t per_bh = blocks_per_bh(S) * kHB;
+  const int64_t per_bh = blocks_per_bh(S, p.r0) * kHB;
   int chunk = handoff ? (int)std::min<int64_t>(BH, (int64_t)(handoff_bytes / per_bh)) : 0;
   if (chunk < min_slices(BH, S)) chunk = 0;  // too few CTAs per launch: recompute instead
   cudaError_t e = cudaSuccess;
@@ -1521,7 +1528,7 @@ static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* hand
     return e;
   }
   p.handoff = handoff;
-  p.blocks_bh = blocks_per_bh(S);
+  p.blocks_bh = blocks_per_bh(S, p.r0);
   for (int bh0 = 0; bh0 < BH && e == cudaSuccess; bh0 += chunk) {
     p.bh0 = bh0;
     const int nbh = std::min(chunk, BH - bh0);
@@ -1533,7 +1540,7 @@ static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* hand
 
 }  // namespace tcb
 
-int64_t tc_bwd_handoff_bytes_per_bh(int S) { return tcb::blocks_per_bh(S) * tcb::kHB; }
+int64_t tc_bwd_handoff_bytes_per_bh(int S, int r0) { return tcb::blocks_per_bh(S, r0) * tcb::kHB; }
 
 static bool rows16(const void* ptr, const int64_t* st) {
   return (reinterpret_cast<uintptr_t>(ptr) % 16) == 0 && (st[0] * 2) % 16 == 0 &&
@@ -1576,9 +1583,11 @@ cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* ha
   std::memset(&p, 0, sizeof(p));
   if (!tcx::encode(&p.tm_q, a.q, dtype, a.B, a.H, a.S, a.D, a.qs, kBM) ||
       !tcx::encode(&p.tm_do, a.dout, dtype, a.B, a.H, a.S, a.D, a.dos, kBM) ||
-      !tcx::encode(&p.tm_k, a.k, dtype, a.B, a.Hkv, a.S, a.D, a.ks, kKT) ||
-      !tcx::encode(&p.tm_v, a.v, dtype, a.B, a.Hkv, a.S, a.D, a.vs, kKT))
+      !tcx::encode(&p.tm_k, a.k, dtype, a.B, a.Hkv, a.Sk, a.D, a.ks, kKT) ||
+      !tcx::encode(&p.tm_v, a.v, dtype, a.B, a.Hkv, a.Sk, a.D, a.vs, kKT))
     return cudaErrorInvalidValue;
+  p.r0 = a.r0;
+  p.Sk = a.Sk;
   p.dq = a.dq;
   p.dk32 = a.dk32;
   p.dv32 = a.dv32;

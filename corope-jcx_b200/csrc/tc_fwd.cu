@@ -85,6 +85,7 @@ struct Params {
   int64_t bias_rs;
   int64_t os[3];
   int B, H, Hkv, S;
+  int r0;  // sequence position of row 0 of q / o (a multiple of kBM)
   float theta;
   int nrow[8];          // B-operand rows read by K-step s (multiple of 16, or 0)
   int nb;               // K^(m) buffers per half window (1 or 2)
@@ -159,8 +160,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
   const int qt = gridDim.x - 1 - blockIdx.x;  // longest query tiles first
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (P.H / P.Hkv);
-  const int q0 = qt * kBM;
-  const int S = P.S;
+  const int q0 = P.r0 + qt * kBM;  // sequence position of the tile's first row
+  const int S = P.r0 + P.S;        // end of this launch's rows (sequence position)
   const int W0 = min(S - 1, q0 + kBM - 1) / kW;  // highest window
   const int T0 = W0 / 4;                         // highest K/V tile
 
@@ -215,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         prefetch_tmap(&P.tm_v);
         mbar_expect_tx(&bars[B_Q], NS * 16384);
         for (int s = 0; s < NS; ++s)
-          tma_load_4d(smem + L::Q + s * 16384, &P.tm_q, &bars[B_Q], 64 * s, q0, h, b);
+          tma_load_4d(smem + L::Q + s * 16384, &P.tm_q, &bars[B_Q], 64 * s, q0 - P.r0, h, b);
         int last_use[2] = {-1, -1};
         for (int n = 0; T0 - n >= 0; ++n) {
           const int tile = T0 - n, st = n & 1, u = n >> 1;
@@ -605,7 +606,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       tc_fence_after();
       const float ltot = lsum + lds32f(s_xch + (256 + (rg ^ 1) * 128 + r) * 4);
       const float inv = 1.0f / ltot;
-      T* orow = reinterpret_cast<T*>(P.o) + b * P.os[0] + h * P.os[1] + (int64_t)t * P.os[2] +
+      T* orow = reinterpret_cast<T*>(P.o) + b * P.os[0] + h * P.os[1] +
+                (int64_t)(t - P.r0) * P.os[2] +
                 rg * (D / 2);
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
@@ -623,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         }
       }
       if (t < S && rg == 0) {
-        const int64_t ri = ((int64_t)b * P.H + h) * S + t;
+        const int64_t ri = ((int64_t)b * P.H + h) * P.S + (t - P.r0);
         const float M = m_true * 0.6931471805599453f;
         const float Lv = ltot * exp2f(m_used - m_true);
         if (P.m) P.m[ri] = M;
@@ -708,9 +710,10 @@ cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st) {
   std::lock_guard<std::mutex> g(mu);
   std::memset(&p, 0, sizeof(p));
   if (!encode(&p.tm_q, a.q, dtype, a.B, a.H, a.S, a.D, a.qs, kBM) ||
-      !encode(&p.tm_k, a.k, dtype, a.B, a.Hkv, a.S, a.D, a.ks, kKT) ||
-      !encode(&p.tm_v, a.v, dtype, a.B, a.Hkv, a.S, a.D, a.vs, kKT))
+      !encode(&p.tm_k, a.k, dtype, a.B, a.Hkv, a.Sk, a.D, a.ks, kKT) ||
+      !encode(&p.tm_v, a.v, dtype, a.B, a.Hkv, a.Sk, a.D, a.vs, kKT))
     return cudaErrorInvalidValue;
+  p.r0 = a.r0;
   p.o = a.o;
   p.m = a.m; p.l = a.l; p.a = a.a; p.lse = a.lse;
   p.thetas = a.thetas; p.theta = a.theta;

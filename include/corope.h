@@ -143,6 +143,40 @@ int corope_bwd_noalloc(const corope_bwd_params_t *p, corope_stream_t stream);
 /* Size in bytes of the built-in scratch of corope_bwd_noalloc. */
 size_t corope_bwd_noalloc_scratch_bytes(void);
 
+/* ---- Query chunks (sequence-sharded callers).  No counterpart in the
+ * reference, which runs whole sequences on one device.  A rank of a
+ * sequence-sharded job holds some query rows of a sequence and, after an
+ * all-gather, every key / value row: the chunk calls compute exactly the
+ * rows a whole-sequence call would produce for those query positions.
+ *
+ * In the params, q, o, m, l, a, lse, dout and dq hold `seq_len` rows that
+ * sit at sequence positions q_row0 .. q_row0 + seq_len - 1; k and v hold
+ * kv_len rows from position 0; a bias is indexed by sequence positions. */
+typedef struct {
+  int64_t q_row0;      /* sequence position of row 0 of q; a multiple of 128 */
+  int32_t kv_len;      /* rows of k and v; at least q_row0 + seq_len */
+  int32_t reserved;    /* 0 */
+  float *dk_accum;     /* backward: fp32 [B, kv_heads, kv_len, D], contiguous;
+                          the call ADDS this chunk's dk (zero it once first) */
+  float *dv_accum;     /* backward: the same for dv */
+} corope_chunk_t;
+
+/* Forward of a query chunk (MHA, or MQA/GQA with kv_heads dividing heads). */
+int corope_fwd_chunk(const corope_fwd_params_t *p, const corope_chunk_t *chunk,
+                     corope_stream_t stream);
+
+/* Workspace of corope_bwd_chunk at its fastest, and the least it accepts
+ * (delta and lse rows only; dk / dv go to the chunk's accumulators). */
+size_t corope_bwd_chunk_workspace_bytes(const corope_bwd_params_t *p, const corope_chunk_t *chunk);
+size_t corope_bwd_chunk_min_workspace_bytes(const corope_bwd_params_t *p,
+                                            const corope_chunk_t *chunk);
+
+/* Backward of a query chunk: writes dq of its rows and adds its dk, dv
+ * (all kv_len key rows; keys past the chunk's last row get nothing) to
+ * chunk->dk_accum / dv_accum; p->dk and p->dv are not used. */
+int corope_bwd_chunk(const corope_bwd_params_t *p, const corope_chunk_t *chunk,
+                     corope_stream_t stream);
+
 /* Message for the last non-zero status returned on this thread. */
 const char *corope_last_error(void);
 
@@ -159,7 +193,7 @@ size_t corope_params_size(int which);
 /* ABI version of this header (COROPE_ABI_VERSION). */
 int corope_abi_version(void);
 
-#define COROPE_ABI_VERSION 1
+#define COROPE_ABI_VERSION 2
 
 #ifdef __cplusplus
 }

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_struct_layout():
     lib = _lib.load_library()
-    assert lib.corope_abi_version() == 1
+    assert lib.corope_abi_version() == 2
     assert lib.corope_params_size(0) == ctypes.sizeof(_lib.FwdParams)
     assert lib.corope_params_size(1) == ctypes.sizeof(_lib.BwdParams)
 
@@ -93,3 +93,34 @@ def test_backward_workspace_checks():
     assert lib.corope_bwd(ctypes.byref(p), None) == _lib.ERR_WORKSPACE
     p.workspace, p.workspace_bytes = fake, need - 1
     assert lib.corope_bwd(ctypes.byref(p), None) == _lib.ERR_WORKSPACE
+
+
+def test_chunk_argument_checks_without_gpu():
+    """corope_fwd_chunk / corope_bwd_chunk refuse a NULL chunk, an offset off
+    the 128-row tiles, a key range shorter than the chunk and missing fp32
+    accumulators before touching the device."""
+    lib = _lib.load_library()
+    p = _fwd_params(S=128)
+    c = _lib.ChunkParams()
+    assert lib.corope_fwd_chunk(ctypes.byref(p), None, None) == _lib.ERR_INVALID
+    c.q_row0, c.kv_len = 100, 1024
+    assert lib.corope_fwd_chunk(ctypes.byref(p), ctypes.byref(c), None) == _lib.ERR_INVALID
+    c.q_row0, c.kv_len = 256, 300
+    assert lib.corope_fwd_chunk(ctypes.byref(p), ctypes.byref(c), None) == _lib.ERR_INVALID
+    assert b"kv_len" in lib.corope_last_error()
+    b = _lib.BwdParams()
+    fake = 1 << 20
+    b.q = b.k = b.v = b.o = b.dout = b.dq = fake
+    b.m = b.l = b.a = fake
+    st = _lib._I64x3(4 * 128 * 64, 128 * 64, 64)
+    b.q_stride = b.k_stride = b.v_stride = b.o_stride = b.do_stride = b.dq_stride = st
+    b.batch, b.heads, b.kv_heads, b.seq_len, b.head_dim = 1, 4, 4, 128, 64
+    b.sm_scale, b.theta, b.causal, b.dtype = 0.125, 1e4, 1, 2
+    c.q_row0, c.kv_len = 256, 512
+    assert lib.corope_bwd_chunk(ctypes.byref(b), ctypes.byref(c), None) == _lib.ERR_INVALID
+    assert b"dk_accum" in lib.corope_last_error()
+    # the chunk workspace holds delta / lse rows and the chunk's hand-off only
+    lo = lib.corope_bwd_chunk_min_workspace_bytes(ctypes.byref(b), ctypes.byref(c))
+    hi = lib.corope_bwd_chunk_workspace_bytes(ctypes.byref(b), ctypes.byref(c))
+    assert lo == 2 * 4 * 128 * 4 and hi > lo
+    assert hi - lo == 4 * ((256 + 127) // 16 + 1) * 20992

@@ -419,3 +419,60 @@ def test_backward_with_contextual_bias(algo, D):
         assert torch.isfinite(mine).all(), name
         assert maxabs(mine, r) < G_MAXABS, name
         assert rel_l2(mine, r) < REL_L2, name
+
+
+@pytest.mark.parametrize("algo,D,hkv", [("tensor", 128, None), ("tensor", 64, 1), ("exact", 64, None)])
+def test_query_chunks_equal_whole_sequence(algo, D, hkv):
+    """corope_fwd_chunk / corope_bwd_chunk over the query chunks of a
+    sequence (as the ranks of a sequence-sharded job would run them, here one
+    after the other on one GPU) reproduce the whole-sequence calls: O, M, L, A
+    and dq bit for bit (each row is computed the same way), dk / dv up to the
+    order of the fp32 additions."""
+    from CoROPE import _lib
+    B, H, S = 2, 4, 1024
+    (q, k, v, do), cpu = inputs(B, H, S, D, 81, torch.bfloat16, hkv=hkv)
+    sm = 1 / math.sqrt(D)
+    mqa = hkv is not None
+    fwd = co_rope_mqa_forward if mqa else co_rope_forward
+    saved, o = fwd(q, k, v, sm, theta=5e5, algo=algo)
+    m, l, a = saved[4], saved[5], saved[6]
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    _lib.bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm, 5e5, algo=algo)
+    # four query chunks, visited in a shuffled order
+    bounds = [(0, 256), (256, 640), (640, 768), (768, 1024)]
+    oc, dqc = torch.empty_like(o), torch.empty_like(dq)
+    dk_acc = torch.zeros(k.shape, dtype=torch.float32, device=DEV)
+    dv_acc = torch.zeros_like(dk_acc)
+    for r0, r1 in (bounds[2], bounds[0], bounds[3], bounds[1]):
+        n = r1 - r0
+        mc, lc, ac = (torch.empty(B, H, n, device=DEV) for _ in range(3))
+        _lib.fwd(q[:, :, r0:r1], k, v, oc[:, :, r0:r1], mc, lc, ac, None, sm, 5e5, algo=algo,
+                 mqa=True, q_row0=r0)
+        assert torch.equal(mc, m[:, :, r0:r1]) and torch.equal(lc, l[:, :, r0:r1])
+        assert torch.equal(ac, a[:, :, r0:r1])
+        _lib.bwd(q[:, :, r0:r1], k, v, oc[:, :, r0:r1], do[:, :, r0:r1], mc, lc, ac,
+                 dqc[:, :, r0:r1], None, None, sm, 5e5, algo=algo, q_row0=r0,
+                 dk_accum=dk_acc, dv_accum=dv_acc)
+    torch.cuda.synchronize()
+    assert _lib.take_device_error() == 0
+    assert torch.equal(oc, o)
+    assert torch.equal(dqc, dq)
+    for name, mine, ref in (("dk", dk_acc, dk), ("dv", dv_acc, dv)):
+        ref = ref.float()
+        assert (mine - ref).abs().max().item() <= 1e-2 * ref.abs().max().item() + 1e-6, name
+        assert rel_l2(mine.to(ref.dtype), ref) < 5e-3, name
+
+
+def test_query_chunk_argument_checks():
+    """Chunk offsets off the 128-row tiles and key ranges too short for the
+    chunk are refused before any device work."""
+    from CoROPE import _lib
+    (q, k, v, _), _ = inputs(1, 2, 256, 64, 5, torch.bfloat16)
+    o = torch.empty_like(q)
+    m, l, a = (torch.empty(1, 2, 128, device=DEV) for _ in range(3))
+    with pytest.raises(ValueError):
+        _lib.fwd(q[:, :, 100:228], k, v, o[:, :, 100:228], m, l, a, None, 0.125, 1e4,
+                 mqa=True, q_row0=100)
+    with pytest.raises(ValueError):
+        _lib.fwd(q[:, :, 128:256], k[:, :, :200], v[:, :, :200], o[:, :, 128:256], m, l, a,
+                 None, 0.125, 1e4, mqa=True, q_row0=128)
