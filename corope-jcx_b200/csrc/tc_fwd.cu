@@ -373,17 +373,18 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             if (i0 + j < my_n) {
+              // (-i)^m: odd terms swap the pair's components (one byte
+              // permute), terms 2, 3 mod 4 negate one or both (a sign-bit xor)
               const uint32_t fl = d[j].y >> 16;
-              const bool swp = fl & 1u;
-              const float sre = (fl & 2u) ? -1.f : 1.f, sim = (fl & 4u) ? -1.f : 1.f;
+              const uint32_t sel = (fl & 1u) ? 0x1032u : 0x3210u;
+              const uint32_t sgn = ((fl & 2u) ? 0x8000u : 0u) | ((fl & 4u) ? 0x80000000u : 0u);
               const uint32_t in[4] = {kv[j].x, kv[j].y, kv[j].z, kv[j].w};
               const float cfa[4] = {cf[j].x, cf[j].y, cf[j].z, cf[j].w};
               uint32_t out[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                const float ke = E::lo(in[e]), ko = E::hi(in[e]);
-                const float a = swp ? ko : ke, bq = swp ? ke : ko;
-                out[e] = E::pack(sre * cfa[e] * a, sim * cfa[e] * bq);
+                const uint32_t wv = __byte_perm(in[e], 0u, sel) ^ sgn;
+                out[e] = E::pack(cfa[e] * E::lo(wv), cfa[e] * E::hi(wv));
               }
               sts128(bt + (d[j].y & 0xffffu), make_uint4(out[0], out[1], out[2], out[3]));
             }
