@@ -40,6 +40,7 @@ class FwdParams(ctypes.Structure):
         ("seq_len", ctypes.c_int32), ("head_dim", ctypes.c_int32),
         ("sm_scale", ctypes.c_float), ("theta", ctypes.c_float),
         ("causal", ctypes.c_int32), ("dtype", ctypes.c_int32), ("algo", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
     ]
 
 
@@ -110,6 +111,10 @@ def load_library():
             lib.corope_abi_version.argtypes = []
             lib.corope_abi_version.restype = ctypes.c_int
             chunk_p = ctypes.POINTER(ChunkParams)
+            lib.corope_fwd_workspace_bytes.argtypes = [ctypes.POINTER(FwdParams)]
+            lib.corope_fwd_workspace_bytes.restype = ctypes.c_size_t
+            lib.corope_fwd_chunk_workspace_bytes.argtypes = [ctypes.POINTER(FwdParams), chunk_p]
+            lib.corope_fwd_chunk_workspace_bytes.restype = ctypes.c_size_t
             lib.corope_fwd_chunk.argtypes = [ctypes.POINTER(FwdParams), chunk_p, ctypes.c_void_p]
             lib.corope_fwd_chunk.restype = ctypes.c_int
             lib.corope_bwd_chunk.argtypes = [ctypes.POINTER(BwdParams), chunk_p, ctypes.c_void_p]
@@ -192,10 +197,12 @@ def default_scale(head_dim: int, sm_scale) -> float:
 
 
 def fwd(q, k, v, o, m, l, a, lse, sm_scale, theta, bias=None, algo="auto", thetas=None,
-        mqa=False, q_row0=None):
+        mqa=False, q_row0=None, workspace=True):
     """Launch corope_fwd / corope_mqa_fwd on the current stream of q.  With
     ``q_row0`` (corope_fwd_chunk) q, o, m, l, a, lse are the query rows at
-    sequence positions q_row0.. and k, v hold every key row from 0."""
+    sequence positions q_row0.. and k, v hold every key row from 0.
+    ``workspace=False`` runs the tensor-core forward without its scaled-key
+    panels (the kernel builds the operands itself; same results)."""
     lib = load_library()
     B, H, S, D = q.shape
     p = FwdParams()
@@ -212,9 +219,18 @@ def fwd(q, k, v, o, m, l, a, lse, sm_scale, theta, bias=None, algo="auto", theta
     p.sm_scale, p.theta = float(sm_scale), float(theta)
     p.causal, p.dtype, p.algo = 1, _dtype_code(q), algo_code(algo)
     stream = torch.cuda.current_stream(q.device).cuda_stream
+    c = None
     if q_row0 is not None:
         c = ChunkParams()
         c.q_row0, c.kv_len = int(q_row0), k.shape[2]
+    ws = None
+    if workspace:
+        nbytes = (lib.corope_fwd_workspace_bytes(ctypes.byref(p)) if c is None else
+                  lib.corope_fwd_chunk_workspace_bytes(ctypes.byref(p), ctypes.byref(c)))
+        if nbytes:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+            p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
+    if c is not None:
         with torch.cuda.device(q.device):
             rc = lib.corope_fwd_chunk(ctypes.byref(p), ctypes.byref(c), ctypes.c_void_p(stream))
         _check(rc, "corope_fwd_chunk")

@@ -14,7 +14,9 @@ bool exact_supports_head_dim(int D);
 // tensor-core path (tc_fwd.cu); returns cudaErrorNotSupported when the
 // shape is outside its coverage
 bool tc_fwd_supported(const FwdArgs& a, int dtype);
-cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st);
+cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st, void* ws,
+                          size_t ws_bytes);
+size_t tc_fwd_workspace_bytes(const FwdArgs& a);
 int tc_take_device_error();
 bool tc_bwd_supported(const BwdArgs& a, int dtype);
 cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* handoff,
@@ -155,8 +157,11 @@ static int fwd_common(const corope_fwd_params_t* p, corope_stream_t stream, bool
                 "tensor-core forward needs bf16/f16, head_dim 64 or 128 and 16-byte aligned rows");
   if (p->algo != COROPE_ALGO_EXACT && p->algo != COROPE_ALGO_AUTO && p->algo != COROPE_ALGO_TENSOR)
     return fail(COROPE_ERR_INVALID, "unknown algo %d", p->algo);
-  cudaError_t e = (p->algo != COROPE_ALGO_EXACT && tc_ok) ? tc_fwd_launch(a, p->dtype, st)
-                                                          : exact_fwd_launch(a, p->dtype, st);
+  if (p->workspace && !aligned(p->workspace, 256))
+    return fail(COROPE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  cudaError_t e = (p->algo != COROPE_ALGO_EXACT && tc_ok)
+                      ? tc_fwd_launch(a, p->dtype, st, p->workspace, p->workspace_bytes)
+                      : exact_fwd_launch(a, p->dtype, st);
   if (e != cudaSuccess) return cuda_fail(e, "forward launch");
   return COROPE_OK;
 }
@@ -195,6 +200,24 @@ extern "C" {
 
 int corope_fwd(const corope_fwd_params_t* p, corope_stream_t stream) {
   return fwd_common(p, stream, false);
+}
+
+size_t corope_fwd_workspace_bytes(const corope_fwd_params_t* p) {
+  if (!p || p->batch <= 0 || p->heads <= 0 || p->kv_heads <= 0 || p->seq_len <= 0 ||
+      (p->head_dim != 64 && p->head_dim != 128) || p->algo == COROPE_ALGO_EXACT ||
+      (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16) || !(p->theta > 0.f))
+    return 0;
+  FwdArgs a{};
+  a.B = p->batch; a.Hkv = p->kv_heads; a.Sk = p->seq_len; a.D = p->head_dim;
+  a.theta = p->theta; a.sm_scale = p->sm_scale;
+  return tc_fwd_workspace_bytes(a);
+}
+
+size_t corope_fwd_chunk_workspace_bytes(const corope_fwd_params_t* p, const corope_chunk_t* c) {
+  if (!c || c->kv_len <= 0) return 0;
+  corope_fwd_params_t q = *p;
+  q.seq_len = c->kv_len;
+  return corope_fwd_workspace_bytes(&q);
 }
 
 int corope_mqa_fwd(const corope_fwd_params_t* p, corope_stream_t stream) {

@@ -78,6 +78,9 @@ enum : int {
 
 struct Params {
   CUtensorMap tm_q, tm_k, tm_v;
+  CUtensorMap tm_km[2];  // precomputed K^(m) panels per slab (KMT launches)
+  int km_nhw;            // half windows per (b, kv head) in the panels
+  int km_rows[2];        // panel rows per slab
   void* o;
   float *m, *l, *a, *lse;
   const float* thetas;
@@ -138,7 +141,10 @@ enum {
 using tcx::ElemTraits;
 using tcx::sigmoid_f;
 
-template <typename T, int D, bool HAS_BIAS>
+// KMT: the K^(m) operands come from precomputed panels in global memory
+// (tcx::panel_kernel) by TMA, one copy per slab and half window, instead of
+// being built from the K tiles by warps 12-15.
+template <typename T, int D, bool HAS_BIAS, bool KMT>
 __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant__ Params P) {
   using L = Layout<D>;
   using E = ElemTraits<T>;
@@ -169,13 +175,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
     mbar_init(&bars[B_Q], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[B_KVF + i], 1);
-      mbar_init(&bars[B_KVE + i], 1 + 128);
+      mbar_init(&bars[B_KVE + i], KMT ? 1 : 1 + 128);
       mbar_init(&bars[B_SG + i], 1);
       mbar_init(&bars[B_GF + i], 1);
       mbar_init(&bars[B_GE + i], 256);
     }
     for (int i = 0; i < 4; ++i) {
-      mbar_init(&bars[B_BF + i], 128);
+      mbar_init(&bars[B_BF + i], KMT ? 1 : 128);
       mbar_init(&bars[B_BE + i], 1);
     }
     mbar_init(&bars[B_AV], 256);
@@ -300,6 +306,36 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         mma_commit(&bars[B_DRAIN2]);
         mbar_wait(&bars[B_DRAIN2], 0, err, kErrDrain);
       }
+    }
+    __syncwarp();
+    regs_inc<128>();
+  } else if (warp >= 12 && KMT) {
+    regs_dec<kBldRegs>();
+    named_bar(1, kThreads);
+    // ------------------------------------------------- K^(m) panel loads
+    if (warp == 12 && lane == 0) {
+      prefetch_tmap(&P.tm_km[0]);
+      if (NS > 1) prefetch_tmap(&P.tm_km[1]);
+      const uint32_t bytes = (P.km_rows[0] + (NS > 1 ? P.km_rows[1] : 0)) * 128;
+      const int panel0 = (b * P.Hkv + hk) * P.km_nhw;
+      int last[4] = {-1, -1, -1, -1};  // [half][buffer]: last use issued
+      bool ok = true;
+      for (int w = W0; ok && w >= 0; --w) {
+        const int k = W0 - w, buf = k % nb, use = k / nb;
+        for (int hh = 0; hh < 2; ++hh) {
+          const int i = 2 * hh + buf;
+          if (use > 0 && !(ok = mbar_wait(&bars[B_BE + i], (use - 1) & 1, err, kErrBEmpty))) break;
+          mbar_expect_tx(&bars[B_BF + i], bytes);
+          uint8_t* dst = smem + L::BOP + (hh * nb + buf) * P.b_buf_bytes;
+          for (int s = 0; s < NS; ++s)
+            tma_load_3d(dst + P.b_slab_off[s], &P.tm_km[s], &bars[B_BF + i], 0, 0,
+                        panel0 + 2 * w + hh);
+          last[i] = use;
+        }
+      }
+      // no copy may still be in flight when the CTA exits
+      for (int i = 0; i < 4; ++i)
+        if (last[i] >= 0) mbar_wait(&bars[B_BF + i], last[i] & 1, err, kErrDrain);
     }
     __syncwarp();
     regs_inc<128>();
@@ -668,24 +704,53 @@ static int plan_buffers(Params& p) {
   return L::BOP + 2 * p.nb * p.b_buf_bytes + 1024;
 }
 
+template <typename T> constexpr int E_dtype() {
+  return ElemTraits<T>::kBf16 ? COROPE_DTYPE_BF16 : COROPE_DTYPE_F16;
+}
+
+template <typename T, int D, bool HAS_BIAS, bool KMT>
+static cudaError_t launch_k(const Params& p, int smem, dim3 grid, cudaStream_t st) {
+  auto kern = fwd_kernel<T, D, HAS_BIAS, KMT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kSmemLimit);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+// With a workspace of tcx::panel_bytes<kM> bytes the K^(m) operands are
+// written once by tcx::panel_kernel and loaded by TMA; without one the
+// forward kernel's builder warps make them from the K tiles.
 template <typename T, int D>
-static cudaError_t launch_t(Params& p, const FwdArgs& a, cudaStream_t st) {
+static cudaError_t launch_t(Params& p, const FwdArgs& a, cudaStream_t st, void* ws,
+                            size_t ws_bytes) {
   const int smem = plan_buffers<D>(p);
   if (smem > kSmemLimit) return cudaErrorInvalidValue;
   dim3 grid((a.S + kBM - 1) / kBM, a.H, a.B);
-  cudaError_t e;
-  if (a.bias) {
-    auto kern = fwd_kernel<T, D, true>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  static tcx::PanelArgs pa;  // guarded by the caller's lock
+  const size_t need = tcx::panel_bytes<kM>(a.B, a.Hkv, a.Sk, D, a.theta, a.sm_scale, &pa);
+  const bool kmt = ws && need > 0 && ws_bytes >= need;
+  if (kmt) {
+    const int64_t np = tcx::panel_count(a.B, a.Hkv, a.Sk);
+    pa.k = a.k;
+    for (int i = 0; i < 3; ++i) pa.ks[i] = a.ks[i];
+    pa.out[0] = ws;
+    pa.out[1] = static_cast<uint8_t*>(ws) + np * pa.rows[0] * 128;
+    for (int s = 0; s < D / 64; ++s)
+      if (!tcx::encode_panels(&p.tm_km[s], pa.out[s], E_dtype<T>(), pa.rows[s], np))
+        return cudaErrorInvalidValue;
+    p.km_nhw = pa.nhw;
+    p.km_rows[0] = pa.rows[0];
+    p.km_rows[1] = pa.rows[1];
+    tcx::panel_kernel<T, D><<<dim3(pa.nhw, a.B * a.Hkv), 128, 0, st>>>(pa);
+    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    kern<<<grid, kThreads, smem, st>>>(p);
-  } else {
-    auto kern = fwd_kernel<T, D, false>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    if (e != cudaSuccess) return e;
-    kern<<<grid, kThreads, smem, st>>>(p);
   }
-  return cudaGetLastError();
+  if (a.bias)
+    return kmt ? launch_k<T, D, true, true>(p, smem, grid, st)
+               : launch_k<T, D, true, false>(p, smem, grid, st);
+  return kmt ? launch_k<T, D, false, true>(p, smem, grid, st)
+             : launch_k<T, D, false, false>(p, smem, grid, st);
 }
 
 }  // namespace tc
@@ -704,7 +769,12 @@ bool tc_fwd_supported(const FwdArgs& a, int dtype) {
   return tc::get_encoder() != nullptr;
 }
 
-cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st) {
+size_t tc_fwd_workspace_bytes(const FwdArgs& a) {
+  return tcx::panel_bytes<tc::kM>(a.B, a.Hkv, a.Sk, a.D, a.theta, a.sm_scale);
+}
+
+cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st, void* ws,
+                          size_t ws_bytes) {
   using namespace tc;
   static Params p;  // large (>4 KB); filled per call under a lock
   static std::mutex mu;
@@ -724,8 +794,10 @@ cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st) {
   fill_coefficients(p, a.D, a.theta, a.sm_scale);
   const bool bf = dtype == COROPE_DTYPE_BF16;
   if (a.D == 64)
-    return bf ? launch_t<__nv_bfloat16, 64>(p, a, st) : launch_t<__half, 64>(p, a, st);
-  return bf ? launch_t<__nv_bfloat16, 128>(p, a, st) : launch_t<__half, 128>(p, a, st);
+    return bf ? launch_t<__nv_bfloat16, 64>(p, a, st, ws, ws_bytes)
+              : launch_t<__half, 64>(p, a, st, ws, ws_bytes);
+  return bf ? launch_t<__nv_bfloat16, 128>(p, a, st, ws, ws_bytes)
+            : launch_t<__half, 128>(p, a, st, ws, ws_bytes);
 }
 
 }  // namespace corope

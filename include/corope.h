@@ -76,6 +76,8 @@ typedef struct {
   int32_t causal; /* must be 1 */
   int32_t dtype;  /* corope_dtype_t */
   int32_t algo;   /* corope_algo_t */
+  void *workspace;          /* optional device scratch, 256-byte aligned */
+  size_t workspace_bytes;   /* see corope_fwd_workspace_bytes */
 } corope_fwd_params_t;
 
 typedef struct {
@@ -95,6 +97,12 @@ typedef struct {
   void *workspace;                    /* device scratch, 256-byte aligned */
   size_t workspace_bytes;
 } corope_bwd_params_t;
+
+/* Bytes of workspace with which the tensor-core forward reads its scaled-key
+ * operands from panels written once per call (one launch before the forward
+ * kernel) instead of rebuilding them in every CTA; 0 when the path has none.
+ * Any workspace smaller than this (or none) gives the same results. */
+size_t corope_fwd_workspace_bytes(const corope_fwd_params_t *p);
 
 /* Forward.  Replaces the launch of co_rope_fwd_kernel in
  * CoROPE/forward.py:123-178 (host wrapper co_rope_forward, launch at
@@ -161,9 +169,11 @@ typedef struct {
   float *dv_accum;     /* backward: the same for dv */
 } corope_chunk_t;
 
-/* Forward of a query chunk (MHA, or MQA/GQA with kv_heads dividing heads). */
+/* Forward of a query chunk (MHA, or MQA/GQA with kv_heads dividing heads),
+ * and its optional workspace (panels of all kv_len keys). */
 int corope_fwd_chunk(const corope_fwd_params_t *p, const corope_chunk_t *chunk,
                      corope_stream_t stream);
+size_t corope_fwd_chunk_workspace_bytes(const corope_fwd_params_t *p, const corope_chunk_t *chunk);
 
 /* Workspace of corope_bwd_chunk at its fastest, and the least it accepts
  * (delta and lse rows only; dk / dv go to the chunk's accumulators). */
@@ -193,7 +203,7 @@ size_t corope_params_size(int which);
 /* ABI version of this header (COROPE_ABI_VERSION). */
 int corope_abi_version(void);
 
-#define COROPE_ABI_VERSION 2
+#define COROPE_ABI_VERSION 3
 
 #ifdef __cplusplus
 }

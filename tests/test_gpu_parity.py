@@ -476,3 +476,26 @@ def test_query_chunk_argument_checks():
     with pytest.raises(ValueError):
         _lib.fwd(q[:, :, 128:256], k[:, :, :200], v[:, :, :200], o[:, :, 128:256], m, l, a,
                  None, 0.125, 1e4, mqa=True, q_row0=128)
+
+
+@pytest.mark.parametrize("D,hkv,theta,bias", [(128, None, 1e4, False), (64, None, 5e5, True),
+                                              (128, 1, 5e5, False), (128, 2, 1e4, True)])
+def test_forward_panels_equal_in_kernel_builders(D, hkv, theta, bias):
+    """The tensor-core forward with its scaled-key panels (written once per
+    call, loaded by TMA) and without them (built in every CTA) gets the same
+    operand bits, so O, M, L, A agree bit for bit."""
+    from CoROPE import _lib
+    B, H, S = 2, 4, 700
+    (q, k, v, _), _ = inputs(B, H, S, D, 91, torch.bfloat16, hkv=hkv)
+    bias_t = (torch.randn(S, S, generator=torch.Generator().manual_seed(9)) * 0.3).to(DEV) if bias else None
+    outs = []
+    for ws in (True, False):
+        o = torch.empty_like(q)
+        m, l, a = (torch.empty(B, H, S, device=DEV) for _ in range(3))
+        _lib.fwd(q, k, v, o, m, l, a, None, 1 / math.sqrt(D), theta, bias=bias_t, algo="tensor",
+                 mqa=True, workspace=ws)
+        outs.append((o, m, l, a))
+    torch.cuda.synchronize()
+    assert _lib.take_device_error() == 0
+    for x, y in zip(*outs):
+        assert torch.equal(x, y)
