@@ -119,6 +119,8 @@ def load_library():
             lib.corope_fwd_chunk.restype = ctypes.c_int
             lib.corope_bwd_chunk.argtypes = [ctypes.POINTER(BwdParams), chunk_p, ctypes.c_void_p]
             lib.corope_bwd_chunk.restype = ctypes.c_int
+            lib.corope_bwd_panel_bytes.argtypes = [ctypes.POINTER(BwdParams)]
+            lib.corope_bwd_panel_bytes.restype = ctypes.c_size_t
             for name in ("corope_bwd_chunk_workspace_bytes", "corope_bwd_chunk_min_workspace_bytes"):
                 getattr(lib, name).argtypes = [ctypes.POINTER(BwdParams), chunk_p]
                 getattr(lib, name).restype = ctypes.c_size_t
@@ -252,23 +254,33 @@ def auto_workspace_bytes(lib, p, device, chunk=None):
     if chunk is None:
         full = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
         least = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
+        panels = lib.corope_bwd_panel_bytes(ctypes.byref(p))
     else:
         full = lib.corope_bwd_chunk_workspace_bytes(ctypes.byref(p), ctypes.byref(chunk))
         least = lib.corope_bwd_chunk_min_workspace_bytes(ctypes.byref(p), ctypes.byref(chunk))
+        keys = BwdParams.from_buffer_copy(p)
+        keys.seq_len = chunk.kv_len
+        panels = lib.corope_bwd_panel_bytes(ctypes.byref(keys))
     free, _ = torch.cuda.mem_get_info(device)
     budget = (free + torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)) // 4
-    return fit_workspace(full, least, p.batch * p.heads, budget)
+    return fit_workspace(full, least, p.batch * p.heads, budget, panels)
 
 
-def fit_workspace(full, least, units, budget):
-    """Largest of full / least + k whole hand-off slices / least within
-    `budget` bytes (least even when it does not fit: the call then fails in
-    the allocator, as the caller's own allocation would)."""
+def fit_workspace(full, least, units, budget, panels=0):
+    """Largest of full / least + panels + k whole hand-off slices / least
+    within `budget` bytes (least even when it does not fit: the call then
+    fails in the allocator, as the caller's own allocation would).  The
+    library lays the workspace out as [least][panels][hand-off]."""
     if full <= budget or full == least:
         return full
-    per = (full - least) // units  # >= one slice's bytes (the region is 256-aligned)
-    slices = max(0, (budget - least) // per) if per > 0 else 0
-    return least + min(slices, units) * per
+    if least + panels > budget:
+        return least
+    base = least + panels
+    per = (full - base) // units  # >= one slice's bytes (the region is 256-aligned)
+    if per <= 0:
+        return base
+    slices = max(0, (budget - base) // per)
+    return base + min(slices, units) * per
 
 
 def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="auto",

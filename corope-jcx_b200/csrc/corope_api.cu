@@ -20,7 +20,8 @@ size_t tc_fwd_workspace_bytes(const FwdArgs& a);
 int tc_take_device_error();
 bool tc_bwd_supported(const BwdArgs& a, int dtype);
 cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* handoff,
-                          size_t handoff_bytes);
+                          size_t handoff_bytes, void* panels);
+size_t tc_bwd_panel_bytes(const BwdArgs& a);
 int64_t tc_bwd_handoff_bytes_per_bh(int S, int r0);
 int tcb_take_device_error();
 cudaError_t bwd_pre_launch(const BwdArgs& a, int dtype, cudaStream_t st);
@@ -188,6 +189,18 @@ static size_t bwd_handoff_ws(const corope_bwd_params_t* p, int r0 = 0) {
                   (size_t)tc_bwd_handoff_bytes_per_bh(p->seq_len, r0));
 }
 
+// Optional scaled-key panels of the dQ kernel (tensor-core path), placed
+// right after the minimum workspace when the workspace has room for them.
+static size_t bwd_panel_ws(const corope_bwd_params_t* p, int kv_len) {
+  if ((p->head_dim != 64 && p->head_dim != 128) || p->algo == COROPE_ALGO_EXACT ||
+      (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16) || !(p->theta > 0.f))
+    return 0;
+  BwdArgs a{};
+  a.B = p->batch; a.Hkv = p->kv_heads; a.Sk = kv_len; a.D = p->head_dim;
+  a.theta = p->theta; a.sm_scale = p->sm_scale;
+  return align256(tc_bwd_panel_bytes(a));
+}
+
 static bool sizes_ok(const corope_bwd_params_t* p) {
   return p && p->batch > 0 && p->heads > 0 && p->kv_heads > 0 && p->seq_len > 0 &&
          p->head_dim > 0;
@@ -226,7 +239,12 @@ int corope_mqa_fwd(const corope_fwd_params_t* p, corope_stream_t stream) {
 
 size_t corope_bwd_workspace_bytes(const corope_bwd_params_t* p) {
   if (!sizes_ok(p)) return 0;
-  return bwd_ws(p) + bwd_handoff_ws(p);
+  return bwd_ws(p) + bwd_panel_ws(p, p->seq_len) + bwd_handoff_ws(p);
+}
+
+size_t corope_bwd_panel_bytes(const corope_bwd_params_t* p) {
+  if (!sizes_ok(p)) return 0;
+  return bwd_panel_ws(p, p->seq_len);
 }
 
 size_t corope_bwd_min_workspace_bytes(const corope_bwd_params_t* p) {
@@ -245,8 +263,8 @@ int corope_fwd_chunk(const corope_fwd_params_t* p, const corope_chunk_t* chunk,
 }
 
 size_t corope_bwd_chunk_workspace_bytes(const corope_bwd_params_t* p, const corope_chunk_t* c) {
-  if (!sizes_ok(p) || !c || c->q_row0 < 0 || c->q_row0 % 128 != 0) return 0;
-  return bwd_ws(p, true) + bwd_handoff_ws(p, (int)c->q_row0);
+  if (!sizes_ok(p) || !c || c->q_row0 < 0 || c->q_row0 % 128 != 0 || c->kv_len <= 0) return 0;
+  return bwd_ws(p, true) + bwd_panel_ws(p, c->kv_len) + bwd_handoff_ws(p, (int)c->q_row0);
 }
 
 size_t corope_bwd_chunk_min_workspace_bytes(const corope_bwd_params_t* p,
@@ -335,10 +353,17 @@ static int bwd_common(const corope_bwd_params_t* p, corope_stream_t stream,
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
   if (p->algo != COROPE_ALGO_EXACT && tc_ok) {
     e = bwd_pre_launch(a, p->dtype, st);
-    const size_t base = need;
+    // [minimum][panels, when they fit][hand-off region: the rest]
+    size_t base = need;
+    const size_t panels = bwd_panel_ws(p, Sk);
+    void* panel_ptr = nullptr;
+    if (panels && p->workspace_bytes >= base + panels) {
+      panel_ptr = static_cast<char*>(p->workspace) + base;
+      base += panels;
+    }
     if (e == cudaSuccess)
       e = tc_bwd_launch(a, p->dtype, st, static_cast<char*>(p->workspace) + base,
-                        p->workspace_bytes - base);
+                        p->workspace_bytes - base, panel_ptr);
     if (e == cudaSuccess && !chunk) e = bwd_post_launch(a, p->dtype, st);
   } else {
     e = exact_bwd_launch(a, p->dtype, st);

@@ -93,6 +93,9 @@ enum : int {
 
 struct Params {
   CUtensorMap tm_q, tm_k, tm_v, tm_do;
+  CUtensorMap tm_km[2];  // precomputed K^(m) panels per slab (KMT launches)
+  int km_nhw;            // half windows per (b, kv head) in the panels
+  int km_rows[2];        // panel rows per slab
   void* dq;              // dQ launch output, element type of q
   float *dk32, *dv32;    // dK launch accumulators [B, Hkv, Sk, D]
   const float *lse, *delta, *a;  // [B, H, S]
@@ -201,8 +204,11 @@ __device__ __forceinline__ float2 unpack_cs(uint32_t v) {
   return __half22float2(*reinterpret_cast<const __half2*>(&v));
 }
 
-template <typename T, int D, int MODE, bool HAS_BIAS, int KM>
+// KMT (dQ launch only): the K^(m) operands come from precomputed panels in
+// global memory (tcx::panel_kernel) by TMA instead of warps 12-15.
+template <typename T, int D, int MODE, bool HAS_BIAS, int KM, bool KMT>
 __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant__ Params P) {
+  static_assert(!KMT || MODE == MODE_DQ, "panels feed the dQ launch only");
   using E = ElemTraits<T>;
   using L = SmemTail<MODE, KM>;
   using tq = TQ<KM>;
@@ -240,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     mbar_init(&bars[B_Q], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[B_KVF + i], 1);
-      mbar_init(&bars[B_KVE + i], 2 + 128);  // warps 10 and 11 + the builders
+      mbar_init(&bars[B_KVE + i], KMT ? 2 : 2 + 128);  // warps 10 and 11 (+ the builders)
       mbar_init(&bars[B_SDF + i], 1);
       mbar_init(&bars[B_SDE + i], 256);
       mbar_init(&bars[B_GF + i], 1);
@@ -251,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     mbar_init(&bars[B_CF2], 1);
     mbar_init(&bars[B_CE2], 128);
     for (int i = 0; i < 4; ++i) {
-      mbar_init(&bars[B_BF + i], 128);
+      mbar_init(&bars[B_BF + i], KMT ? 1 : 128);
       mbar_init(&bars[B_BE + i], MODE == MODE_DQ ? 2 : 1);  // G (+ X) done with K^(m)
     }
     mbar_init(&bars[B_AVF], 256);
@@ -490,6 +496,36 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         mma_commit(&bars[B_DRAIN6]);
         mbar_wait(&bars[B_DRAIN6], 0, err, kErrDrain);
       }
+    }
+    __syncwarp();
+    regs_inc<128>();
+  } else if (warp >= 12 && KMT) {
+    regs_dec<kBldRegs>();
+    named_bar(1, kThreads);
+    // ------------------------------------------------------ K^(m) panel loads
+    if (warp == 12 && lane == 0) {
+      prefetch_tmap(&P.tm_km[0]);
+      if (DSL > 1) prefetch_tmap(&P.tm_km[1]);
+      const uint32_t bytes = (P.km_rows[0] + (DSL > 1 ? P.km_rows[1] : 0)) * 128;
+      const int panel0 = (b * P.Hkv + hk) * P.km_nhw;
+      int last[4] = {-1, -1, -1, -1};  // [half][buffer]: last use issued
+      bool ok = true;
+      for (int w = 0; ok && w <= WL; ++w) {
+        const int buf = w % nb, use = w / nb;
+        for (int hh = 0; hh < 2; ++hh) {
+          const int i = 2 * hh + buf;
+          if (use > 0 && !(ok = mbar_wait(&bars[B_BE + i], (use - 1) & 1, err, kErrBEmpty))) break;
+          mbar_expect_tx(&bars[B_BF + i], bytes);
+          uint8_t* dst = smem + P.bop + (hh * nb + buf) * P.b_buf_bytes;
+          for (int s = 0; s < DSL; ++s)
+            tma_load_3d(dst + P.b_slab_off[s], &P.tm_km[s], &bars[B_BF + i], 0, 0,
+                        panel0 + 2 * w + hh);
+          last[i] = use;
+        }
+      }
+      // no copy may still be in flight when the CTA exits
+      for (int i = 0; i < 4; ++i)
+        if (last[i] >= 0) mbar_wait(&bars[B_BF + i], last[i] & 1, err, kErrDrain);
     }
     __syncwarp();
     regs_inc<128>();
@@ -1462,6 +1498,16 @@ struct Terms {
   static constexpr int value = (MODE == MODE_DK && D == 128) ? 14 : kMB;
 };
 
+template <typename T, int D, int MODE, bool HAS_BIAS, int KM, bool KMT>
+static cudaError_t launch_k(const Params& p, int smem, dim3 grid, cudaStream_t st) {
+  auto kern = bwd_kernel<T, D, MODE, HAS_BIAS, KM, KMT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kSmemLimit);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, kThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
 template <typename T, int D, int MODE>
 static cudaError_t launch_mode(Params& p, bool bias, int S, int nbh, cudaStream_t st,
                                float theta, float sm_scale) {
@@ -1470,19 +1516,11 @@ static cudaError_t launch_mode(Params& p, bool bias, int S, int nbh, cudaStream_
   const int smem = plan<MODE, KM>(p);
   if (smem > kSmemLimit) return cudaErrorInvalidValue;
   dim3 grid((S + kBM - 1) / kBM, nbh);
-  cudaError_t e;
-  if (bias) {
-    auto kern = bwd_kernel<T, D, MODE, true, KM>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    if (e != cudaSuccess) return e;
-    kern<<<grid, kThreads, smem, st>>>(p);
-  } else {
-    auto kern = bwd_kernel<T, D, MODE, false, KM>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    if (e != cudaSuccess) return e;
-    kern<<<grid, kThreads, smem, st>>>(p);
-  }
-  return cudaGetLastError();
+  if (MODE == MODE_DQ && p.km_nhw > 0)  // panels were written for this call
+    return bias ? launch_k<T, D, MODE, true, KM, MODE == MODE_DQ>(p, smem, grid, st)
+                : launch_k<T, D, MODE, false, KM, MODE == MODE_DQ>(p, smem, grid, st);
+  return bias ? launch_k<T, D, MODE, true, KM, false>(p, smem, grid, st)
+              : launch_k<T, D, MODE, false, KM, false>(p, smem, grid, st);
 }
 
 template <typename T, int D>
@@ -1513,10 +1551,39 @@ static int64_t blocks_per_bh(int S, int r0 = 0) {
   return n;
 }
 
+template <typename T> constexpr int E_dtype() {
+  return ElemTraits<T>::kBf16 ? COROPE_DTYPE_BF16 : COROPE_DTYPE_F16;
+}
+
+// Write the dQ launch's K^(m) panels (all Sk keys, 16 terms) into `panels`
+// and point the tensor maps at them.
 template <typename T, int D>
-static cudaError_t launch_all(Params& p, bool bias, int BH, int S, uint8_t* handoff,
-                              size_t handoff_bytes, cudaStream_t st, float theta,
-                              float sm_scale) {
+static cudaError_t make_panels(Params& p, const BwdArgs& a, void* panels, cudaStream_t st) {
+  static tcx::PanelArgs pa;  // guarded by the caller's lock
+  tcx::panel_bytes<kMB>(a.B, a.Hkv, a.Sk, D, a.theta, a.sm_scale, &pa);
+  const int64_t np = tcx::panel_count(a.B, a.Hkv, a.Sk);
+  pa.k = a.k;
+  for (int i = 0; i < 3; ++i) pa.ks[i] = a.ks[i];
+  pa.out[0] = panels;
+  pa.out[1] = static_cast<uint8_t*>(panels) + np * pa.rows[0] * 128;
+  for (int s = 0; s < D / 64; ++s)
+    if (!tcx::encode_panels(&p.tm_km[s], pa.out[s], E_dtype<T>(), pa.rows[s], np))
+      return cudaErrorInvalidValue;
+  p.km_nhw = pa.nhw;
+  p.km_rows[0] = pa.rows[0];
+  p.km_rows[1] = pa.rows[1];
+  tcx::panel_kernel<T, D><<<dim3(pa.nhw, a.B * a.Hkv), 128, 0, st>>>(pa);
+  return cudaGetLastError();
+}
+
+template <typename T, int D>
+static cudaError_t launch_all(Params& p, const BwdArgs& a, bool bias, int BH, int S,
+                              uint8_t* handoff, size_t handoff_bytes, void* panels,
+                              cudaStream_t st, float theta, float sm_scale) {
+  if (panels) {
+    cudaError_t e = make_panels<T, D>(p, a, panels, st);
+    if (e != cudaSuccess) return e;
+  }
   const int64_t per_bh = blocks_per_bh(S, p.r0) * kHB;
   int chunk = handoff ? (int)std::min<int64_t>(BH, (int64_t)(handoff_bytes / per_bh)) : 0;
   if (chunk < min_slices(BH, S)) chunk = 0;  // too few CTAs per launch: recompute instead
@@ -1575,8 +1642,12 @@ bool tc_bwd_supported(const BwdArgs& a, int dtype) {
 // region large enough for min_slices (b, h) slices the dK launch reads the
 // dQ launch's per-pair results (slice by slice through the region); otherwise
 // it recomputes them.
+size_t tc_bwd_panel_bytes(const BwdArgs& a) {
+  return tcx::panel_bytes<tcb::kMB>(a.B, a.Hkv, a.Sk, a.D, a.theta, a.sm_scale);
+}
+
 cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* handoff,
-                          size_t handoff_bytes) {
+                          size_t handoff_bytes, void* panels) {
   using namespace tcb;
   static Params p;
   static std::mutex mu;
@@ -1605,15 +1676,14 @@ cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* ha
   uint8_t* hp = static_cast<uint8_t*>(handoff);
   const int BH = a.B * a.H;
   if (dtype == COROPE_DTYPE_BF16)
-    return a.D == 64
-               ? launch_all<__nv_bfloat16, 64>(p, bias, BH, a.S, hp, handoff_bytes, st, a.theta,
-                                                a.sm_scale)
-               : launch_all<__nv_bfloat16, 128>(p, bias, BH, a.S, hp, handoff_bytes, st, a.theta,
-                                                 a.sm_scale);
-  return a.D == 64 ? launch_all<__half, 64>(p, bias, BH, a.S, hp, handoff_bytes, st, a.theta,
-                                            a.sm_scale)
-                   : launch_all<__half, 128>(p, bias, BH, a.S, hp, handoff_bytes, st, a.theta,
-                                             a.sm_scale);
+    return a.D == 64 ? launch_all<__nv_bfloat16, 64>(p, a, bias, BH, a.S, hp, handoff_bytes,
+                                                      panels, st, a.theta, a.sm_scale)
+                     : launch_all<__nv_bfloat16, 128>(p, a, bias, BH, a.S, hp, handoff_bytes,
+                                                       panels, st, a.theta, a.sm_scale);
+  return a.D == 64 ? launch_all<__half, 64>(p, a, bias, BH, a.S, hp, handoff_bytes, panels, st,
+                                            a.theta, a.sm_scale)
+                   : launch_all<__half, 128>(p, a, bias, BH, a.S, hp, handoff_bytes, panels, st,
+                                             a.theta, a.sm_scale);
 }
 
 }  // namespace corope

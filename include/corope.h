@@ -127,6 +127,13 @@ size_t corope_bwd_workspace_bytes(const corope_bwd_params_t *p);
  * per-(row, key) results).  No counterpart in the reference. */
 size_t corope_bwd_min_workspace_bytes(const corope_bwd_params_t *p);
 
+/* Part of corope_bwd_workspace_bytes() holding the dQ kernel's scaled-key
+ * panels (written once per call instead of rebuilt in every CTA).  The
+ * workspace is laid out as [minimum][panels][hand-off region]: the panels are
+ * used when the workspace holds at least minimum + panels, and the hand-off
+ * region takes what is left. */
+size_t corope_bwd_panel_bytes(const corope_bwd_params_t *p);
+
 /* Backward: dq, dk, dv of the CoRoPE attention (gradients through the
  * softmax, the rotation, the contextual positions and the sigmoid gates).
  * Replaces the launch of co_rope_bwd_kernel in

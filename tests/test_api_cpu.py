@@ -83,3 +83,11 @@ def test_auto_workspace_fits_whole_slices():
     assert fit_workspace(full, least, units, budget=0) == least
     # no hand-off region at all (exact path, or head dims without one)
     assert fit_workspace(least, least, units, budget=0) == least
+    # with scaled-key panels: [least][panels][slices]
+    panels = 5000
+    full = least + panels + per * units
+    assert fit_workspace(full, least, units, full, panels) == full
+    assert fit_workspace(full, least, units, least + panels + 2 * per + 7, panels) == \
+        least + panels + 2 * per
+    assert fit_workspace(full, least, units, least + panels + 10, panels) == least + panels
+    assert fit_workspace(full, least, units, least + panels - 1, panels) == least

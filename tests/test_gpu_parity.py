@@ -323,12 +323,14 @@ def test_tensor_backward_s2048_d128():
 
 
 @pytest.mark.parametrize("D", [64, 128])
-@pytest.mark.parametrize("mode", ["full", "chunked", "min"])
+@pytest.mark.parametrize("mode", ["full", "chunked", "panels", "min"])
 def test_tensor_backward_workspace_paths(mode, D):
-    """The three ways the tensor-core backward uses its workspace give the
-    oracle's gradients: a full hand-off region (the dK kernel reads the dQ
-    kernel's per-pair results), a region for 17 of the 24 (b, h) slices
-    (two rounds of both kernels), and the minimum (the dK kernel recomputes)."""
+    """The ways the tensor-core backward uses its workspace give the oracle's
+    gradients: scaled-key panels plus a full hand-off region (the dK kernel
+    reads the dQ kernel's per-pair results), panels plus a region for 17 of
+    the 24 (b, h) slices (two rounds of both kernels), panels alone (the dK
+    kernel recomputes), and the minimum (no panels: the dQ kernel builds its
+    operands, the dK kernel recomputes)."""
     from CoROPE import _lib
     B, H, S = 2, 12, 300
     (q, k, v, do), cpu = inputs(B, H, S, D, 57, torch.bfloat16)
@@ -339,16 +341,19 @@ def test_tensor_backward_workspace_paths(mode, D):
 
     def sizes():
         p = _lib.BwdParams()
+        p.theta, p.sm_scale = 1e4, sm
         p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, H, S, D
         p.dtype, p.algo = _lib._dtype_code(q), _lib.algo_code("tensor")
         lib = _lib.load_library()
         return (lib.corope_bwd_min_workspace_bytes(ctypes.byref(p)),
-                lib.corope_bwd_workspace_bytes(ctypes.byref(p)))
+                lib.corope_bwd_workspace_bytes(ctypes.byref(p)),
+                lib.corope_bwd_panel_bytes(ctypes.byref(p)))
 
-    lo, hi = sizes()
-    per_bh = (hi - lo) // (B * H)
-    assert per_bh > 0 and lo + per_bh * B * H == hi
-    ws = {"full": "full", "min": "min", "chunked": lo + 17 * per_bh}[mode]
+    lo, hi, panels = sizes()
+    per_bh = (hi - lo - panels) // (B * H)
+    assert panels > 0 and per_bh > 0 and lo + panels + per_bh * B * H == hi
+    ws = {"full": "full", "min": "min", "panels": lo + panels,
+          "chunked": lo + panels + 17 * per_bh}[mode]
     _lib.bwd(q_, k_, v_, o_, do, m_, l_, a_, dq, dk, dv, sm, 1e4, algo="tensor", workspace=ws)
     torch.cuda.synchronize()
     assert _lib.take_device_error() == 0
@@ -499,3 +504,29 @@ def test_forward_panels_equal_in_kernel_builders(D, hkv, theta, bias):
     assert _lib.take_device_error() == 0
     for x, y in zip(*outs):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_backward_panels_equal_in_kernel_builders(D):
+    """The dQ kernel fed by the scaled-key panels and the one building its
+    operands in every CTA give bit-identical dq (same operand bits)."""
+    from CoROPE import _lib
+    B, H, S = 2, 4, 640
+    (q, k, v, do), _ = inputs(B, H, S, D, 93, torch.bfloat16)
+    sm = 1 / math.sqrt(D)
+    saved, o = co_rope_forward(q, k, v, sm, theta=5e5, algo="tensor")
+    p = _lib.BwdParams()
+    p.theta, p.sm_scale = 5e5, sm
+    p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, H, S, D
+    p.dtype, p.algo = _lib._dtype_code(q), _lib.algo_code("tensor")
+    lib = _lib.load_library()
+    lo, panels = (lib.corope_bwd_min_workspace_bytes(ctypes.byref(p)),
+                  lib.corope_bwd_panel_bytes(ctypes.byref(p)))
+    res = []
+    for ws in (lo, lo + panels):
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        _lib.bwd(*saved[:4], do, *saved[4:], dq, dk, dv, sm, 5e5, algo="tensor", workspace=ws)
+        res.append(dq)
+    torch.cuda.synchronize()
+    assert _lib.take_device_error() == 0
+    assert torch.equal(res[0], res[1])
