@@ -46,10 +46,11 @@ CPU_SAMPLE_ROWS = 48
 # summed over its kernels) from ncu captures of B=1,H=8,S=2048,D=128, scaled to
 # this workload.  Exact kernel: by query rows x heads (x32),
 # profiles/exact_bwd_b1h8s2048d128.md.  Tensor-core kernels: dominated by the
-# dQ -> dK hand-off, 362.5 MB over 8 x 1088 (b, h, query tile, window) blocks,
-# i.e. 41.6 KB per block, times the 128 x 4224 blocks of this workload;
+# dQ -> dK hand-off and the dQ kernel's panel reads, 411.9 MB over 8 x 1088
+# (b, h, query tile, window) blocks, i.e. 47.3 KB per block, times the
+# 128 x 4224 blocks of this workload;
 # profiles/tc_bwd_b1h8s2048d128.md.
-NCU_TRAFFIC_BYTES = {"exact": 33.78e6 * 32, "tensor": 362.5e6 / (8 * 1088) * (128 * 4224)}
+NCU_TRAFFIC_BYTES = {"exact": 33.78e6 * 32, "tensor": 411.9e6 / (8 * 1088) * (128 * 4224)}
 
 
 def causal_pairs(B, H, S):
@@ -332,10 +333,11 @@ def run_ours(args):
     fwd_used = "exact" if algo == "exact" else "tensor"
     bwd_used = "exact" if algo == "exact" else "tensor"
     used = f"fwd {fwd_used}, bwd {bwd_used}"
-    # our kernels per step: forward 1; backward: delta/lse, then either the
-    # exact main kernel or the dQ and dK tensor-core kernels, then the fp32
-    # dk/dv conversion
-    launches_per_step = 1 + (3 if bwd_used == "exact" else 4)
+    # our kernels per step: forward: the scaled-key panels and the forward
+    # kernel (tensor path) or the exact kernel; backward: delta/lse, then
+    # either the exact main kernel or the panels and the dQ and dK
+    # tensor-core kernels, then the fp32 dk/dv conversion
+    launches_per_step = (2 if fwd_used == "tensor" else 1) + (3 if bwd_used == "exact" else 5)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -230,8 +230,9 @@ def fwd(q, k, v, o, m, l, a, lse, sm_scale, theta, bias=None, algo="auto", theta
         nbytes = (lib.corope_fwd_workspace_bytes(ctypes.byref(p)) if c is None else
                   lib.corope_fwd_chunk_workspace_bytes(ctypes.byref(p), ctypes.byref(c)))
         if nbytes:
-            ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
-            p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
+            ws, nbytes = _alloc_workspace(nbytes, 0, q.device)
+            if nbytes:
+                p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
     if c is not None:
         with torch.cuda.device(q.device):
             rc = lib.corope_fwd_chunk(ctypes.byref(p), ctypes.byref(c), ctypes.c_void_p(stream))
@@ -243,14 +244,38 @@ def fwd(q, k, v, o, m, l, a, lse, sm_scale, theta, bias=None, algo="auto", theta
     _check(rc, "corope_mqa_fwd" if mqa else "corope_fwd")
 
 
+_total_memory = {}
+
+
+def _workspace_budget(device) -> int:
+    """A quarter of the device's memory (queried once per device).  Asking
+    the driver for free memory on every call would cost a driver round trip
+    per backward; a fixed budget also keeps the request the same from call to
+    call, so torch's cache serves it again."""
+    key = str(device)
+    if key not in _total_memory:
+        _total_memory[key] = torch.cuda.get_device_properties(device).total_memory
+    return _total_memory[key] // 4
+
+
+def _alloc_workspace(nbytes, least, device):
+    """torch-allocated workspace; if the allocator cannot give ``nbytes`` the
+    call falls back to ``least`` (the kernels then skip the optional parts)."""
+    try:
+        return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
+    except torch.OutOfMemoryError:
+        if nbytes <= least:
+            raise
+        return torch.empty(least, dtype=torch.uint8, device=device), least
+
+
 def auto_workspace_bytes(lib, p, device, chunk=None):
     """The workspace "auto" gives corope_bwd: the full size when it fits in a
-    quarter of the memory the device and torch's cache have free, else the
-    minimum plus as many whole (b, h) hand-off slices as fit there (long
+    quarter of the device's memory, else the minimum plus the scaled-key
+    panels plus as many whole (b, h) hand-off slices as fit there (long
     sequences: the hand-off region grows with S^2, 5.5 GB per (b, h) at
     S=32768; from 2 slices on a launch already has 512 CTAs), else the
-    minimum.  A quarter leaves the caller's own tensors room and keeps the
-    request the same from call to call, so torch's cache can serve it again."""
+    minimum."""
     if chunk is None:
         full = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
         least = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
@@ -261,9 +286,7 @@ def auto_workspace_bytes(lib, p, device, chunk=None):
         keys = BwdParams.from_buffer_copy(p)
         keys.seq_len = chunk.kv_len
         panels = lib.corope_bwd_panel_bytes(ctypes.byref(keys))
-    free, _ = torch.cuda.mem_get_info(device)
-    budget = (free + torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)) // 4
-    return fit_workspace(full, least, p.batch * p.heads, budget, panels)
+    return fit_workspace(full, least, p.batch * p.heads, _workspace_budget(device), panels)
 
 
 def fit_workspace(full, least, units, budget, panels=0):
@@ -332,7 +355,9 @@ def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="a
                   lib.corope_bwd_chunk_min_workspace_bytes(ctypes.byref(p), ctypes.byref(chunk)))
     else:
         nbytes = int(workspace)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    least = (lib.corope_bwd_min_workspace_bytes(ctypes.byref(p)) if chunk is None else
+             lib.corope_bwd_chunk_min_workspace_bytes(ctypes.byref(p), ctypes.byref(chunk)))
+    ws, nbytes = _alloc_workspace(nbytes, least, q.device)
     p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
     stream = torch.cuda.current_stream(q.device).cuda_stream
     with torch.cuda.device(q.device):
