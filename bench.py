@@ -276,33 +276,47 @@ def run_ours(args):
     # dq, dk, dv back, all inside the timed region.  As a training loader
     # would, the copies run on their own streams: step i+1's inputs go up
     # (into the other of two device slots) and step i's results come down
-    # while the kernels of step i run.
+    # while the kernels of step i run; within a step the forward needs only
+    # q, k, v and o comes down during the backward, so only the first
+    # step's q, k, v and the last step's gradients are not overlapped.
     host = [t.cpu().pin_memory() for t in (q, k, v, do)]
     outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(4)]
     slots = [[torch.empty_like(t) for t in (q, k, v, do)] for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in host)
     d2h = sum(t.numel() * t.element_size() for t in outs)
     s_up, s_down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    up_done = [torch.cuda.Event() for _ in range(2)]
+    qkv_up = [torch.cuda.Event() for _ in range(2)]   # q, k, v of a slot are on the device
+    do_up = [torch.cuda.Event() for _ in range(2)]    # and its dO
     slot_free = [torch.cuda.Event() for _ in range(2)]
+    fwd_done = torch.cuda.Event()
 
     def upload(i):
         with torch.cuda.stream(s_up):
             if i >= 2:
                 s_up.wait_event(slot_free[i % 2])
-            for dst, src in zip(slots[i % 2], host):
+            for dst, src in zip(slots[i % 2][:3], host[:3]):
                 dst.copy_(src, non_blocking=True)
-            up_done[i % 2].record(s_up)
+            qkv_up[i % 2].record(s_up)
+            slots[i % 2][3].copy_(host[3], non_blocking=True)
+            do_up[i % 2].record(s_up)
 
     def compute_and_download(i):
+        # the forward starts once q, k, v are up (dO follows while it runs);
+        # o goes down while the backward runs, the gradients after it
         sl = slots[i % 2]
-        stream.wait_event(up_done[i % 2])
+        stream.wait_event(qkv_up[i % 2])
         saved, o = co_rope_forward(sl[0], sl[1], sl[2], sm, theta=theta, algo=algo)
+        fwd_done.record(stream)
+        with torch.cuda.stream(s_down):
+            s_down.wait_event(fwd_done)
+            outs[0].copy_(o, non_blocking=True)
+            o.record_stream(s_down)
+        stream.wait_event(do_up[i % 2])
         g = co_rope_backward(saved, sl[3], sm, theta, algo=algo)
         slot_free[i % 2].record(stream)
         s_down.wait_stream(stream)
         with torch.cuda.stream(s_down):
-            for dst, src in zip(outs, (o, *g)):
+            for dst, src in zip(outs[1:], g):
                 dst.copy_(src, non_blocking=True)
                 src.record_stream(s_down)
 
@@ -378,7 +392,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--algo", default="auto", choices=["auto", "exact", "tensor"])
