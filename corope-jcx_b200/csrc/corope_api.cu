@@ -227,7 +227,7 @@ size_t corope_fwd_workspace_bytes(const corope_fwd_params_t* p) {
 }
 
 size_t corope_fwd_chunk_workspace_bytes(const corope_fwd_params_t* p, const corope_chunk_t* c) {
-  if (!c || c->kv_len <= 0) return 0;
+  if (!p || !c || c->kv_len <= 0) return 0;
   corope_fwd_params_t q = *p;
   q.seq_len = c->kv_len;
   return corope_fwd_workspace_bytes(&q);

@@ -128,3 +128,18 @@ def test_chunk_argument_checks_without_gpu():
     panels = lib.corope_bwd_panel_bytes(ctypes.byref(keys))
     assert lo == 2 * 4 * 128 * 4 and panels > 0
     assert hi - lo - panels == 4 * ((256 + 127) // 16 + 1) * 20992
+
+
+def test_size_queries_accept_null():
+    """Every size query answers 0 for a NULL params / chunk instead of
+    dereferencing it."""
+    lib = _lib.load_library()
+    assert lib.corope_fwd_workspace_bytes(None) == 0
+    assert lib.corope_fwd_chunk_workspace_bytes(None, None) == 0
+    assert lib.corope_bwd_workspace_bytes(None) == 0
+    assert lib.corope_bwd_min_workspace_bytes(None) == 0
+    assert lib.corope_bwd_panel_bytes(None) == 0
+    assert lib.corope_bwd_chunk_workspace_bytes(None, None) == 0
+    assert lib.corope_bwd_chunk_min_workspace_bytes(None, None) == 0
+    p = _fwd_params()
+    assert lib.corope_fwd_chunk_workspace_bytes(ctypes.byref(p), None) == 0
