@@ -530,3 +530,37 @@ def test_backward_panels_equal_in_kernel_builders(D):
     torch.cuda.synchronize()
     assert _lib.take_device_error() == 0
     assert torch.equal(res[0], res[1])
+
+
+def test_forward_backward_capture_in_cuda_graph():
+    """The public forward and backward make no host synchronisation and
+    allocate only through torch, so a training step can be captured in a CUDA
+    graph and replayed: the replay reproduces the eager outputs (O and dq bit
+    for bit; dk, dv up to the order of the fp32 atomics)."""
+    B, H, S, D = 2, 4, 512, 128
+    (q, k, v, do), _ = inputs(B, H, S, D, 101, torch.bfloat16)
+    sm = 1 / math.sqrt(D)
+
+    def step():
+        saved, o = co_rope_forward(q, k, v, sm, theta=1e4)
+        dq, dk, dv = co_rope_backward(saved, do, sm, 1e4)
+        return o, dq, dk, dv
+
+    eager = step()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()  # warm the allocator and the kernel attributes on the side stream
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        captured = step()
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    from CoROPE import _lib
+    assert _lib.take_device_error() == 0
+    assert torch.equal(captured[0], eager[0]) and torch.equal(captured[1], eager[1])
+    for x, y in zip(captured[2:], eager[2:]):
+        assert rel_l2(x, y) < 1e-3
