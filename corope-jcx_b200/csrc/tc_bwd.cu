@@ -712,6 +712,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     const int r = tid & 127;
     const int t = q0 + r;
     const bool row_ok = t < S;
+    // windows below the tile's first row of a tile inside the rows need no
+    // causal or row mask (CTA-uniform)
+    auto diag_window = [&](int w) { return w * kW + kW - 1 > q0 || q0 + kBM > S; };
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const int64_t ri = ((int64_t)b * P.H + h) * P.S + min(t - P.r0, P.S - 1);
     const float A_t = P.a[ri];
@@ -745,11 +748,13 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       mbar_arrive(&bars[B_SDE + sb]);
       const int j0 = w * kW;
       float z[16], uu[16];
-      float zsum = 0.f;
+      if (diag_window(w)) {
 #pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {
-        z[jj] = (row_ok && j0 + jj <= t) ? sigmoid_f(__uint_as_float(sraw[jj])) : 0.f;
-        zsum += z[jj];
+        for (int jj = 0; jj < 16; ++jj)
+          z[jj] = (row_ok && j0 + jj <= t) ? sigmoid_f(__uint_as_float(sraw[jj])) : 0.f;
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) z[jj] = sigmoid_f(__uint_as_float(sraw[jj]));
       }
       float suf = 0.f;  // in-window suffix after key jj
 #pragma unroll
@@ -757,6 +762,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         uu[jj] = fmaf(suf, 1.0f / kC0, -1.0f);
         suf += z[jj];
       }
+      const float zsum = suf;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int kk = 8 * (i >> 2) + (i & 3);
@@ -927,16 +933,29 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         clenshaw(uj, f, fd);
         float dl[4], da[4], pr[4];
         float sum4 = 0.f;
+        if (diag_window(w)) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int kj = j0 + 8 * hh + 4 * rg + i;
-          const bool valid = row_ok && kj <= t;
-          float lg = f[i];
-          if (HAS_BIAS && valid) lg = fmaf(P.bias[(int64_t)t * P.bias_rs + kj], kLog2e, lg);
-          pr[i] = valid ? exp2f(lg - lse2) : 0.f;
-          dl[i] = pr[i] * (dpj[i] - delta);
-          da[i] = valid ? dl[i] * (kLn2 / kC0) * fd[i] : 0.f;
-          sum4 += da[i];
+          for (int i = 0; i < 4; ++i) {
+            const int kj = j0 + 8 * hh + 4 * rg + i;
+            const bool valid = row_ok && kj <= t;
+            float lg = f[i];
+            if (HAS_BIAS && valid) lg = fmaf(P.bias[(int64_t)t * P.bias_rs + kj], kLog2e, lg);
+            pr[i] = valid ? exp2f(lg - lse2) : 0.f;
+            dl[i] = pr[i] * (dpj[i] - delta);
+            da[i] = valid ? dl[i] * (kLn2 / kC0) * fd[i] : 0.f;
+            sum4 += da[i];
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int kj = j0 + 8 * hh + 4 * rg + i;
+            float lg = f[i];
+            if (HAS_BIAS) lg = fmaf(P.bias[(int64_t)t * P.bias_rs + kj], kLog2e, lg);
+            pr[i] = exp2f(lg - lse2);
+            dl[i] = pr[i] * (dpj[i] - delta);
+            da[i] = dl[i] * (kLn2 / kC0) * fd[i];
+            sum4 += da[i];
+          }
         }
         // publish this group's sum for the partner group
         sts32f(s_xch + ((hh * 2 + rg) * 128 + r) * 4, sum4);
