@@ -1,6 +1,7 @@
 """CPU oracle for CoRoPE attention -- TEST INFRASTRUCTURE ONLY.
 
-This module is the checker for the CUDA kernels of this repository.  Only the
+This module is the reference the CUDA kernels of this repository are tested
+against.  Only the
 tests, ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` may
 import it.  The product path (the ``CoROPE`` package and the C-ABI library)
 never calls into it and fails loudly when the CUDA library is missing.
