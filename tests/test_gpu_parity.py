@@ -323,14 +323,15 @@ def test_tensor_backward_s2048_d128():
 
 
 @pytest.mark.parametrize("D", [64, 128])
-@pytest.mark.parametrize("mode", ["full", "chunked", "panels", "min"])
+@pytest.mark.parametrize("mode", ["full", "chunked", "chunked-no-panels", "panels", "min"])
 def test_tensor_backward_workspace_paths(mode, D):
     """The ways the tensor-core backward uses its workspace give the oracle's
     gradients: scaled-key panels plus a full hand-off region (the dK kernel
     reads the dQ kernel's per-pair results), panels plus a region for 17 of
     the 24 (b, h) slices (two rounds of both kernels), panels alone (the dK
     kernel recomputes), and the minimum (no panels: the dQ kernel builds its
-    operands, the dK kernel recomputes)."""
+    operands, the dK kernel recomputes) -- and 16 slices without the panels
+    (the dQ kernel builds its operands, both kernels run slice by slice)."""
     from CoROPE import _lib
     B, H, S = 2, 12, 300
     (q, k, v, do), cpu = inputs(B, H, S, D, 57, torch.bfloat16)
@@ -353,7 +354,12 @@ def test_tensor_backward_workspace_paths(mode, D):
     per_bh = (hi - lo - panels) // (B * H)
     assert panels > 0 and per_bh > 0 and lo + panels + per_bh * B * H == hi
     ws = {"full": "full", "min": "min", "panels": lo + panels,
-          "chunked": lo + panels + 17 * per_bh}[mode]
+          "chunked": lo + panels + 17 * per_bh,
+          # 16 slices (the fewest a launch takes at this length) fit but the
+          # panels do not (they come first when they fit)
+          "chunked-no-panels": lo + 16 * per_bh}[mode]
+    if mode == "chunked-no-panels":
+        assert 16 * per_bh < panels
     _lib.bwd(q_, k_, v_, o_, do, m_, l_, a_, dq, dk, dv, sm, 1e4, algo="tensor", workspace=ws)
     torch.cuda.synchronize()
     assert _lib.take_device_error() == 0
