@@ -371,6 +371,10 @@ def run_ours(args):
                        "flop_convention": "FA causal: fwd 4*D*P, bwd 10*D*P"},
             "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
             "pct_of_peak": 100 * value / world / sustained,
+            # the reference benchmark's own convention (benchmark.py:172-176):
+            # fwd 4*D*B*H*S^2 and bwd 6*D*B*H*S^2, not halved for causal
+            "value_reference_convention": world * (4 + 6) * D * B * H * S * S
+                                          / (ms_step * 1e-3) / 1e12,
             "roofline": {"bound": "tensor", "kernel": f"corope_bwd ({bwd_used})",
                          "achieved": bwd_tflops, "peak": sustained, "unit": "TFLOP/s",
                          "frac": bwd_tflops / sustained, "peak_source": f"{peak_src} sustained",
