@@ -281,15 +281,15 @@ int corope_bwd_chunk(const corope_bwd_params_t* p, const corope_chunk_t* chunk,
 
 }  // extern "C"
 
-static int bwd_common(const corope_bwd_params_t* p, corope_stream_t stream,
-                      const corope_chunk_t* chunk) {
+// The backward's argument checks, everything before its workspace: sizes,
+// flags, tensors, saved state, bias stride and algo.  Touches no device.
+static int bwd_check_args(const corope_bwd_params_t* p, const corope_chunk_t* chunk) {
   if (!p) return fail(COROPE_ERR_INVALID, "params is NULL");
   int rc = check_common(p->batch, p->heads, p->kv_heads, p->seq_len, p->head_dim, p->causal,
                         p->dtype, p->sm_scale, p->theta);
   if (rc) return rc;
   if (chunk && (rc = check_chunk(chunk, p->seq_len))) return rc;
   const int r0 = chunk ? (int)chunk->q_row0 : 0;
-  const int Sk = chunk ? chunk->kv_len : p->seq_len;
   if ((rc = check_tensor(p->q, p->q_stride, "q", p->dtype))) return rc;
   if ((rc = check_tensor(p->k, p->k_stride, "k", p->dtype))) return rc;
   if ((rc = check_tensor(p->v, p->v_stride, "v", p->dtype))) return rc;
@@ -309,6 +309,23 @@ static int bwd_common(const corope_bwd_params_t* p, corope_stream_t stream,
     return fail(COROPE_ERR_INVALID, "bias_row_stride must be >= seq_len (q_row0 + seq_len)");
   if (p->algo != COROPE_ALGO_EXACT && p->algo != COROPE_ALGO_AUTO && p->algo != COROPE_ALGO_TENSOR)
     return fail(COROPE_ERR_INVALID, "unknown algo %d", p->algo);
+  return COROPE_OK;
+}
+
+namespace corope {
+// For the other translation units: the backward's argument checks (above) and
+// the device check, which corope_bwd runs before and after its workspace
+// checks respectively.
+int bwd_check_args(const corope_bwd_params_t* p) { return ::bwd_check_args(p, nullptr); }
+int device_check() { return check_device(); }
+}  // namespace corope
+
+static int bwd_common(const corope_bwd_params_t* p, corope_stream_t stream,
+                      const corope_chunk_t* chunk) {
+  int rc = bwd_check_args(p, chunk);
+  if (rc) return rc;
+  const int r0 = chunk ? (int)chunk->q_row0 : 0;
+  const int Sk = chunk ? chunk->kv_len : p->seq_len;
   const size_t need = bwd_ws(p, chunk != nullptr);
   if (!p->workspace || p->workspace_bytes < need)
     return fail(COROPE_ERR_WORKSPACE, "workspace of %zu bytes required (got %zu)", need,

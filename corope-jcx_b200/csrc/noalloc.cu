@@ -29,7 +29,10 @@
 #include "common.cuh"
 
 namespace corope {
-int set_last_error(int code, const char* msg);  // corope_api.cu
+// corope_api.cu
+int set_last_error(int code, const char* msg);
+int bwd_check_args(const corope_bwd_params_t* p);
+int device_check();
 }
 
 namespace {
@@ -52,7 +55,10 @@ size_t corope_bwd_min_workspace_bytes(const corope_bwd_params_t* p);
 size_t corope_bwd_noalloc_scratch_bytes(void) { return kScratchBytes; }
 
 int corope_bwd_noalloc(const corope_bwd_params_t* p, corope_stream_t stream) {
-  if (!p) return corope_bwd(p, stream);  // reports the NULL-params error
+  // the same statuses, in the same order, as corope_bwd: arguments, then the
+  // scratch size (in place of the workspace), then the device
+  int rc = corope::bwd_check_args(p);
+  if (rc) return rc;
   const size_t need = corope_bwd_min_workspace_bytes(p);
   if (need > kScratchBytes) {
     char msg[200];
@@ -62,6 +68,7 @@ int corope_bwd_noalloc(const corope_bwd_params_t* p, corope_stream_t stream) {
              need, kScratchBytes);
     return corope::set_last_error(COROPE_ERR_WORKSPACE, msg);
   }
+  if ((rc = corope::device_check())) return rc;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return corope::set_last_error(COROPE_ERR_CUDA, "corope_bwd_noalloc: no usable current device");

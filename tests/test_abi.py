@@ -95,6 +95,45 @@ def test_backward_workspace_checks():
     assert lib.corope_bwd(ctypes.byref(p), None) == _lib.ERR_WORKSPACE
 
 
+def _bwd_params(**kw):
+    p = _lib.BwdParams()
+    fake = 1 << 20
+    for n in ("q", "k", "v", "o", "dout", "m", "l", "a", "dq", "dk", "dv"):
+        setattr(p, n, fake)
+    S, D = 128, kw.get("D", 64)
+    st = _lib._I64x3(2 * S * D, S * D, D)
+    for n in ("q_stride", "k_stride", "v_stride", "o_stride", "do_stride", "dq_stride",
+              "dk_stride", "dv_stride"):
+        setattr(p, n, st)
+    p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = 1, 2, kw.get("Hkv", 2), S, D
+    p.sm_scale, p.theta = 0.125, 1e4
+    p.causal, p.dtype, p.algo = kw.get("causal", 1), kw.get("dtype", 2), kw.get("algo", 0)
+    for n in kw.get("null", ()):
+        setattr(p, n, None)
+    return p
+
+
+@pytest.mark.parametrize("fn", ["corope_bwd", "corope_bwd_noalloc"])
+@pytest.mark.parametrize("kw,code", [
+    (dict(dtype=7), _lib.ERR_INVALID),
+    (dict(causal=0), _lib.ERR_UNSUPPORTED),
+    (dict(algo=9), _lib.ERR_INVALID),
+    (dict(D=256), _lib.ERR_UNSUPPORTED),
+    (dict(Hkv=3), _lib.ERR_INVALID),
+    (dict(null=("q",)), _lib.ERR_INVALID),
+    (dict(null=("dk",)), _lib.ERR_INVALID),
+    (dict(null=("m", "l", "a")), _lib.ERR_INVALID),
+])
+def test_backward_argument_checks(fn, kw, code):
+    """corope_bwd and corope_bwd_noalloc refuse bad arguments with the same
+    status, before any device work (so without a GPU too)."""
+    lib = _lib.load_library()
+    p = _bwd_params(**kw)
+    assert getattr(lib, fn)(ctypes.byref(p), None) == code
+    assert lib.corope_last_error()
+    assert getattr(lib, fn)(None, None) == _lib.ERR_INVALID
+
+
 def test_chunk_argument_checks_without_gpu():
     """corope_fwd_chunk / corope_bwd_chunk refuse a NULL chunk, an offset off
     the 128-row tiles, a key range shorter than the chunk and missing fp32

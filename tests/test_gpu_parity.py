@@ -119,6 +119,41 @@ def test_config2_forward_bf16_sampled(algo):
         check_rows(o, m, a, cpu, b, h, rows, sm, 1e4)
 
 
+def test_bench_workload_forward_backward():
+    """The bench step itself: B=4, H=32, S=4096, D=128 bf16, theta 1e4, on the
+    bench's own inputs (``bench.make_inputs``), forward + backward through the
+    public API with the default ("auto") workspace, as ``bench.py`` runs it.
+    Against the per-row oracle: dq of sampled rows and dk, dv of the last 32
+    keys (every row that reaches them is sampled) on three (b, h) slices, and
+    the forward of every row of a fourth slice."""
+    import bench
+    from CoROPE import _lib
+    B, H, S, D, theta = 4, 32, 4096, 128, 1e4
+    assert (bench.WORKLOAD["B"], bench.WORKLOAD["H"], bench.WORKLOAD["S"], bench.WORKLOAD["D"],
+            bench.WORKLOAD["theta"]) == (B, H, S, D, theta)
+    q, k, v, do = bench.make_inputs(0, torch.device(DEV))
+    sm = 1 / math.sqrt(D)
+    saved, o = co_rope_forward(q, k, v, sm, theta=theta)
+    dq, dk, dv = co_rope_backward(saved, do, sm, theta)
+    torch.cuda.synchronize()
+    assert _lib.take_device_error() == 0
+    m, a = saved[4], saved[6]
+    cpu = [t.double().cpu() for t in (q, k, v, do)]
+    n = 32
+    rows = torch.cat([torch.tensor([0, 1]),
+                      torch.randint(2, S - n, (6,), generator=torch.Generator().manual_seed(5)),
+                      torch.arange(S - n, S)])
+    for b, h in ((0, 0), (3, 31), (1, 17)):
+        rq, rk, rv = O.backward_rows(cpu[0][b, h], cpu[1][b, h], cpu[2][b, h], cpu[3][b, h],
+                                     rows, sm, theta)
+        for name, mine, r in (("dq", dq[b, h, rows], rq), ("dk", dk[b, h, S - n:], rk[S - n:]),
+                              ("dv", dv[b, h, S - n:], rv[S - n:])):
+            assert torch.isfinite(mine).all(), name
+            assert maxabs(mine, r) < G_MAXABS, (name, b, h)
+            assert rel_l2(mine, r) < REL_L2, (name, b, h)
+    check_rows(o, m, a, cpu, 2, 7, torch.arange(S), sm, theta)
+
+
 @pytest.mark.parametrize("algo", FWD_ALGOS)
 def test_config4_mqa_forward_bf16_sampled(algo):
     """MQA: B=4, Hq=32, Hkv=1, S=8192, D=128 bf16, seed 3, theta 5e5."""
