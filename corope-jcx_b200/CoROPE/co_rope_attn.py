@@ -30,15 +30,11 @@ class CoRoPEAttentionFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_output):
-        q_out, k_out, v_out, o_out, m_out, l_out, a_k_out = ctx.saved_tensors
-        batch_size, num_heads, seq_len, head_dim = q_out.shape
-        thetas = 1.0 / (ctx.theta ** (torch.arange(0, head_dim, 2, device=q_out.device).float()
-                                      / head_dim))
-        thetas = thetas.repeat_interleave(2)
-        thetas = thetas.unsqueeze(0).repeat(num_heads, 1).contiguous()
-        dq, dk, dv, _ = co_rope_backward(q_out, k_out, v_out, o_out, m_out, l_out, a_k_out,
-                                         grad_output, thetas, ctx.causal, ctx.sm_scale,
-                                         theta=ctx.theta)
+        # the (saved, do, sm_scale, theta) convention: the library builds its
+        # own frequency table from theta (the reference's [H, D] table at
+        # co_rope_attn.py:38-42 only feeds its 11-argument backward)
+        dq, dk, dv = co_rope_backward(tuple(ctx.saved_tensors), grad_output, ctx.sm_scale,
+                                      ctx.theta, causal=ctx.causal)
         return dq, dk, dv, None, None, None
 
 

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this folder from the REFERENCE implementation.
 
-Run in a container that has the reference checkout (read-only) at
-``/root/reference`` (or pass its path as argv[1]):
+Run where a checkout of the reference is available (read-only is enough),
+passing its path:
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py [/path/to/reference]
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py /path/to/reference
 
 What it records (all on CPU, fp32):
 
@@ -40,7 +40,9 @@ os.environ.setdefault("TRITON_INTERPRET", "1")
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) != 2:
+    sys.exit("usage: TRITON_INTERPRET=1 python tests/golden/make_golden.py /path/to/reference")
+REF = sys.argv[1]
 sys.path.insert(0, REF)
 HERE = os.path.dirname(os.path.abspath(__file__))
 
