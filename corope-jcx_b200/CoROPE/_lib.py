@@ -244,18 +244,9 @@ def fwd(q, k, v, o, m, l, a, lse, sm_scale, theta, bias=None, algo="auto", theta
     _check(rc, "corope_mqa_fwd" if mqa else "corope_fwd")
 
 
-_total_memory = {}
-
-
-def _workspace_budget(device) -> int:
-    """A quarter of the device's memory (queried once per device).  Asking
-    the driver for free memory on every call would cost a driver round trip
-    per backward; a fixed budget also keeps the request the same from call to
-    call, so torch's cache serves it again."""
-    key = str(device)
-    if key not in _total_memory:
-        _total_memory[key] = torch.cuda.get_device_properties(device).total_memory
-    return _total_memory[key] // 4
+# Workspace the "auto" backward takes at most, unless one slice group of the
+# hand-off needs more (see auto_workspace_bytes).
+AUTO_WORKSPACE_BUDGET = 4 << 30
 
 
 def _alloc_workspace(nbytes, least, device):
@@ -269,13 +260,22 @@ def _alloc_workspace(nbytes, least, device):
         return torch.empty(least, dtype=torch.uint8, device=device), least
 
 
+def min_slices(units, seq_len):
+    """Fewest (b, h) slices the library runs per hand-off launch pair: 16, or
+    fewer when they already make 512 CTAs of 128 query rows, or all units."""
+    qtiles = (seq_len + 127) // 128
+    return min(units, 16, (512 + qtiles - 1) // qtiles)
+
+
 def auto_workspace_bytes(lib, p, device, chunk=None):
-    """The workspace "auto" gives corope_bwd: the full size when it fits in a
-    quarter of the device's memory, else the minimum plus the scaled-key
-    panels plus as many whole (b, h) hand-off slices as fit there (long
-    sequences: the hand-off region grows with S^2, 5.5 GB per (b, h) at
-    S=32768; from 2 slices on a launch already has 512 CTAs), else the
-    minimum."""
+    """The workspace "auto" gives corope_bwd: the full size when it fits in
+    AUTO_WORKSPACE_BUDGET (4 GiB), else the minimum plus the scaled-key
+    panels plus as many whole (b, h) hand-off slices as fit there -- but never
+    fewer than one slice group of the library's hand-off launches (long
+    sequences: 2 slices of 1.1 GB at S=32768), since below that the dK kernel
+    recomputes the per-pair work instead.  The budget is fixed, not a share of
+    free memory: asking the driver for free memory would cost a round trip on
+    every backward, and a fixed request lets torch's cache serve it again."""
     if chunk is None:
         full = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
         least = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
@@ -286,7 +286,12 @@ def auto_workspace_bytes(lib, p, device, chunk=None):
         keys = BwdParams.from_buffer_copy(p)
         keys.seq_len = chunk.kv_len
         panels = lib.corope_bwd_panel_bytes(ctypes.byref(keys))
-    return fit_workspace(full, least, p.batch * p.heads, _workspace_budget(device), panels)
+    units = p.batch * p.heads
+    budget = AUTO_WORKSPACE_BUDGET
+    if full > budget and full > least + panels:
+        per = (full - least - panels) // units
+        budget = max(budget, least + panels + min_slices(units, p.seq_len) * per)
+    return fit_workspace(full, least, units, budget, panels)
 
 
 def fit_workspace(full, least, units, budget, panels=0):
@@ -309,8 +314,8 @@ def fit_workspace(full, least, units, budget, panels=0):
 def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="auto",
         thetas=None, workspace="auto", q_row0=None, dk_accum=None, dv_accum=None):
     """Launch corope_bwd on the current stream of q with a torch-allocated
-    workspace: "auto" (the full size when it fits in free memory, else as many
-    hand-off slices as fit), "full" (corope_bwd_workspace_bytes, the fastest),
+    workspace: "auto" (auto_workspace_bytes: the full size up to 4 GiB, else
+    as many hand-off slices as fit), "full" (corope_bwd_workspace_bytes, the fastest),
     "min" (corope_bwd_min_workspace_bytes) or a byte count in between.
 
     With ``q_row0`` (corope_bwd_chunk) q, o, do, m, l, a, dq are the query rows

@@ -17,14 +17,18 @@
 //
 // Two launches share that per-pair work and differ in what they accumulate:
 //
-//   dQ launch:  X = Y . K^(m) (K = 14 terms x 16 keys) and dq_t +=
+//   dQ launch:  X = Y . K^(m) (K = 16 terms x 16 keys) and dq_t +=
 //               ln2 R(-(C_t + c0) theta) X_t  (per-row rotation after the GEMM),
-//               plus the gate part dq += dS K (UMMA straight into TMEM).
-//   dK launch:  C^T = v^T . Y (M = head dim, N = 14 terms x 8 keys, K = the 128
-//               query rows), then per head dim a combine over the 14 terms
-//               with the coefficients and the (i)^m pair rotation; plus
-//               dV^T = dO^T P and dK_gate^T = Q^T dS; fp32 atomics into the
-//               dk/dv accumulators of the workspace (query tiles race on keys).
+//               plus the gate part dq += dS K (UMMA straight into TMEM); and
+//               once per window dV^T = dO^T P and dK_gate^T = Q^T dS, added
+//               to the dv / dk accumulators of the workspace (fp32 atomics:
+//               query tiles race on keys).
+//   dK launch:  C^T = v^T . Y (M = head dim, N = 16 terms x 8 keys, K = the 128
+//               query rows), then per head dim a combine over the 16 terms
+//               with the coefficients and the (i)^m pair rotation, added to
+//               the dk accumulator.  With a hand-off region it reads dl from
+//               the dQ launch and recomputes only the gates (dk3_kernel);
+//               without one it recomputes the whole per-pair chain.
 //
 // Roles per CTA (128 query rows of one (b, h), 512 threads): warps 0-7 are
 // two row warpgroups that share every row -- warpgroup g takes keys 4g..4g+3
@@ -32,10 +36,11 @@
 // and the dQ update, and the two meet once per half through shared memory
 // for the running gate-gradient prefix; warp 8 TMA; warp 9 UMMA for the G
 // GEMMs; warp 10 UMMA for the launch's own GEMMs; warp 11 UMMA for the gate
-// and dP GEMMs; warps 12-15 build K^(m) (and, in the dK launch, run the
-// per-dimension combine).  Each UMMA issue costs the issuing thread about
-// as long as the tensor core takes to read the operands from shared memory,
-// so the GEMM families sit on separate threads.
+// and dP GEMMs; warps 12-15 build K^(m) (unless it comes from the panels) and
+// add the launch's accumulators to the workspace (dQ launch: dV^T and
+// dK_gate^T; dK launch: the per-dimension combine of C^T).  Each UMMA issue
+// costs the issuing thread about as long as the tensor core takes to read the
+// operands from shared memory, so the GEMM families sit on separate threads.
 // Registers are re-balanced with setmaxnreg: rows 176, builders 104, the
 // TMA/UMMA warpgroup 56 (2 x 176 + 104 + 56 = 4 x 128, the launch budget).
 // Every wait is bounded as in the forward.
@@ -73,14 +78,13 @@ using tcx::sigmoid_f;
 // Head dims 64 and 128.  Shared-memory tiles are always laid out for 128
 // (two 64-element slabs); with 64 the second slab of Q, dO and the A rows is
 // zero, which keeps the transposed GEMMs (M = head dim) at M = 128.
-// Chebyshev terms: 16 in the backward (the position derivative of a 14-term
-// expansion errs by up to 2.4% at the highest frequency, 0.2% with 16); the
-// recompute dK kernel at head dim 128 keeps 14 to fit its shared memory.
-constexpr int kMB = 16;      // most terms any backward kernel uses
+// Chebyshev terms: 16 in every backward kernel (the position derivative of a
+// 14-term expansion errs by up to 2.4% at the highest frequency, 0.2% with 16).
+constexpr int kMB = 16;      // Chebyshev terms of the backward
 constexpr int NS = 2;        // 64-element slabs in the shared-memory layout
 constexpr int NPX = 64;      // rotation pairs of the widest head dim (table width)
 constexpr int kBM = 128;     // query rows per CTA
-constexpr int kKT = 32;      // keys per K/V tile (2 windows)
+constexpr int kKT = 16;      // keys per K/V tile (one window)
 constexpr int kThreads = 512;
 constexpr int kRowRegs = 176, kBldRegs = 104, kCtlRegs = 56;
 static_assert(2 * kRowRegs + kBldRegs + kCtlRegs == 4 * 128, "register split");
@@ -121,14 +125,14 @@ struct Params {
 // shared memory (bytes from the 1024-aligned base)
 constexpr int S_Q = 0;                       // [NS][128 rows][128 B]
 constexpr int S_DO = S_Q + NS * 16384;
-constexpr int S_K = S_DO + NS * 16384;       // [2 stages][NS][32 rows][128 B]
-constexpr int S_V = S_K + 2 * NS * 4096;
-constexpr int S_AV = S_V + 2 * NS * 4096;    // A operand rows [NS][128][128 B]
-constexpr int S_Y = S_AV + NS * 16384;       // dK: Y | P rows [NS][128][128 B];
+constexpr int S_K = S_DO + NS * 16384;       // [2 stages][NS][16 rows][128 B]
+constexpr int S_V = S_K + 2 * NS * 2048;
+constexpr int S_AV = S_V + 2 * NS * 2048;    // A operand rows [NS][128][128 B]
+constexpr int S_Y = S_AV + NS * 16384;       // dK: Y rows [NS][128][128 B];
                                              // dQ: staged (cos, sin) [8 chunks][256 threads][16 B]
-constexpr int S_DS = S_Y + NS * 16384;       // dK: P | dS rows [128][128 B] (bytes 64..127)
+constexpr int S_DS = S_Y + NS * 16384;       // dQ: P | dS rows [128][128 B] (bytes 64..127)
 template <int MODE, int KM> struct SmemTail {
-  static constexpr int COEF = S_DS + (MODE == MODE_DK ? 16384 : 0);
+  static constexpr int COEF = S_DS + (MODE == MODE_DQ ? 16384 : 0);
   static constexpr int TH = COEF + KM * NPX * 4;
   static constexpr int BAR = TH + NPX * 4;
   static constexpr int NBAR = 40;
@@ -141,26 +145,80 @@ template <int MODE, int KM> struct SmemTail {
 template <int KM> struct TQ {  // dQ launch
   static constexpr uint32_t GW = 8 * KM;
   static constexpr int NSD = KM > 14 ? 1 : 2;  // gate / dP buffers
+  // YT: Y (4 KM cols); DVK: dV^T (16 keys) | dK_gate^T (16 keys)
   static constexpr uint32_t X = 0, DQ = 128, G = 256, SG0 = G + GW, DP0 = SG0 + 16 * NSD,
-                            YT = DP0 + 16 * NSD;  // Y (4 KM cols) | dS (8 cols)
-  static_assert(YT + 4 * KM + 8 <= 512, "tmem");
-};
-template <int KM> struct TK {  // recompute dK launch
-  // C0 / C1: C^T of the window's halves; DVK: dV^T (16 keys) | dK_gate^T (16 keys)
-  static constexpr uint32_t GW = 8 * KM;
-  static constexpr uint32_t G = 0, SG0 = GW, DP0 = GW + 16, AVT = GW + 32, C0 = AVT + 64,
-                            C1 = C0 + GW, DVK = C1 + GW;
+                            YT = DP0 + 16 * NSD, DVK = YT + 4 * KM;
   static_assert(DVK + 32 <= 512, "tmem");
 };
+template <int KM> struct TK {  // recompute dK launch
+  // C0 / C1: C^T of the window's halves
+  static constexpr uint32_t GW = 8 * KM;
+  static constexpr uint32_t G = 0, SG0 = GW, DP0 = GW + 16, AVT = GW + 32, C0 = AVT + 64,
+                            C1 = C0 + GW;
+  static_assert(C1 + GW <= 512, "tmem");
+};
 
-// Hand-off block (one per (b, h, query tile, window), 128 rows): what the dK
-// launch needs to rebuild Y without the gates, the G GEMM or the Clenshaw
-// sums.  Quad q = 2 * half + row group holds keys 8 half + 4 group + 0..3.
-constexpr int HB_DL = 0;                       // dl, fp32        [4 quads][128 rows][4]
-constexpr int HB_PD = HB_DL + 4 * 128 * 16;    // P | dS, 16-bit  [4 quads][128 rows][4 + 4]
-constexpr int HB_U = HB_PD + 4 * 128 * 16;     // u, 16-bit fixed [4 quads][128 rows][4]
-constexpr int HB_C = HB_U + 4 * 128 * 8;       // carry, fp32     [128 rows]
-constexpr int kHB = HB_C + 128 * 4;
+// Hand-off block (one per (b, h, query tile, window), 128 rows x 16 keys):
+// dl = P (dP - delta) of each (row, key) as f16, which the dK launch needs,
+// with the in-window positions u (recomputed there from the gates), to
+// rebuild Y_m = dl T_m(u).  Quad q = 2 * half + row group holds keys
+// 8 half + 4 group + 0..3, 8 bytes per row.
+constexpr int kHB = 4 * 128 * 8;
+// dl -> f16 pair, saturated at the largest finite f16
+__device__ __forceinline__ uint32_t pack_dl(float a, float b) {
+  constexpr float kMax = 65504.f;
+  return sm100::pack_f16(fminf(fmaxf(a, -kMax), kMax), fminf(fmaxf(b, -kMax), kMax));
+}
+__device__ __forceinline__ float2 unpack_dl(uint32_t v) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&v));
+}
+
+// Gates of one window for one row, shared by the dQ and dK launches so that
+// both derive the same positions from the same gate scores: z_j =
+// sigmoid(s_j) (0 where `keep` says so), u_j = (sum_{i>j} z_i) / c0 - 1 (the
+// scaled in-window position of key j); returns sum_j z_j.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float gate_sigmoid(float s) {
+  return rcp_approx(__fadd_rn(1.0f, ex2_approx(__fmul_rn(s, -kLog2e))));
+}
+template <bool MASKED>
+__device__ __forceinline__ float window_gates(const uint32_t (&sraw)[16], int j0, int t,
+                                              bool row_ok, float (&z)[16], float (&uu)[16]) {
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) {
+    const float g = gate_sigmoid(__uint_as_float(sraw[jj]));
+    z[jj] = MASKED ? ((row_ok && j0 + jj <= t) ? g : 0.f) : g;
+  }
+  float suf = 0.f;  // in-window suffix after key jj
+#pragma unroll
+  for (int jj = 15; jj >= 0; --jj) {
+    uu[jj] = __fmaf_rn(suf, 1.0f / kC0, -1.0f);
+    suf = __fadd_rn(suf, z[jj]);
+  }
+  return suf;
+}
+// Compensated (Kahan) running gate prefix: the prefix reaches ~S/2, where
+// fp32 steps are 2^-10 at S = 32768, and a plain running sum over S/16
+// windows drifts by ~1e-2 -- an angle error of that size in the fastest
+// rotation.  base - base_c is the prefix to ~1 ulp.  Returns the gate sum of
+// the keys after the window, A_t - prefix.
+__device__ __forceinline__ float advance_prefix(float zsum, float A_t, float& base,
+                                                float& base_c) {
+  const float y = __fsub_rn(zsum, base_c);
+  const float s2 = __fadd_rn(base, y);
+  base_c = __fsub_rn(__fsub_rn(s2, base), y);
+  base = s2;
+  return __fadd_rn(__fsub_rn(A_t, base), base_c);
+}
 // first block of query tile qt within its (b, h): tiles before it are full
 // (8 (q + 1) windows each)
 __host__ __device__ constexpr int64_t tile_block0(int qt) { return 4ll * qt * (qt + 1); }
@@ -168,14 +226,6 @@ __host__ __device__ constexpr int64_t tile_block0(int qt) { return 4ll * qt * (q
 __host__ __device__ constexpr int64_t chunk_block0(int r0, int qt) {
   return tile_block0(r0 / 128 + qt) - tile_block0(r0 / 128);
 }
-// u in [-1, 1] -> 16-bit fixed point, rounded, saturating at both ends
-__device__ __forceinline__ uint32_t u_encode(float u) {
-  unsigned short q;
-  asm("cvt.rni.sat.u16.f32 %0, %1;" : "=h"(q) : "f"(fmaf(u, 32767.5f, 32767.5f)));
-  return q;
-}
-__device__ __forceinline__ float u_decode(uint32_t q) { return fmaf((float)q, 1.0f / 32767.5f, -1.0f); }
-
 enum {
   B_Q = 0, B_KVF = 1, B_KVE = 3, B_SDF = 5, B_SDE = 7, B_AVF = 9,
   B_BF = 11,  // [half][buf]
@@ -187,7 +237,7 @@ enum {
   B_CF = 28, B_CE = 30, B_YFREE = 32,            // dK launch: [half] x 2
   B_DRAIN11 = 33, B_DRAIN5 = 34, B_DRAIN6 = 35,
   B_XCH = 36,                                    // [half]
-  B_CF2 = 38, B_CE2 = 39                         // dK launch: dV / dK_gate GEMMs
+  B_CF2 = 38, B_CE2 = 39                         // dQ launch: dV / dK_gate GEMMs
 };
 
 __device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&r)[4]) {
@@ -329,22 +379,45 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           tma_load_4d(smem + S_Q + s * 16384, &P.tm_q, &bars[B_Q], 64 * s, q0 - P.r0, h, b);
           tma_load_4d(smem + S_DO + s * 16384, &P.tm_do, &bars[B_Q], 64 * s, q0 - P.r0, h, b);
         }
-        const int TL = WL / 2;  // last K/V tile
         int last_use[2] = {-1, -1};
-        for (int n = 0; n <= TL; ++n) {
+        for (int n = 0; n <= WL; ++n) {  // tile n = the keys of window n
           const int st = n & 1, u = n >> 1;
           if (n >= 2 && !mbar_wait(&bars[B_KVE + st], (u - 1) & 1, err, kErrKvEmpty)) break;
-          mbar_expect_tx(&bars[B_KVF + st], 2 * DSL * 4096);
+          mbar_expect_tx(&bars[B_KVF + st], 2 * DSL * 2048);
           for (int s = 0; s < DSL; ++s) {
-            tma_load_4d(smem + S_K + (st * NS + s) * 4096, &P.tm_k, &bars[B_KVF + st], 64 * s,
+            tma_load_4d(smem + S_K + (st * NS + s) * 2048, &P.tm_k, &bars[B_KVF + st], 64 * s,
                         kKT * n, hk, b);
-            tma_load_4d(smem + S_V + (st * NS + s) * 4096, &P.tm_v, &bars[B_KVF + st], 64 * s,
+            tma_load_4d(smem + S_V + (st * NS + s) * 2048, &P.tm_v, &bars[B_KVF + st], 64 * s,
                         kKT * n, hk, b);
           }
           last_use[st] = u;
         }
         for (int st = 0; st < 2; ++st)
           if (last_use[st] >= 0) mbar_wait(&bars[B_KVF + st], last_use[st] & 1, err, kErrDrain);
+      } else if (KMT && lane == 1) {
+        // ------------------------------------------- K^(m) panel loads
+        prefetch_tmap(&P.tm_km[0]);
+        if (DSL > 1) prefetch_tmap(&P.tm_km[1]);
+        const uint32_t bytes = (P.km_rows[0] + (DSL > 1 ? P.km_rows[1] : 0)) * 128;
+        const int panel0 = (b * P.Hkv + hk) * P.km_nhw;
+        int last[4] = {-1, -1, -1, -1};  // [half][buffer]: last use issued
+        bool ok = true;
+        for (int w = 0; ok && w <= WL; ++w) {
+          const int buf = w % nb, use = w / nb;
+          for (int hh = 0; hh < 2; ++hh) {
+            const int i = 2 * hh + buf;
+            if (use > 0 && !(ok = mbar_wait(&bars[B_BE + i], (use - 1) & 1, err, kErrBEmpty))) break;
+            mbar_expect_tx(&bars[B_BF + i], bytes);
+            uint8_t* dst = smem + P.bop + (hh * nb + buf) * P.b_buf_bytes;
+            for (int s = 0; s < DSL; ++s)
+              tma_load_3d(dst + P.b_slab_off[s], &P.tm_km[s], &bars[B_BF + i], 0, 0,
+                          panel0 + 2 * w + hh);
+            last[i] = use;
+          }
+        }
+        // no copy may still be in flight when the CTA exits
+        for (int i = 0; i < 4; ++i)
+          if (last[i] >= 0) mbar_wait(&bars[B_BF + i], last[i] & 1, err, kErrDrain);
       }
     } else if (warp == 9) {
       // ---------------------------------------------- UMMA: G GEMMs
@@ -391,25 +464,25 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         const uint32_t id_n16 = idesc_f16(128, 16, E::kBf16, false);
         bool ok = mbar_wait(&bars[B_Q], 0, err, kErrQ);
         for (int w = 0; ok && w <= WL; ++w) {
-          const int n = w >> 1, st = n & 1, sb = w % NSD;
-          if (!(ok = mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull))) break;
+          const int st = w & 1, sb = w % NSD;
+          if (!(ok = mbar_wait(&bars[B_KVF + st], (w >> 1) & 1, err, kErrKvFull))) break;
           if (w >= NSD &&
               !(ok = mbar_wait(&bars[B_SDE + sb], ((w / NSD) - 1) & 1, err, kErrSdEmpty)))
             break;
           tc_fence_after();
-          const uint32_t kt = sK + st * NS * 4096 + (w & 1) * kW * 128;
-          const uint32_t vt = sV + st * NS * 4096 + (w & 1) * kW * 128;
+          const uint32_t kt = sK + st * NS * 2048;
+          const uint32_t vt = sV + st * NS * 2048;
           const uint32_t dsg = tmem + T_SG0 + 16 * sb;
           const uint32_t ddp = tmem + T_DP0 + 16 * sb;
 #pragma unroll
           for (int s = 0; s < KSTEPS; ++s) {
             const uint32_t off = (s >> 2) * 16384 + 32 * (s & 3);
-            const uint32_t koff = (s >> 2) * 4096 + 32 * (s & 3);
+            const uint32_t koff = (s >> 2) * 2048 + 32 * (s & 3);
             mma_ss(dsg, sdesc_kmajor(sQ + off), sdesc_kmajor(kt + koff), id_n16, s > 0);
             mma_ss(ddp, sdesc_kmajor(sDO + off), sdesc_kmajor(vt + koff), id_n16, s > 0);
           }
           mma_commit(&bars[B_SDF + sb]);
-          if (w & 1) mma_commit(&bars[B_KVE + st]);  // last window of the tile
+          mma_commit(&bars[B_KVE + st]);
         }
         mma_commit(&bars[B_DRAIN11]);
         mbar_wait(&bars[B_DRAIN11], 0, err, kErrDrain);
@@ -422,9 +495,10 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         if (MODE == MODE_DQ) {
           const uint32_t id_x = idesc_f16(128, 64, E::kBf16, true);   // B = K^(m), MN-major
           const uint32_t id_g = idesc_f16(128, D, E::kBf16, true);    // B = K tile, MN-major
+          const uint32_t id_s = idesc_f16(128, 16, E::kBf16, true) | (1u << 15);  // A, B MN-major
           for (int w = 0; ok && w <= WL; ++w) {
             const int buf = w % nb;
-            const int n = w >> 1, st = n & 1;
+            const int st = w & 1;
             for (int hh = 0; hh < 2 && ok; ++hh) {
               ok = mbar_wait(&bars[hh ? B_YB : B_YA], w & 1, err, kErrY);
               // X is free once the rows have folded the previous window into dq
@@ -448,17 +522,31 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
               if (hh == 0) mma_commit(&bars[B_YDONE]);  // Y half A consumed
             }
             if (!ok) break;
-            // gate part: dq += dS K_w  (A = dS from tensor memory, B = K tile)
-            if (!(ok = mbar_wait(&bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull))) break;
-            mma_ts(tmem + tq::DQ, tmem + tq::YT + 4 * kM,
-                   sdesc_mnmajor(sK + st * NS * 4096 + (w & 1) * kW * 128, 4096), id_g, w > 0);
+            // gate part: dq += dS K_w  (A = the dS rows, bytes 96..127 of the
+            // P | dS rows in shared memory; B = the window's K tile)
+            if (!(ok = mbar_wait(&bars[B_KVF + st], (w >> 1) & 1, err, kErrKvFull))) break;
+            mma_ss(tmem + tq::DQ, sdesc_kmajor(sDS + 96), sdesc_mnmajor(sK + st * NS * 2048, 2048),
+                   id_g, w > 0);
             mma_commit(&bars[B_XF]);
-            mma_commit(&bars[B_YTFREE]);
-            if (w & 1) mma_commit(&bars[B_KVE + st]);
+            // dV^T = dO^T P and dK_gate^T = Q^T dS over the window's 16 keys
+            // (B = bytes 64..95 / 96..127 of the P | dS rows, K = the 128
+            // query rows), once warps 12-15 have read the previous window's
+            if (w > 0 && !(ok = mbar_wait(&bars[B_CE2], (w - 1) & 1, err, kErrCEmpty))) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int s = 0; s < 8; ++s) {
+              const uint32_t ko = 2048 * s;
+              mma_ss(tmem + tq::DVK, sdesc_mnmajor(sDO + ko, 16384),
+                     sdesc_mnmajor(sDS + ko + 64, 16384), id_s, s > 0);
+              mma_ss(tmem + tq::DVK + 16, sdesc_mnmajor(sQ + ko, 16384),
+                     sdesc_mnmajor(sDS + ko + 96, 16384), id_s, s > 0);
+            }
+            mma_commit(&bars[B_CF2]);
+            mma_commit(&bars[B_YTFREE]);  // Y, P and dS rows all read
+            mma_commit(&bars[B_KVE + st]);
           }
         } else {
           const uint32_t id_c = idesc_f16(128, 8 * kM, E::kBf16, true) | (1u << 15);  // A, B MN-major
-          const uint32_t id_s = idesc_f16(128, 16, E::kBf16, true) | (1u << 15);
           for (int w = 0; ok && w <= WL; ++w) {
             for (int hh = 0; hh < 2 && ok; ++hh) {
               ok = mbar_wait(&bars[hh ? B_YB : B_YA], w & 1, err, kErrY);
@@ -476,21 +564,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
               if (hh == 0) mma_commit(&bars[B_YDONE]);
             }
             if (!ok) break;
-            // once per window: dV^T = dO^T P and dK_gate^T = Q^T dS over the
-            // 16 keys (B = bytes 96..127 of the P rows and of the dS rows)
-            if (w > 0 && !(ok = mbar_wait(&bars[B_CE2], (w - 1) & 1, err, kErrCEmpty))) break;
-            tc_fence_after();
-#pragma unroll 1
-            for (int s = 0; s < 8; ++s) {
-              const uint32_t ko = 2048 * s;
-              mma_ss(tmem + tk::DVK, sdesc_mnmajor(sDO + ko, 16384),
-                     sdesc_mnmajor(sDS + ko + 64, 16384), id_s, s > 0);
-              mma_ss(tmem + tk::DVK + 16, sdesc_mnmajor(sQ + ko, 16384),
-                     sdesc_mnmajor(sDS + ko + 96, 16384), id_s, s > 0);
-            }
-            mma_commit(&bars[B_CF2]);
-            mma_commit(&bars[B_YFREE]);  // A rows, Y | P rows and dS rows all read
-            if (w & 1) mma_commit(&bars[B_KVE + ((w >> 1) & 1)]);
+            mma_commit(&bars[B_YFREE]);  // A rows and Y rows all read
+            mma_commit(&bars[B_KVE + (w & 1)]);
           }
         }
         mma_commit(&bars[B_DRAIN6]);
@@ -499,45 +574,17 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     }
     __syncwarp();
     regs_inc<128>();
-  } else if (warp >= 12 && KMT) {
-    regs_dec<kBldRegs>();
-    named_bar(1, kThreads);
-    // ------------------------------------------------------ K^(m) panel loads
-    if (warp == 12 && lane == 0) {
-      prefetch_tmap(&P.tm_km[0]);
-      if (DSL > 1) prefetch_tmap(&P.tm_km[1]);
-      const uint32_t bytes = (P.km_rows[0] + (DSL > 1 ? P.km_rows[1] : 0)) * 128;
-      const int panel0 = (b * P.Hkv + hk) * P.km_nhw;
-      int last[4] = {-1, -1, -1, -1};  // [half][buffer]: last use issued
-      bool ok = true;
-      for (int w = 0; ok && w <= WL; ++w) {
-        const int buf = w % nb, use = w / nb;
-        for (int hh = 0; hh < 2; ++hh) {
-          const int i = 2 * hh + buf;
-          if (use > 0 && !(ok = mbar_wait(&bars[B_BE + i], (use - 1) & 1, err, kErrBEmpty))) break;
-          mbar_expect_tx(&bars[B_BF + i], bytes);
-          uint8_t* dst = smem + P.bop + (hh * nb + buf) * P.b_buf_bytes;
-          for (int s = 0; s < DSL; ++s)
-            tma_load_3d(dst + P.b_slab_off[s], &P.tm_km[s], &bars[B_BF + i], 0, 0,
-                        panel0 + 2 * w + hh);
-          last[i] = use;
-        }
-      }
-      // no copy may still be in flight when the CTA exits
-      for (int i = 0; i < 4; ++i)
-        if (last[i] >= 0) mbar_wait(&bars[B_BF + i], last[i] & 1, err, kErrDrain);
-    }
-    __syncwarp();
-    regs_inc<128>();
   } else if (warp >= 12) {
-    // ----------------------- K^(m) builder (+ per-dimension combine, dK launch)
+    // ------ K^(m) builder (without panels) + accumulation into the workspace:
+    // dQ launch: dV^T and dK_gate^T of each window; dK launch: the
+    // per-dimension combine of C^T
     regs_dec<kBldRegs>();
     named_bar(1, kThreads);
     const int kMaxItems = P.max_items;
     const int gt = tid - 384;
     uint2* items = reinterpret_cast<uint2*>(smem + L::ITEMS);
     int my_n = 0;
-    {
+    if (!KMT) {
       int item_end[8];
       int acc = 0;
 #pragma unroll
@@ -556,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             if (it >= item_end[q]) { s2 = q + 1; base = item_end[q]; }
           const int local = it - base;
           const int r = local >> 1, c = 2 * s2 + (local & 1), m = r >> 3, j = r & 7;
-          const uint32_t kofs = (c >> 3) * 4096 + j * 128 + (((c & 7) ^ j) << 4);
+          const uint32_t kofs = (c >> 3) * 2048 + j * 128 + (((c & 7) ^ j) << 4);
           const uint32_t cofs = (m * NPX + 4 * c) * 4;
           const uint32_t bofs = P.b_slab_off[c >> 3] + sw128_offset(r, c & 7);
           const uint32_t flags = (m & 1) | ((m & 2) ? 2u : 0u) | (((m + 1) & 2) ? 4u : 0u);
@@ -590,13 +637,13 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 
     auto build = [&](int w) -> bool {
       const int buf = w % nb, use = w / nb;
-      const int n = w >> 1, st = n & 1;
-      if (!wwait(bars[B_KVF + st], (n >> 1) & 1, err, kErrKvFull)) return false;
+      const int st = w & 1;
+      if (!wwait(bars[B_KVF + st], (w >> 1) & 1, err, kErrKvFull)) return false;
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
         if (use > 0 && !wwait(bars[B_BE + 2 * hh + buf], (use - 1) & 1, err, kErrBEmpty))
           return false;
-        const uint32_t kt = sK + st * NS * 4096 + (2 * (w & 1) + hh) * 1024;
+        const uint32_t kt = sK + st * NS * 2048 + hh * 1024;
         const uint32_t bt = sB + (hh * nb + buf) * P.b_buf_bytes;
 #pragma unroll 1
         for (int i0 = 0; i0 < my_n; i0 += 4) {
@@ -633,7 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         fence_async_smem();
         mbar_arrive(&bars[B_BF + 2 * hh + buf]);
       }
-      if (w & 1) mbar_arrive(&bars[B_KVE + st]);
+      mbar_arrive(&bars[B_KVE + st]);
       return true;
     };
 
@@ -669,38 +716,42 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         tc_fence_before();
         mbar_arrive(&bars[B_CE + hh]);
       }
-      float dv[16];
-      {
-        if (!wwait(bars[B_CF2], w & 1, err, kErrC)) return false;
-        tc_fence_after();
-        uint32_t g[2][16];
-        tmem_ld16(lane_base + tk::DVK, g[0]);       // dO^T P  (16 keys)
-        tmem_ld16(lane_base + tk::DVK + 16, g[1]);  // Q^T dS  (16 keys)
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&bars[B_CE2]);
+      const int d = gt;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          dv[j] = __uint_as_float(g[0][j]);
-          dk[j] += __uint_as_float(g[1][j]);
-        }
+      for (int j = 0; j < 16; ++j) {
+        const int key = w * kW + j;
+        if (key < P.Sk && d < D) atomicAdd(dk32 + (int64_t)key * D + d, dk[j]);
       }
+      return true;
+    };
+
+    // dQ launch: dV^T = dO^T P and dK_gate^T = Q^T dS of window w (this
+    // thread's head dim d, the window's 16 keys) into the accumulators
+    auto dvk = [&](int w) -> bool {
+      if (!wwait(bars[B_CF2], w & 1, err, kErrC)) return false;
+      tc_fence_after();
+      uint32_t g[2][16];
+      tmem_ld16(lane_base + tq::DVK, g[0]);       // dO^T P  (16 keys)
+      tmem_ld16(lane_base + tq::DVK + 16, g[1]);  // Q^T dS  (16 keys)
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bars[B_CE2]);
       const int d = gt;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = w * kW + j;
         if (key < P.Sk && d < D) {
-          atomicAdd(dk32 + (int64_t)key * D + d, dk[j]);
-          atomicAdd(dv32 + (int64_t)key * D + d, dv[j]);
+          atomicAdd(dv32 + (int64_t)key * D + d, __uint_as_float(g[0][j]));
+          atomicAdd(dk32 + (int64_t)key * D + d, __uint_as_float(g[1][j]));
         }
       }
       return true;
     };
 
-    bool ok = build(0);
+    bool ok = KMT ? true : build(0);
     for (int w = 0; ok && w <= WL; ++w) {
-      if (w + 1 <= WL) ok = build(w + 1);
-      if (ok && MODE == MODE_DK) ok = combine(w);
+      if (!KMT && w + 1 <= WL) ok = build(w + 1);
+      if (ok) ok = MODE == MODE_DK ? combine(w) : dvk(w);
     }
     __syncwarp();
     regs_inc<128>();
@@ -722,10 +773,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     const float delta = P.delta[ri];
     const uint32_t s_xch = smem_u32(smem + L::XCH);
     const uint32_t s_cs = sY + (rg * 128 + r) * 16;  // dQ: staged (cos, sin), chunk q at + 4096 q
-    // gate prefix through the current window, compensated (Kahan): the prefix
-    // reaches ~S/2, where fp32 steps are 2^-10 at S = 32768, and a plain
-    // running sum over S/16 windows drifts by ~1e-2 -- an angle error of that
-    // size in the fastest rotation.  base - base_c is the prefix to ~1 ulp.
+    // compensated gate prefix through the current window (advance_prefix)
     float base = 0.f, base_c = 0.f;
     float carry = 0.f;   // gate sum of the keys after the current window
     float da_run = 0.f;  // gate-gradient prefix before the current half
@@ -748,21 +796,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       mbar_arrive(&bars[B_SDE + sb]);
       const int j0 = w * kW;
       float z[16], uu[16];
-      if (diag_window(w)) {
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj)
-          z[jj] = (row_ok && j0 + jj <= t) ? sigmoid_f(__uint_as_float(sraw[jj])) : 0.f;
-      } else {
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) z[jj] = sigmoid_f(__uint_as_float(sraw[jj]));
-      }
-      float suf = 0.f;  // in-window suffix after key jj
-#pragma unroll
-      for (int jj = 15; jj >= 0; --jj) {
-        uu[jj] = fmaf(suf, 1.0f / kC0, -1.0f);
-        suf += z[jj];
-      }
-      const float zsum = suf;
+      const float zsum = diag_window(w) ? window_gates<true>(sraw, j0, t, row_ok, z, uu)
+                                        : window_gates<false>(sraw, j0, t, row_ok, z, uu);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int kk = 8 * (i >> 2) + (i & 3);
@@ -774,13 +809,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         dpo[i] = __uint_as_float(d4a[i]);
         dpo[4 + i] = __uint_as_float(d4b[i]);
       }
-      {
-        const float y = zsum - base_c;
-        const float s2 = base + y;
-        base_c = (s2 - base) - y;
-        base = s2;
-      }
-      carry = (A_t - base) + base_c;
+      carry = advance_prefix(zsum, A_t, base, base_c);
       return true;
     };
 
@@ -898,7 +927,6 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     auto halves = [&](int w) -> bool {
       const int j0 = w * kW;
       uint8_t* const hblk = hblk0 ? hblk0 + (int64_t)w * kHB : nullptr;
-      if (hblk && rg == 0) *reinterpret_cast<float*>(hblk + HB_C + 4 * r) = carry;
       if (MODE == MODE_DK) {
         // the previous window's C GEMMs are done with the A rows and the Y
         // buffer: copy this window's A half from tensor to shared memory
@@ -917,7 +945,6 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           }
         }
       }
-      uint32_t dsa0 = 0u, dsa1 = 0u;  // dS of half A (packed), written with half B
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
         if (!wwait(bars[B_GF + hh], w & 1, err, kErrG)) return false;
@@ -957,9 +984,12 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             sum4 += da[i];
           }
         }
-        // publish this group's sum for the partner group
-        sts32f(s_xch + ((hh * 2 + rg) * 128 + r) * 4, sum4);
-        mbar_arrive(&bars[B_XCH + hh]);
+        // publish this group's sum for the partner group (the dK launch
+        // needs no gate gradient)
+        if (MODE == MODE_DQ) {
+          sts32f(s_xch + ((hh * 2 + rg) * 128 + r) * 4, sum4);
+          mbar_arrive(&bars[B_XCH + hh]);
+        }
         // Y_m = dl T_m(u), packed per term for the group's 4 keys
         uint32_t y[kM][2];
 #pragma unroll
@@ -992,15 +1022,20 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             tc_fence_before();
             mbar_arrive(&bars[B_YA]);
           }
+          // P -> chunk 4 + hh of the P | dS rows (B operand of dV^T); the
+          // previous window's GEMMs are done with them (B_YTFREE above)
+          sts64(sDS + sw128_offset(r, 4 + hh) + 8 * rg, E::pack(pr[0], pr[1]),
+                E::pack(pr[2], pr[3]));
         } else {
-          // Y | P rows into shared memory (B operand of the C GEMMs)
+          // Y rows into shared memory (B operand of the C GEMMs)
           if (hh == 1 && !wwait(bars[B_YDONE], w & 1, err, kErrY)) return false;
 #pragma unroll
           for (int m = 0; m < kM; ++m)  // element 8 m + key: chunk m of the row
             sts64(sY + (m >> 3) * 16384 + sw128_offset(r, m & 7) + 8 * rg, y[m][0], y[m][1]);
-          sts64(sDS + sw128_offset(r, 4 + hh) + 8 * rg, E::pack(pr[0], pr[1]),
-                E::pack(pr[2], pr[3]));
+          fence_async_smem();
+          mbar_arrive(&bars[hh ? B_YB : B_YA]);
         }
+        if (MODE == MODE_DK) continue;
         // gate-gradient prefix: group 0's keys precede group 1's in the half
         if (!wwait(bars[B_XCH + hh], w & 1, err, kErrXch)) return false;
         const float other = lds32f(s_xch + ((hh * 2 + (rg ^ 1)) * 128 + r) * 4);
@@ -1012,32 +1047,20 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           run += da[i];
         }
         da_run += sum4 + other;
-        const uint32_t ds0 = E::pack(ds[0], ds[1]), ds1 = E::pack(ds[2], ds[3]);
         if (hblk) {
           const int qd = 2 * hh + rg;
-          *reinterpret_cast<float4*>(hblk + HB_DL + (qd * 128 + r) * 16) =
-              make_float4(dl[0], dl[1], dl[2], dl[3]);
-          *reinterpret_cast<uint4*>(hblk + HB_PD + (qd * 128 + r) * 16) =
-              make_uint4(E::pack(pr[0], pr[1]), E::pack(pr[2], pr[3]), ds0, ds1);
-          *reinterpret_cast<uint2*>(hblk + HB_U + (qd * 128 + r) * 8) =
-              make_uint2(u_encode(uj[0]) | (u_encode(uj[1]) << 16),
-                         u_encode(uj[2]) | (u_encode(uj[3]) << 16));
+          *reinterpret_cast<uint2*>(hblk + (qd * 128 + r) * 8) =
+              make_uint2(pack_dl(dl[0], dl[1]), pack_dl(dl[2], dl[3]));
         }
-        if (MODE == MODE_DQ) {
-          if (hh == 0) {
-            dsa0 = ds0;
-            dsa1 = ds1;
-          } else {
-            tmem_st2(lane_base + tq::YT + 4 * kM + 2 * rg, dsa0, dsa1);
-            tmem_st2(lane_base + tq::YT + 4 * kM + 4 + 2 * rg, ds0, ds1);
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&bars[B_YB]);
-          }
-        } else {
-          sts64(sDS + sw128_offset(r, 6 + hh) + 8 * rg, ds0, ds1);
+        // dS -> chunk 6 + hh of the P | dS rows (A operand of dq += dS K,
+        // B operand of dK_gate^T); half B completes the window's rows
+        sts64(sDS + sw128_offset(r, 6 + hh) + 8 * rg, E::pack(ds[0], ds[1]),
+              E::pack(ds[2], ds[3]));
+        if (hh == 1) {
           fence_async_smem();
-          mbar_arrive(&bars[hh ? B_YB : B_YA]);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&bars[B_YB]);
         }
       }
       return true;
@@ -1123,50 +1146,56 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 }
 
 // ------------------------------------------------------------------
-// dK launch fed by the dQ launch's hand-off.  Per window it only rebuilds
-// the A rows v = R((carry + c0) theta) q and Y_m = dl T_m(u), then runs
-//   C^T = v^T Y (each half), dV^T = dO^T P and dK_gate^T = Q^T dS
-// on the tensor cores and the per-dimension combine with fp32 atomics into
-// the dk / dv accumulators.  No K/V tiles, gates, G GEMM or K^(m) are needed.
+// dK launch fed by the dQ launch's hand-off (dl of every (row, key), f16).
+// Per window it recomputes the gate scores Q K^T on the tensor cores and, with
+// the dQ launch's own arithmetic (window_gates, advance_prefix), the in-window
+// positions u and the carry; rebuilds the A rows v = R((carry + c0) theta) q
+// and Y_m = dl T_m(u); then runs
+//   C^T = v^T Y  (each half; M = head dim, N = 16 terms x 8 keys, K = the 128
+//                 query rows)
+// on the tensor cores and the per-dimension combine with fp32 atomics into the
+// dk accumulator.  dV and the gate part of dK come from the dQ launch.
 //
 // Roles (512 threads): warps 0-7 two row warpgroups (group g: pairs
-// 32g..32g+31 of the A rows, keys 4g..4g+3 of each half); warp 8 TMA; warp 9
-// UMMA; warps 12-15 combine (one head dim per thread); registers re-split as
-// in the dQ launch.  The A rows and the tensor-memory accumulators are
+// 32g..32g+31 of the A rows, keys 4g..4g+3 of each half); warp 8 TMA (Q once,
+// the 16 keys of each window); warp 9 UMMA for C; warp 10 UMMA for the gate
+// scores; warps 12-15 combine (one head dim per thread); registers re-split as
+// in the dQ launch.  The A rows, the gate scores and the half-A C^T region are
 // double-buffered over windows.
-namespace k2 {
-constexpr int Q = 0, DO = 32768, AV = 65536;  // AV: 2 buffers of [NS][128][128 B]
-constexpr int YA = AV + 2 * 32768;            // Y half A rows (16 terms x 8 keys)
-constexpr int YB = YA + 32768;                // Y half B rows
-constexpr int PD = YB + 32768;                // P (chunks 4-5) | dS (chunks 6-7) rows
-constexpr int COEF = PD + 16384;
+namespace k3 {
+constexpr int Q = 0, AV = 32768;             // AV: 2 buffers of [NS][128][128 B]
+constexpr int YA = AV + 2 * 32768;           // Y half A rows (16 terms x 8 keys)
+constexpr int YB = YA + 32768;               // Y half B rows
+constexpr int KT = YB + 32768;               // a window's keys: [2 stages][NS][16][128 B]
+constexpr int COEF = KT + 2 * NS * 2048;
 constexpr int TH = COEF + kMB * NPX * 4;
 constexpr int BAR = TH + NPX * 4;
-constexpr int SLOT = BAR + 16 * 8;
+constexpr int SLOT = BAR + 24 * 8;
 constexpr int TOTAL = SLOT + 16;
 // RDY / YFREE per half: the rows write the next window's half A while the
 // tensor core still reads half B of the current one
 enum { B_Q = 0, B_RDY = 1, B_AVE = 3, B_YFREE = 5, B_CF = 7, B_CE = 9, B_DRAIN = 11,
-       B_CE1 = 12 };
-// tensor memory: C^T of half A double-buffered (window parity b at 128 b),
-// C^T of half B single (its GEMM waits until the combine has read it), and
-// dV^T | dK_gate^T double-buffered
-constexpr uint32_t C0 = 0, C1 = 256, DVK = 384;
-}  // namespace k2
+       B_CE1 = 12, B_KF = 13, B_KE = 15, B_SF = 17, B_SE = 19, B_DRAIN2 = 21 };
+// tensor memory: C^T of half A double-buffered (window parity b at 128 b), C^T
+// of half B single (its GEMM waits until the combine has read it), the gate
+// scores double-buffered
+constexpr uint32_t C0 = 0, C1 = 256, SG = 384;
+static_assert(SG + 32 <= 512, "tmem");
+}  // namespace k3
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(kThreads, 1) dk3_kernel(const __grid_constant__ Params P) {
   using E = ElemTraits<T>;
   using namespace sm100;
-  constexpr int NP = D / 2, DSL = D / 64, PW = NP / 2;
+  constexpr int NP = D / 2, DSL = D / 64, PW = NP / 2, KSTEPS = D / 16;
   constexpr int kM = kMB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + k2::BAR);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + k2::SLOT);
-  float* s_coef = reinterpret_cast<float*>(smem + k2::COEF);
-  float* s_th = reinterpret_cast<float*>(smem + k2::TH);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + k3::BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + k3::SLOT);
+  float* s_coef = reinterpret_cast<float*>(smem + k3::COEF);
+  float* s_th = reinterpret_cast<float*>(smem + k3::TH);
   int* err = &g_corope_bwd_error;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1179,26 +1208,29 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
   const int WL = min(S - 1, q0 + kBM - 1) / kW;
 
   if (tid == 0) {
-    mbar_init(&bars[k2::B_Q], 1);
+    mbar_init(&bars[k3::B_Q], 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[k2::B_RDY + i], 256);
-      mbar_init(&bars[k2::B_YFREE + i], 1);
-      mbar_init(&bars[k2::B_AVE + i], 1);
-      mbar_init(&bars[k2::B_CF + i], 1);
-      mbar_init(&bars[k2::B_CE + i], 128);
+      mbar_init(&bars[k3::B_RDY + i], 256);
+      mbar_init(&bars[k3::B_YFREE + i], 1);
+      mbar_init(&bars[k3::B_AVE + i], 1);
+      mbar_init(&bars[k3::B_CF + i], 1);
+      mbar_init(&bars[k3::B_CE + i], 128);
+      mbar_init(&bars[k3::B_KF + i], 1);
+      mbar_init(&bars[k3::B_KE + i], 1);
+      mbar_init(&bars[k3::B_SF + i], 1);
+      mbar_init(&bars[k3::B_SE + i], 256);
     }
-    mbar_init(&bars[k2::B_DRAIN], 1);
-    mbar_init(&bars[k2::B_CE1], 128);
+    mbar_init(&bars[k3::B_DRAIN], 1);
+    mbar_init(&bars[k3::B_DRAIN2], 1);
+    mbar_init(&bars[k3::B_CE1], 128);
     fence_mbar_init();
   }
   for (int i = tid; i < kM * NPX; i += kThreads) s_coef[i] = P.coef[i / NPX][i % NPX];
   for (int p = tid; p < NP; p += kThreads) s_th[p] = theta_at(P.thetas, P.theta, p, D);
-  if (DSL == 1) {  // D = 64: the second slab of Q, dO and both A buffers is zero
+  if (DSL == 1) {  // D = 64: the second slab of both A buffers is zero
     for (int i = tid; i < 1024; i += kThreads) {
-      reinterpret_cast<uint4*>(smem + k2::Q + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
-      reinterpret_cast<uint4*>(smem + k2::DO + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
-      reinterpret_cast<uint4*>(smem + k2::AV + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
-      reinterpret_cast<uint4*>(smem + k2::AV + 32768 + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
+      reinterpret_cast<uint4*>(smem + k3::AV + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
+      reinterpret_cast<uint4*>(smem + k3::AV + 32768 + 16384)[i] = make_uint4(0u, 0u, 0u, 0u);
     }
     fence_async_smem();
   }
@@ -1210,70 +1242,90 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t sQ = smem_u32(smem + k2::Q), sDO = smem_u32(smem + k2::DO);
-  const uint32_t sAV = smem_u32(smem + k2::AV);
-  const uint32_t sYA = smem_u32(smem + k2::YA), sYB = smem_u32(smem + k2::YB);
-  const uint32_t sPD = smem_u32(smem + k2::PD);
+  const uint32_t sQ = smem_u32(smem + k3::Q), sAV = smem_u32(smem + k3::AV);
+  const uint32_t sYA = smem_u32(smem + k3::YA), sYB = smem_u32(smem + k3::YB);
+  const uint32_t sKT = smem_u32(smem + k3::KT);
   const uint32_t s_th_u = smem_u32(s_th);
 
   if (warp >= 8 && warp < 12) {
-  regs_dec<kCtlRegs>();
-  named_bar(1, kThreads);
-  if (warp == 8) {
-    // ------------------------------------------------------------ TMA
-    if (lane == 0) {
+    regs_dec<kCtlRegs>();
+    named_bar(1, kThreads);
+    if (warp == 8 && lane == 0) {
+      // ---------------------------------------------------------- TMA
       prefetch_tmap(&P.tm_q);
-      prefetch_tmap(&P.tm_do);
-      mbar_expect_tx(&bars[k2::B_Q], 2 * DSL * 16384);
-      for (int s = 0; s < DSL; ++s) {
-        tma_load_4d(smem + k2::Q + s * 16384, &P.tm_q, &bars[k2::B_Q], 64 * s, q0 - P.r0, h, b);
-        tma_load_4d(smem + k2::DO + s * 16384, &P.tm_do, &bars[k2::B_Q], 64 * s, q0 - P.r0, h, b);
+      prefetch_tmap(&P.tm_k);
+      mbar_expect_tx(&bars[k3::B_Q], DSL * 16384);
+      for (int s = 0; s < DSL; ++s)
+        tma_load_4d(smem + k3::Q + s * 16384, &P.tm_q, &bars[k3::B_Q], 64 * s, q0 - P.r0, h, b);
+      int last_use[2] = {-1, -1};
+      for (int n = 0; n <= WL; ++n) {  // the keys of window n
+        const int st = n & 1, u = n >> 1;
+        if (n >= 2 && !mbar_wait(&bars[k3::B_KE + st], (u - 1) & 1, err, kErrKvEmpty)) break;
+        mbar_expect_tx(&bars[k3::B_KF + st], DSL * 2048);
+        for (int s = 0; s < DSL; ++s)
+          tma_load_4d(smem + k3::KT + (st * NS + s) * 2048, &P.tm_k, &bars[k3::B_KF + st],
+                      64 * s, kKT * n, hk, b);
+        last_use[st] = u;
       }
-      mbar_wait(&bars[k2::B_Q], 0, err, kErrDrain);
-    }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ UMMA
-    if (lane == 0) {
+      // no copy may still be in flight when the CTA exits
+      mbar_wait(&bars[k3::B_Q], 0, err, kErrDrain);
+      for (int st = 0; st < 2; ++st)
+        if (last_use[st] >= 0) mbar_wait(&bars[k3::B_KF + st], last_use[st] & 1, err, kErrDrain);
+    } else if (warp == 9 && lane == 0) {
+      // ------------------------------------------------- UMMA: C^T = v^T Y
+      // half A, then half B; K = the 128 query rows, 16 per step
       const uint32_t id_c = idesc_f16(128, 8 * kM, E::kBf16, true) | (1u << 15);  // A, B MN-major
-      const uint32_t id_s = idesc_f16(128, 16, E::kBf16, true) | (1u << 15);
-      bool ok = mbar_wait(&bars[k2::B_Q], 0, err, kErrQ);
+      bool ok = true;
       for (int w = 0; ok && w <= WL; ++w) {
         const int bf = w & 1;
         const uint32_t av = sAV + 32768 * bf;
-        // half A: C^T = v^T Y_A and dV^T = dO^T P; then half B: C^T = v^T Y_B
-        // and dK_gate^T = Q^T dS.  K = the 128 query rows, 16 per step.
         for (int hh = 0; hh < 2 && ok; ++hh) {
-          if (!(ok = mbar_wait(&bars[k2::B_RDY + hh], w & 1, err, kErrY))) break;
+          if (!(ok = mbar_wait(&bars[k3::B_RDY + hh], w & 1, err, kErrY))) break;
           if (hh == 0 && w >= 2 &&
-              !(ok = mbar_wait(&bars[k2::B_CE + bf], ((w >> 1) - 1) & 1, err, kErrCEmpty)))
+              !(ok = mbar_wait(&bars[k3::B_CE + bf], ((w >> 1) - 1) & 1, err, kErrCEmpty)))
             break;
           if (hh == 1 && w >= 1 &&
-              !(ok = mbar_wait(&bars[k2::B_CE1], (w - 1) & 1, err, kErrCEmpty)))
+              !(ok = mbar_wait(&bars[k3::B_CE1], (w - 1) & 1, err, kErrCEmpty)))
             break;
           tc_fence_after();
           const uint32_t yr = hh ? sYB : sYA;
-          const uint32_t other = hh ? sQ : sDO;
-          const uint32_t cacc = tmem + (hh ? k2::C1 : k2::C0 + 128 * bf);
+          const uint32_t cacc = tmem + (hh ? k3::C1 : k3::C0 + 128 * bf);
 #pragma unroll 1
-          for (int s = 0; s < 8; ++s) {
+          for (int s = 0; s < 8; ++s)
             mma_ss(cacc, sdesc_mnmajor(av + 2048 * s, 16384), sdesc_mnmajor(yr + 2048 * s, 16384),
                    id_c, s > 0);
-            mma_ss(tmem + k2::DVK + 32 * bf + 16 * hh, sdesc_mnmajor(other + 2048 * s, 16384),
-                   sdesc_mnmajor(sPD + 2048 * s + 64 + 32 * hh, 16384), id_s, s > 0);
-          }
           if (hh == 1) {
-            mma_commit(&bars[k2::B_CF + bf]);
-            mma_commit(&bars[k2::B_AVE + bf]);
+            mma_commit(&bars[k3::B_CF + bf]);
+            mma_commit(&bars[k3::B_AVE + bf]);
           }
-          mma_commit(&bars[k2::B_YFREE + hh]);
+          mma_commit(&bars[k3::B_YFREE + hh]);
         }
       }
-      mma_commit(&bars[k2::B_DRAIN]);
-      mbar_wait(&bars[k2::B_DRAIN], 0, err, kErrDrain);
+      mma_commit(&bars[k3::B_DRAIN]);
+      mbar_wait(&bars[k3::B_DRAIN], 0, err, kErrDrain);
+    } else if (warp == 10 && lane == 0) {
+      // --------------------------------------- UMMA: gate scores Q K^T
+      const uint32_t id_gate = idesc_f16(128, 16, E::kBf16, false);
+      bool ok = mbar_wait(&bars[k3::B_Q], 0, err, kErrQ);
+      for (int w = 0; ok && w <= WL; ++w) {
+        const int st = w & 1;
+        ok = mbar_wait(&bars[k3::B_KF + st], (w >> 1) & 1, err, kErrKvFull);
+        if (ok && w >= 2) ok = mbar_wait(&bars[k3::B_SE + st], ((w >> 1) - 1) & 1, err, kErrSdEmpty);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t kt = sKT + st * NS * 2048;
+#pragma unroll
+        for (int s = 0; s < KSTEPS; ++s)
+          mma_ss(tmem + k3::SG + 16 * st, sdesc_kmajor(sQ + (s >> 2) * 16384 + 32 * (s & 3)),
+                 sdesc_kmajor(kt + (s >> 2) * 2048 + 32 * (s & 3)), id_gate, s > 0);
+        mma_commit(&bars[k3::B_SF + st]);
+        mma_commit(&bars[k3::B_KE + st]);
+      }
+      mma_commit(&bars[k3::B_DRAIN2]);
+      mbar_wait(&bars[k3::B_DRAIN2], 0, err, kErrDrain);
     }
-  }
-  __syncwarp();
-  regs_inc<128>();
+    __syncwarp();
+    regs_inc<128>();
   } else if (warp >= 12) {
     // ------------------------------------------------------------ combine
     regs_dec<kBldRegs>();
@@ -1296,15 +1348,14 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
     }
     const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
     float* dk32 = P.dk32 + ((int64_t)b * P.Hkv + hk) * P.Sk * D + gt;
-    float* dv32 = P.dv32 + ((int64_t)b * P.Hkv + hk) * P.Sk * D + gt;
     for (int w = 0; w <= WL; ++w) {
       const int bf = w & 1;
-      if (!wwait(bars[k2::B_CF + bf], (w >> 1) & 1, err, kErrC)) break;
+      if (!wwait(bars[k3::B_CF + bf], (w >> 1) & 1, err, kErrC)) break;
       tc_fence_after();
-      float dk[16], dv[16];
+      float dk[16];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        const uint32_t creg = lane_base + (hh ? k2::C1 : k2::C0 + 128 * bf);
+        const uint32_t creg = lane_base + (hh ? k3::C1 : k3::C0 + 128 * bf);
         // even terms use this lane's column of C^T; odd terms the partner
         // component's (d ^ 1), whose coefficient for this lane is minus the
         // partner's own: each lane sums its odd terms with -cm and the sums
@@ -1332,31 +1383,17 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
         }
         if (hh == 1) {  // the single half-B region is free for the next window
           tc_fence_before();
-          mbar_arrive(&bars[k2::B_CE1]);
+          mbar_arrive(&bars[k3::B_CE1]);
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) dk[8 * hh + j] = ev[j] + __shfl_xor_sync(0xffffffffu, od[j], 1);
       }
-      {
-        uint32_t g[2][16];
-        tmem_ld16(lane_base + k2::DVK + 32 * bf, g[0]);       // dO^T P  (16 keys)
-        tmem_ld16(lane_base + k2::DVK + 32 * bf + 16, g[1]);  // Q^T dS  (16 keys)
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          dv[j] = __uint_as_float(g[0][j]);
-          dk[j] += __uint_as_float(g[1][j]);
-        }
-      }
       tc_fence_before();
-      mbar_arrive(&bars[k2::B_CE + bf]);
+      mbar_arrive(&bars[k3::B_CE + bf]);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = w * kW + j;
-        if (key < P.Sk && gt < D) {
-          atomicAdd(dk32 + (int64_t)key * D, dk[j]);
-          atomicAdd(dv32 + (int64_t)key * D, dv[j]);
-        }
+        if (key < P.Sk && gt < D) atomicAdd(dk32 + (int64_t)key * D, dk[j]);
       }
     }
     __syncwarp();
@@ -1367,38 +1404,55 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
     named_bar(1, kThreads);
     const int rg = warp >> 2;
     const int r = tid & 127;
+    const int t = q0 + r;
+    const bool row_ok = t < S;
+    auto diag_window = [&](int w) { return w * kW + kW - 1 > q0 || q0 + kBM > S; };
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const int64_t ri = ((int64_t)b * P.H + h) * P.S + min(t - P.r0, P.S - 1);
+    const float A_t = P.a[ri];
     const uint8_t* hb0 =
         P.handoff + ((int64_t)blockIdx.y * P.blocks_bh + chunk_block0(P.r0, qt)) * kHB;
-    struct Rec {
-      float4 dl[2];
-      uint2 u[2];
-      uint4 pd[2];
-      float carry;
-    };
-    auto load = [&](int w, Rec& x) {
+    // dl of this group's 4 keys of each half of window w (f16 pairs)
+    auto load = [&](int w, uint2 (&x)[2]) {
       const uint8_t* hb = hb0 + (int64_t)w * kHB;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int qd = 2 * hh + rg;
-        const uint4 dl = ldg128_nc(hb + HB_DL + (qd * 128 + r) * 16);
-        x.dl[hh] = make_float4(__uint_as_float(dl.x), __uint_as_float(dl.y),
-                               __uint_as_float(dl.z), __uint_as_float(dl.w));
-        x.pd[hh] = ldg128_nc(hb + HB_PD + (qd * 128 + r) * 16);
-        x.u[hh] = ldg64_nc(hb + HB_U + (qd * 128 + r) * 8);
-      }
-      x.carry = ldg32f_nc(hb + HB_C + 4 * r);
+      for (int hh = 0; hh < 2; ++hh) x[hh] = ldg64_nc(hb + ((2 * hh + rg) * 128 + r) * 8);
     };
     const float th_max = theta_max(s_th, NP);
-    bool ok = wwait(bars[k2::B_Q], 0, err, kErrQ);
-    Rec cur, nxt;
+    float base = 0.f, base_c = 0.f;  // compensated gate prefix (advance_prefix)
+    bool ok = wwait(bars[k3::B_Q], 0, err, kErrQ);
+    uint2 cur[2], nxt[2];
     load(0, cur);
     for (int w = 0; ok && w <= WL; ++w) {
       if (w < WL) load(w + 1, nxt);
+      // ---- gates and positions of window w (the dQ launch's arithmetic)
+      const int st = w & 1;
+      if (!(ok = wwait(bars[k3::B_SF + st], (w >> 1) & 1, err, kErrSd))) break;
+      tc_fence_after();
+      float uo[8];
+      float carry;
+      {
+        uint32_t sraw[16];
+        tmem_ld16(lane_base + k3::SG + 16 * st, sraw);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars[k3::B_SE + st]);
+        float z[16], uu[16];
+        const float zsum = diag_window(w) ? window_gates<true>(sraw, w * kW, t, row_ok, z, uu)
+                                          : window_gates<false>(sraw, w * kW, t, row_ok, z, uu);
+        carry = advance_prefix(zsum, A_t, base, base_c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int kk = 8 * (i >> 2) + (i & 3);
+          uo[i] = rg ? uu[kk + 4] : uu[kk];
+        }
+      }
       // ---- A rows of this group's slab into buffer w & 1
-      if (w >= 2 && !(ok = wwait(bars[k2::B_AVE + (w & 1)], ((w >> 1) - 1) & 1, err, kErrAvEmpty)))
+      if (w >= 2 &&
+          !(ok = wwait(bars[k3::B_AVE + (w & 1)], ((w >> 1) - 1) & 1, err, kErrAvEmpty)))
         break;
       {
-        const float bse = cur.carry + kC0;
+        const float bse = carry + kC0;
         const bool mufu_reduce = __all_sync(0xffffffffu, bse * th_max < kMufuReduceMax);
         const uint32_t av = sAV + 32768 * (w & 1);
 #pragma unroll 1
@@ -1437,15 +1491,15 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
           }
         }
       }
-      // ---- Y_A and P rows, then Y_B and dS rows, each once the previous
-      // window's GEMMs of that half are done with them
+      // ---- Y_A, then Y_B, each once the previous window's GEMM of that half
+      // is done with its rows
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        if (w >= 1 && !(ok = wwait(bars[k2::B_YFREE + hh], (w - 1) & 1, err, kErrY))) break;
+        if (w >= 1 && !(ok = wwait(bars[k3::B_YFREE + hh], (w - 1) & 1, err, kErrY))) break;
         const uint32_t yrow = hh ? sYB : sYA;
-        const float dl[4] = {cur.dl[hh].x, cur.dl[hh].y, cur.dl[hh].z, cur.dl[hh].w};
-        const float uj[4] = {u_decode(cur.u[hh].x & 0xffffu), u_decode(cur.u[hh].x >> 16),
-                             u_decode(cur.u[hh].y & 0xffffu), u_decode(cur.u[hh].y >> 16)};
+        const float2 d01 = unpack_dl(cur[hh].x), d23 = unpack_dl(cur[hh].y);
+        const float dl[4] = {d01.x, d01.y, d23.x, d23.y};
+        const float uj[4] = {uo[4 * hh], uo[4 * hh + 1], uo[4 * hh + 2], uo[4 * hh + 3]};
         uint32_t y[kM][2];
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
@@ -1464,21 +1518,14 @@ __global__ void __launch_bounds__(kThreads, 1) dk2_kernel(const __grid_constant_
           }
         }
 #pragma unroll
-        for (int m = 0; m < kM; ++m)
+        for (int m = 0; m < kM; ++m)  // element 8 m + key: chunk m of the row
           sts64(yrow + (m >> 3) * 16384 + sw128_offset(r, m & 7) + 8 * rg, y[m][0], y[m][1]);
-        // P of both halves -> chunks 4, 5 of the P | dS rows; dS -> chunks 6, 7
-#pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2) {
-          if (hh == 0)
-            sts64(sPD + sw128_offset(r, 4 + q2) + 8 * rg, cur.pd[q2].x, cur.pd[q2].y);
-          else
-            sts64(sPD + sw128_offset(r, 6 + q2) + 8 * rg, cur.pd[q2].z, cur.pd[q2].w);
-        }
         fence_async_smem();
-        mbar_arrive(&bars[k2::B_RDY + hh]);
+        mbar_arrive(&bars[k3::B_RDY + hh]);
       }
       if (!ok) break;
-      cur = nxt;
+      cur[0] = nxt[0];
+      cur[1] = nxt[1];
     }
     __syncwarp();
     regs_dec<128>();
@@ -1508,15 +1555,6 @@ static int plan(Params& p) {
   return p.bop + 2 * p.nb * p.b_buf_bytes + 1024;
 }
 
-// Chebyshev terms of each backward kernel.  The derivative of the truncated
-// series converges one order slower than its value, so the backward keeps 16
-// terms where shared memory allows; the recompute dK kernel at head dim 128
-// holds 14 (its K^(m), Y and P | dS buffers do not fit with 16).
-template <int D, int MODE>
-struct Terms {
-  static constexpr int value = (MODE == MODE_DK && D == 128) ? 14 : kMB;
-};
-
 template <typename T, int D, int MODE, bool HAS_BIAS, int KM, bool KMT>
 static cudaError_t launch_k(const Params& p, int smem, dim3 grid, cudaStream_t st) {
   auto kern = bwd_kernel<T, D, MODE, HAS_BIAS, KM, KMT>;
@@ -1530,7 +1568,7 @@ static cudaError_t launch_k(const Params& p, int smem, dim3 grid, cudaStream_t s
 template <typename T, int D, int MODE>
 static cudaError_t launch_mode(Params& p, bool bias, int S, int nbh, cudaStream_t st,
                                float theta, float sm_scale) {
-  constexpr int KM = Terms<D, MODE>::value;
+  constexpr int KM = kMB;
   tcx::fill_coefficients<KM>(p.coef, p.nrow, D, theta, sm_scale);
   const int smem = plan<MODE, KM>(p);
   if (smem > kSmemLimit) return cudaErrorInvalidValue;
@@ -1543,12 +1581,12 @@ static cudaError_t launch_mode(Params& p, bool bias, int S, int nbh, cudaStream_
 }
 
 template <typename T, int D>
-static cudaError_t launch_dk2(Params& p, int S, int nbh, cudaStream_t st, float theta,
+static cudaError_t launch_dk3(Params& p, int S, int nbh, cudaStream_t st, float theta,
                               float sm_scale) {
   tcx::fill_coefficients<kMB>(p.coef, p.nrow, D, theta, sm_scale);
-  const int smem = k2::TOTAL + 1024;
+  const int smem = k3::TOTAL + 1024;
   dim3 grid((S + kBM - 1) / kBM, nbh);
-  auto kern = dk2_kernel<T, D>;
+  auto kern = dk3_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, smem, st>>>(p);
@@ -1620,7 +1658,7 @@ static cudaError_t launch_all(Params& p, const BwdArgs& a, bool bias, int BH, in
     p.bh0 = bh0;
     const int nbh = std::min(chunk, BH - bh0);
     e = launch_mode<T, D, MODE_DQ>(p, bias, S, nbh, st, theta, sm_scale);
-    if (e == cudaSuccess) e = launch_dk2<T, D>(p, S, nbh, st, theta, sm_scale);
+    if (e == cudaSuccess) e = launch_dk3<T, D>(p, S, nbh, st, theta, sm_scale);
   }
   return e;
 }
@@ -1643,16 +1681,9 @@ bool tc_bwd_supported(const BwdArgs& a, int dtype) {
   // small theta keeps more Chebyshev terms: the K^(m) buffers must still fit
   using namespace tcb;
   Params p;
-  constexpr int kDK128 = Terms<128, MODE_DK>::value, kDK64 = Terms<64, MODE_DK>::value;
   tcx::fill_coefficients<kMB>(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
   if (plan<MODE_DQ, kMB>(p) > tcx::kSmemLimit) return false;
-  if (a.D == 128) {
-    tcx::fill_coefficients<kDK128>(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
-    if (plan<MODE_DK, kDK128>(p) > tcx::kSmemLimit) return false;
-  } else {
-    tcx::fill_coefficients<kDK64>(p.coef, p.nrow, a.D, a.theta, a.sm_scale);
-    if (plan<MODE_DK, kDK64>(p) > tcx::kSmemLimit) return false;
-  }
+  if (plan<MODE_DK, kMB>(p) > tcx::kSmemLimit) return false;
   return tcx::get_encoder() != nullptr;
 }
 

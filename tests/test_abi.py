@@ -166,7 +166,7 @@ def test_chunk_argument_checks_without_gpu():
     keys.seq_len = 512
     panels = lib.corope_bwd_panel_bytes(ctypes.byref(keys))
     assert lo == 2 * 4 * 128 * 4 and panels > 0
-    assert hi - lo - panels == 4 * ((256 + 127) // 16 + 1) * 20992
+    assert hi - lo - panels == 4 * ((256 + 127) // 16 + 1) * 4096
 
 
 def test_size_queries_accept_null():

@@ -410,8 +410,9 @@ def test_long_context_s32768(mode):
     """The long-context shape of one GPU's share (S=32768, D=128 bf16, theta
     5e5, seed 4) on 4 heads: forward rows and the backward against the
     per-row oracle -- dq of sampled rows, dk and dv of the last 32 keys (whose
-    contributing rows are all sampled) -- with the hand-off region in full
-    (22 GB), two (b, h) slices at a time, or not at all."""
+    contributing rows are all sampled) -- with the "auto" workspace (the whole
+    hand-off region of the 4 slices, 4.3 GB, after the panels), two (b, h)
+    slices at a time (the fewest a launch takes at this length), or none."""
     from CoROPE import _lib
     B, H, S, D, theta = 1, 4, 32768, 128, 5e5
     (q, k, v, do), cpu = inputs(B, H, S, D, 4, torch.bfloat16)
@@ -424,7 +425,9 @@ def test_long_context_s32768(mode):
     lib = _lib.load_library()
     lo = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
     hi = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
-    ws = {"auto": "auto", "min": "min", "two-slices": lo + 2 * ((hi - lo) // (B * H))}[mode]
+    panels = lib.corope_bwd_panel_bytes(ctypes.byref(p))
+    per_bh = (hi - lo - panels) // (B * H)
+    ws = {"auto": "auto", "min": "min", "two-slices": lo + panels + 2 * per_bh}[mode]
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     _lib.bwd(q_, k_, v_, o_, do, m_, l_, a_, dq, dk, dv, sm, theta, algo="tensor", workspace=ws)
     torch.cuda.synchronize()
