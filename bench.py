@@ -15,6 +15,9 @@ configurations of the path, one line each:
 * ``mqa``      B=4, Hq=32, Hkv=1, S=8192, D=128, theta 5e5, forward
 * ``long``     B=1, H=32, S=32768, D=128, theta 5e5, forward + backward: one
                GPU's share of B=8 under batch x head sharding
+* ``plain``    plain causal softmax attention forward (no contextual
+               positions) at the bench shape on the same tensor-core pipeline,
+               with the CoRoPE forward timed beside it
 * ``long-seq`` the same sequences sharded over the ranks of a torchrun job
                (zig-zag query chunks, K/V all-gather, dk/dv reduce-scatter;
                global batch = number of ranks)
@@ -399,6 +402,9 @@ WORKLOADS = {
     "long": dict(B=1, H=32, Hkv=32, S=32768, D=128, theta=5e5, seed=4, bwd=True,
                  name="CoRoPE MHA fwd+bwd causal, per GPU B=1 H=32 S=32768 D=128 theta=5e5 "
                       "(one GPU's share of B=8: batch x head sharding)"),
+    "plain": dict(B=4, H=32, Hkv=32, S=4096, D=128, theta=1e4, seed=1, bwd=False, plain=True,
+                  name="plain causal softmax attention fwd (no contextual positions), per GPU "
+                       "B=4 H=32 S=4096 D=128: the baseline kernel on the same pipeline"),
     "long-seq": dict(B=1, H=32, Hkv=32, S=32768, D=128, theta=5e5, seed=4, bwd=True,
                      name="CoRoPE MHA fwd+bwd causal, B=world H=32 S=32768 D=128 theta=5e5, "
                           "every sequence sharded over all ranks (zig-zag query chunks)"),
@@ -408,6 +414,9 @@ WORKLOADS = {
 def workload_metric(name, w):
     if name == "bench":
         return METRIC
+    if w.get("plain"):
+        return (f"plain causal attention fwd TFLOP/s (bf16,B={w['B']},H={w['H']},S={w['S']},"
+                f"D={w['D']}) per GPU x N")
     what = "fwd+bwd" if w["bwd"] else "fwd"
     return (f"CoRoPE attn {what} TFLOP/s (bf16,B={w['B']},H={w['H']},Hkv={w['Hkv']},"
             f"S={w['S']},D={w['D']}) per GPU x N")
@@ -419,8 +428,10 @@ def run_ours(args):
     from CoROPE.co_rope_backward import co_rope_backward
     from CoROPE.co_rope_mqa_forward import co_rope_mqa_forward
     from CoROPE.forward import co_rope_forward
+    from CoROPE.flash import flash_attention
 
     w = dict(WORKLOADS[args.workload])
+    plain = bool(w.get("plain"))
     if args.shape:
         w["B"], w["H"], w["S"], w["D"] = (int(x) for x in args.shape.split(","))
         w["Hkv"] = 1 if args.workload == "mqa" else w["H"]
@@ -451,6 +462,8 @@ def run_ours(args):
     del ins
 
     def forward(q_, k_, v_):
+        if plain:
+            return None, flash_attention(q_, k_, v_, causal=True, sm_scale=sm)
         if seq_sharded:
             return cp.co_rope_forward_cp(q_, k_, v_, sm, theta=theta, algo=algo)
         if mqa:
@@ -584,16 +597,18 @@ def run_ours(args):
                          "previous/next step's kernels; double-buffered input slots"}
 
     burst, sustained, hbm, peak_src = measured_peaks()
-    used = "exact" if algo == "exact" else "tensor"
+    used = "exact" if algo == "exact" and not plain else "tensor"
     # our kernels per step: forward: the scaled-key panels and the forward
     # kernel (tensor path) or the exact kernel; backward: delta/lse, then
     # either the exact main kernel or the panels and the dQ and dK
     # tensor-core kernels, then the fp32 dk/dv conversion
-    launches_per_step = (2 if used == "tensor" else 1) * (2 if seq_sharded else 1)
+    launches_per_step = (2 if used == "tensor" and not plain else 1) * (2 if seq_sharded else 1)
     if w["bwd"]:
         launches_per_step += (3 if used == "exact" else 5) * (2 if seq_sharded else 1)
     if w["bwd"]:
         rk_name, rk_ms, rk_flops = f"corope_bwd ({used})", bwd_ms, fl_bwd
+    elif plain:
+        rk_name, rk_ms, rk_flops = "corope_flash_fwd (plain attention)", fwd_ms, fl_fwd
     else:
         rk_name, rk_ms, rk_flops = f"corope_mqa_fwd ({used})" if mqa else f"corope_fwd ({used})", \
             fwd_ms, fl_fwd
@@ -605,6 +620,25 @@ def run_ours(args):
                     "peak_source": f"{peak_src} sustained bf16",
                     "binding_pipe": ROOFLINE_BINDING.get((args.workload, used)),
                     "traffic": NCU_TRAFFIC_BYTES.get((args.workload, used))}
+
+    extra = {}
+    if plain:
+        # the CoRoPE forward on the same inputs and GPU: what the contextual
+        # positions cost over plain attention
+        cf = lambda: co_rope_forward(q, k, v, sm, theta=theta, algo=algo)  # noqa: E731
+        for _ in range(max(1, args.warmup)):
+            cf()
+        torch.cuda.synchronize()
+        c0, c1 = ev(), ev()
+        c0.record(stream)
+        for _ in range(args.steps):
+            cf()
+        c1.record(stream)
+        torch.cuda.synchronize()
+        corope_ms = max_over_ranks(c0.elapsed_time(c1), world) / args.steps
+        extra = {"corope_fwd_ms": corope_ms,
+                 "corope_fwd_tflops": fl_fwd / (corope_ms * 1e-3) / 1e12,
+                 "corope_over_plain": corope_ms / fwd_ms}
 
     cpu = None
     if (rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "bench"
@@ -625,7 +659,7 @@ def run_ours(args):
                                        else f"bxh-shard{world}"),
                        "algo": used, "l2": "inputs exceed L2 (126 MB); no flush",
                        "flop_convention": "FA causal: fwd 4*D*P, bwd 10*D*P"},
-            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, **extra,
             "pct_of_peak": 100 * value / world / sustained,
             # the reference benchmark's own convention (benchmark.py:172-176):
             # fwd 4*D*B*H*S^2 and bwd 6*D*B*H*S^2, not halved for causal

@@ -121,6 +121,8 @@ def load_library():
             lib.corope_bwd_chunk.restype = ctypes.c_int
             lib.corope_bwd_panel_bytes.argtypes = [ctypes.POINTER(BwdParams)]
             lib.corope_bwd_panel_bytes.restype = ctypes.c_size_t
+            lib.corope_flash_fwd.argtypes = [ctypes.POINTER(FwdParams), ctypes.c_void_p]
+            lib.corope_flash_fwd.restype = ctypes.c_int
             for name in ("corope_bwd_chunk_workspace_bytes", "corope_bwd_chunk_min_workspace_bytes"):
                 getattr(lib, name).argtypes = [ctypes.POINTER(BwdParams), chunk_p]
                 getattr(lib, name).restype = ctypes.c_size_t
@@ -242,6 +244,25 @@ def fwd(q, k, v, o, m, l, a, lse, sm_scale, theta, bias=None, algo="auto", theta
     with torch.cuda.device(q.device):
         rc = fn(ctypes.byref(p), ctypes.c_void_p(stream))
     _check(rc, "corope_mqa_fwd" if mqa else "corope_fwd")
+
+
+def flash_fwd(q, k, v, o, m, lse, sm_scale, causal):
+    """Launch corope_flash_fwd (plain softmax attention on the tensor-core
+    pipeline) on the current stream of q."""
+    lib = load_library()
+    B, H, S, D = q.shape
+    p = FwdParams()
+    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+    p.m, p.lse = _ptr(m), _ptr(lse)
+    p.q_stride, p.k_stride, p.v_stride, p.o_stride = (_strides(q), _strides(k), _strides(v),
+                                                      _strides(o))
+    p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, k.shape[1], S, D
+    p.sm_scale = float(sm_scale)
+    p.causal, p.dtype = 1 if causal else 0, _dtype_code(q)
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    with torch.cuda.device(q.device):
+        rc = lib.corope_flash_fwd(ctypes.byref(p), ctypes.c_void_p(stream))
+    _check(rc, "corope_flash_fwd")
 
 
 # Workspace the "auto" backward takes at most, unless one slice group of the

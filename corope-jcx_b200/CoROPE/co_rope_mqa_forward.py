@@ -1,9 +1,11 @@
 """CoRoPE multi-query attention forward -- drop-in for the reference's
 ``CoROPE/co_rope_mqa_forward.py:co_rope_mqa_forward`` (:107-176).
 
-K and V carry one head shared by all query heads of the batch entry; each
-K/V tile is staged once per CTA and reused by the query heads that run
-there.  The reference adds a fresh random bias ``tril(randn(S, S) * 0.02)``
+K and V carry one head shared by all query heads of the batch entry.  Each
+CTA runs 128 query rows of one query head; the CTAs of a head group read the
+same K/V tiles and the same scaled-key operands (written once per call into
+the workspace), which stay resident in L2 across the group.  The reference
+adds a fresh random bias ``tril(randn(S, S) * 0.02)``
 to the logits on every call (co_rope_mqa_forward.py:146, :72-75).  Here the
 bias is an explicit keyword:
 

@@ -22,6 +22,9 @@ bool tc_bwd_supported(const BwdArgs& a, int dtype);
 cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* handoff,
                           size_t handoff_bytes, void* panels);
 size_t tc_bwd_panel_bytes(const BwdArgs& a);
+bool tc_flash_supported(const FwdArgs& a, int dtype);
+cudaError_t tc_flash_launch(const FwdArgs& a, int dtype, bool causal, cudaStream_t st);
+int tcf_take_device_error();
 int64_t tc_bwd_handoff_bytes_per_bh(int S, int r0);
 int tcb_take_device_error();
 cudaError_t bwd_pre_launch(const BwdArgs& a, int dtype, cudaStream_t st);
@@ -396,7 +399,47 @@ const char* corope_last_error(void) { return g_err; }
 int corope_take_device_error(void) {
   const int f = tc_take_device_error();
   const int g = tcb_take_device_error();
-  return f != 0 ? f : g;
+  const int h = tcf_take_device_error();
+  return f != 0 ? f : g != 0 ? g : h;
+}
+
+int corope_flash_fwd(const corope_fwd_params_t* p, corope_stream_t stream) {
+  if (!p) return fail(COROPE_ERR_INVALID, "params is NULL");
+  if (p->batch <= 0 || p->heads <= 0 || p->kv_heads <= 0 || p->seq_len <= 0 || p->head_dim <= 0)
+    return fail(COROPE_ERR_INVALID, "sizes must be positive (B=%d H=%d Hkv=%d S=%d D=%d)",
+                p->batch, p->heads, p->kv_heads, p->seq_len, p->head_dim);
+  if (p->heads % p->kv_heads != 0)
+    return fail(COROPE_ERR_INVALID, "kv_heads (%d) must divide heads (%d)", p->kv_heads,
+                p->heads);
+  if (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16)
+    return fail(p->dtype == COROPE_DTYPE_F32 ? COROPE_ERR_UNSUPPORTED : COROPE_ERR_INVALID,
+                "plain attention takes bf16 or f16 (dtype %d)", p->dtype);
+  if (p->head_dim != 64 && p->head_dim != 128)
+    return fail(COROPE_ERR_UNSUPPORTED, "plain attention head_dim must be 64 or 128 (got %d)",
+                p->head_dim);
+  if (p->causal != 0 && p->causal != 1)
+    return fail(COROPE_ERR_INVALID, "causal must be 0 or 1 (got %d)", p->causal);
+  if (!(p->sm_scale > 0.f)) return fail(COROPE_ERR_INVALID, "sm_scale must be positive");
+  int rc;
+  if ((rc = check_tensor(p->q, p->q_stride, "q", p->dtype))) return rc;
+  if ((rc = check_tensor(p->k, p->k_stride, "k", p->dtype))) return rc;
+  if ((rc = check_tensor(p->v, p->v_stride, "v", p->dtype))) return rc;
+  if ((rc = check_tensor(p->o, p->o_stride, "o", p->dtype))) return rc;
+  if ((rc = check_device())) return rc;
+  FwdArgs a{};
+  a.q = p->q; a.k = p->k; a.v = p->v; a.o = p->o;
+  a.m = p->m; a.lse = p->lse;
+  copy3(a.qs, p->q_stride); copy3(a.ks, p->k_stride); copy3(a.vs, p->v_stride);
+  copy3(a.os, p->o_stride);
+  a.B = p->batch; a.H = p->heads; a.Hkv = p->kv_heads; a.S = p->seq_len; a.D = p->head_dim;
+  a.Sk = p->seq_len;
+  a.sm_scale = p->sm_scale;
+  if (!tc_flash_supported(a, p->dtype))
+    return fail(COROPE_ERR_UNSUPPORTED, "plain attention needs 16-byte aligned rows");
+  const cudaError_t e =
+      tc_flash_launch(a, p->dtype, p->causal != 0, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "plain attention launch");
+  return COROPE_OK;
 }
 
 size_t corope_params_size(int which) {

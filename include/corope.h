@@ -117,8 +117,9 @@ int corope_mqa_fwd(const corope_fwd_params_t *p, corope_stream_t stream);
 
 /* Bytes of workspace corope_bwd uses at its fastest for these parameters:
  * the minimum below plus, for the tensor-core path (head_dim 64 or 128, bf16/f16),
- * a hand-off region of 20,992 bytes per 128 query rows x 16 keys through
- * which the dQ kernel passes its per-(row, key) results to the dK kernel.
+ * the scaled-key panels and a hand-off region of 4,096 bytes per 128 query
+ * rows x 16 keys through which the dQ kernel passes its per-(row, key)
+ * softmax-gradient weights (f16) to the dK kernel.
  * Any size between the two works (smaller hand-off regions are used slice by
  * slice, or not at all). */
 size_t corope_bwd_workspace_bytes(const corope_bwd_params_t *p);
@@ -193,6 +194,19 @@ size_t corope_bwd_chunk_min_workspace_bytes(const corope_bwd_params_t *p,
  * chunk->dk_accum / dv_accum; p->dk and p->dv are not used. */
 int corope_bwd_chunk(const corope_bwd_params_t *p, const corope_chunk_t *chunk,
                      corope_stream_t stream);
+
+/* ---- Plain attention (no contextual positions), the baseline kernel on
+ * the same tensor-core pipeline.  Replaces the launch of
+ * flash_attention_kernel in CoROPE/flash.py:213-290 (kernel :63-202, launch
+ * at :248): O = softmax(sm_scale Q K^T) V, causal (p->causal = 1) or not
+ * (0), and the row max M of the scaled logits (:239, stored when p->m is
+ * set) plus the optional log-sum-exp.  Uses q, k, v, o, m, lse, the strides,
+ * batch, heads, kv_heads (dividing heads), seq_len, head_dim (64 or 128),
+ * sm_scale, causal and dtype (bf16 or f16) of the params; the rest is
+ * ignored.  Keys past seq_len never enter the softmax (the reference counts
+ * the zero-filled keys of its last 64-key block when causal is 0 and seq_len
+ * is not a multiple of 64). */
+int corope_flash_fwd(const corope_fwd_params_t *p, corope_stream_t stream);
 
 /* Message for the last non-zero status returned on this thread. */
 const char *corope_last_error(void);

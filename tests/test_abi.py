@@ -134,6 +134,22 @@ def test_backward_argument_checks(fn, kw, code):
     assert getattr(lib, fn)(None, None) == _lib.ERR_INVALID
 
 
+@pytest.mark.parametrize("kw,code", [
+    (dict(dtype=7), _lib.ERR_INVALID),
+    (dict(dtype=0), _lib.ERR_UNSUPPORTED),
+    (dict(D=32), _lib.ERR_UNSUPPORTED),
+    (dict(causal=2), _lib.ERR_INVALID),
+    (dict(Hkv=3), _lib.ERR_INVALID),
+])
+def test_plain_attention_argument_checks(kw, code):
+    """corope_flash_fwd refuses bad arguments before any device work."""
+    lib = _lib.load_library()
+    p = _fwd_params(**kw)
+    assert lib.corope_flash_fwd(ctypes.byref(p), None) == code
+    assert lib.corope_last_error()
+    assert lib.corope_flash_fwd(None, None) == _lib.ERR_INVALID
+
+
 def test_chunk_argument_checks_without_gpu():
     """corope_fwd_chunk / corope_bwd_chunk refuse a NULL chunk, an offset off
     the 128-row tiles, a key range shorter than the chunk and missing fp32
