@@ -67,7 +67,8 @@ class ChunkParams(ctypes.Structure):
     """corope_chunk_t: a query chunk at sequence position q_row0 against
     kv_len key rows (sequence-sharded callers)."""
     _fields_ = [
-        ("q_row0", ctypes.c_int64), ("kv_len", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("q_row0", ctypes.c_int64), ("kv_len", ctypes.c_int32),
+        ("accum_chunk_rows", ctypes.c_int32),
         ("dk_accum", ctypes.c_void_p), ("dv_accum", ctypes.c_void_p),
     ]
 
@@ -333,7 +334,8 @@ def fit_workspace(full, least, units, budget, panels=0):
 
 
 def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="auto",
-        thetas=None, workspace="auto", q_row0=None, dk_accum=None, dv_accum=None):
+        thetas=None, workspace="auto", q_row0=None, dk_accum=None, dv_accum=None,
+        accum_chunk_rows=0):
     """Launch corope_bwd on the current stream of q with a torch-allocated
     workspace: "auto" (auto_workspace_bytes: the full size up to 4 GiB, else
     as many hand-off slices as fit), "full" (corope_bwd_workspace_bytes, the fastest),
@@ -342,7 +344,9 @@ def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="a
     With ``q_row0`` (corope_bwd_chunk) q, o, do, m, l, a, dq are the query rows
     at sequence positions q_row0.., k, v hold every key row, ``dk``/``dv`` are
     ignored and this chunk's key gradients are added to the contiguous fp32
-    ``dk_accum``/``dv_accum`` [B, Hkv, kv_len, D]."""
+    ``dk_accum``/``dv_accum``: [B, Hkv, kv_len, D], or with
+    ``accum_chunk_rows`` = C the zig-zag owner-major layout
+    [2, N, B, Hkv, C, D] of 2N chunks of C keys (corope_chunk_t)."""
     lib = load_library()
     B, H, S, D = q.shape
     p = BwdParams()
@@ -364,9 +368,10 @@ def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="a
     else:
         for t in (dk_accum, dv_accum):
             assert t is not None and t.dtype == torch.float32 and t.is_contiguous()
-            assert t.shape == k.shape
+            assert t.numel() == k.numel()
         chunk = ChunkParams()
         chunk.q_row0, chunk.kv_len = int(q_row0), k.shape[2]
+        chunk.accum_chunk_rows = int(accum_chunk_rows)
         chunk.dk_accum, chunk.dv_accum = dk_accum.data_ptr(), dv_accum.data_ptr()
     p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, k.shape[1], S, D
     p.sm_scale, p.theta = float(sm_scale), float(theta)

@@ -14,8 +14,11 @@ points of the library (``corope_fwd_chunk`` / ``corope_bwd_chunk``):
   softmax stay inside the kernel, so no per-row state crosses ranks and the
   results equal the whole-sequence call row for row;
 * backward: K and V are all-gathered again, each chunk adds its key gradients
-  to fp32 accumulators covering the whole sequence, and a reduce-scatter (sum)
-  returns to every rank the dk, dv of its own key chunks.
+  to fp32 accumulators covering the whole sequence, laid out owner-major (the
+  chunks each rank owns side by side), and two reduce-scatters (sum) return to
+  every rank the dk, dv of its own key chunks without a reordering copy;
+* both passes run in kv-head groups sized so that the gathered K / V and the
+  accumulators of a group stay under ``GROUP_BUDGET`` bytes.
 
 Tensors are ``[B, H, 2C, D]`` per rank in zig-zag order (``shard_sequence``
 cuts a full tensor the same way); m, l, a are ``[B, H, 2C]``.
@@ -62,12 +65,26 @@ def _all_gather_sequence(x: torch.Tensor, group, world: int) -> torch.Tensor:
     return unshard_sequence(list(out.chunk(world, dim=0)))
 
 
-def _reduce_scatter_sequence(x: torch.Tensor, group, world: int) -> torch.Tensor:
-    """Sum [B, H, S, D] over ranks and return this rank's zig-zag shard."""
-    src = torch.cat([shard_sequence(x, r, world) for r in range(world)], dim=0)
-    out = torch.empty((x.shape[0],) + tuple(src.shape[1:]), dtype=x.dtype, device=x.device)
-    dist.reduce_scatter_tensor(out, src, op=dist.ReduceOp.SUM, group=group)
-    return out
+# Most bytes one kv-head group of the backward may hold at once: its
+# all-gathered K and V plus the fp32 key-gradient accumulators over the whole
+# sequence (the forward holds only K and V).  Larger problems run in kv-head
+# groups, each gathered, computed and reduced before the next.
+GROUP_BUDGET = 4 << 30
+
+
+def _head_groups(hkv: int, per_head_bytes: int, budget: int):
+    """kv-head ranges [h0, h1) whose buffers fit `budget` bytes (at least one
+    head per group).  Every rank derives the same ranges from the same
+    shapes, so all take the same collectives in the same order."""
+    n = max(1, min(hkv, budget // max(1, per_head_bytes)))
+    return [(h0, min(hkv, h0 + n)) for h0 in range(0, hkv, n)]
+
+
+def accum_slot(c: int, world: int) -> tuple:
+    """(half, rank) of sequence chunk c in the owner-major accumulator layout
+    [2, world, B, Hkv, C, D]: chunk r at [0][r], chunk 2 world - 1 - r at
+    [1][r] -- the two chunks rank r owns (corope_chunk_t.accum_chunk_rows)."""
+    return (0, c) if c < world else (1, 2 * world - 1 - c)
 
 
 class _Kernels:
@@ -78,9 +95,11 @@ class _Kernels:
         _lib.fwd(q, k, v, o, m, l, a, None, sm_scale, theta, algo=algo, mqa=True, q_row0=q_row0)
 
     @staticmethod
-    def bwd(q, k, v, o, do, m, l, a, dq, sm_scale, theta, q_row0, dk_acc, dv_acc, algo):
+    def bwd(q, k, v, o, do, m, l, a, dq, sm_scale, theta, q_row0, dk_acc, dv_acc, algo,
+            accum_chunk_rows):
         _lib.bwd(q, k, v, o, do, m, l, a, dq, None, None, sm_scale, theta, algo=algo,
-                 q_row0=q_row0, dk_accum=dk_acc, dv_accum=dv_acc)
+                 q_row0=q_row0, dk_accum=dk_acc, dv_accum=dv_acc,
+                 accum_chunk_rows=accum_chunk_rows)
 
 
 def _layout(q, k, world):
@@ -93,7 +112,7 @@ def _layout(q, k, world):
 
 
 def co_rope_forward_cp(q, k, v, sm_scale=None, causal=True, theta=10000.0, group=None,
-                       algo="auto", kernels=None):
+                       algo="auto", kernels=None, budget=None):
     """Forward of this rank's zig-zag shard.  Returns
     ``((q, k, v, o, m, l, a), o)`` like ``co_rope_forward``, for the shard."""
     if not causal:
@@ -101,42 +120,66 @@ def co_rope_forward_cp(q, k, v, sm_scale=None, causal=True, theta=10000.0, group
     kern = kernels or _Kernels
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     B, H, C, D = _layout(q, k, world)
+    hkv = k.shape[1]
+    g = H // hkv
     sm_scale = _lib.default_scale(D, sm_scale)
-    k_all = _all_gather_sequence(k, group, world)
-    v_all = _all_gather_sequence(v, group, world)
     o = torch.empty_like(q)
-    state = []
-    for i, c in enumerate(zigzag_chunks(rank, world)):
-        rows = slice(i * C, (i + 1) * C)
-        m, l, a = (torch.empty(B, H, C, dtype=torch.float32, device=q.device) for _ in range(3))
-        kern.fwd(q[:, :, rows], k_all, v_all, o[:, :, rows], m, l, a, sm_scale, theta, c * C,
-                 algo)
-        state.append((m, l, a))
-    m, l, a = (torch.cat([s[j] for s in state], dim=2) for j in range(3))
+    m, l, a = (torch.empty(B, H, 2 * C, dtype=torch.float32, device=q.device) for _ in range(3))
+    per_head = 2 * B * (2 * world * C) * D * k.element_size()
+    for h0, h1 in _head_groups(hkv, per_head, budget or GROUP_BUDGET):
+        hs = slice(h0 * g, h1 * g)
+        k_all = _all_gather_sequence(k[:, h0:h1], group, world)
+        v_all = _all_gather_sequence(v[:, h0:h1], group, world)
+        for i, c in enumerate(zigzag_chunks(rank, world)):
+            rows = slice(i * C, (i + 1) * C)
+            mi, li, ai = (torch.empty(B, (h1 - h0) * g, C, dtype=torch.float32, device=q.device)
+                          for _ in range(3))
+            kern.fwd(q[:, hs, rows], k_all, v_all, o[:, hs, rows], mi, li, ai, sm_scale, theta,
+                     c * C, algo)
+            m[:, hs, rows], l[:, hs, rows], a[:, hs, rows] = mi, li, ai
+        del k_all, v_all
     return (q, k, v, o, m, l, a), o
 
 
 def co_rope_backward_cp(saved, do, sm_scale=None, theta=10000.0, group=None, algo="auto",
-                        kernels=None):
+                        kernels=None, budget=None):
     """Backward of this rank's shard: (dq, dk, dv) of the shard's rows and
-    key chunks (dk, dv summed over every rank's queries)."""
+    key chunks (dk, dv summed over every rank's queries).  Per kv-head group:
+    K and V all-gathered, every local query chunk adds its key gradients to
+    fp32 accumulators over the whole sequence in the owner-major layout, and
+    one reduce-scatter per half of that layout hands each rank the sums of its
+    own two chunks -- no reordering copy of the accumulators."""
     kern = kernels or _Kernels
     q, k, v, o, m, l, a = saved
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     B, H, C, D = _layout(q, k, world)
+    hkv = k.shape[1]
+    g = H // hkv
     sm_scale = _lib.default_scale(D, sm_scale)
-    k_all = _all_gather_sequence(k, group, world)
-    v_all = _all_gather_sequence(v, group, world)
-    dk_acc = torch.zeros(k_all.shape, dtype=torch.float32, device=q.device)
-    dv_acc = torch.zeros_like(dk_acc)
     dq = torch.empty_like(q)
-    for i, c in enumerate(zigzag_chunks(rank, world)):
-        rows = slice(i * C, (i + 1) * C)
-        mi, li, ai = (x[:, :, rows].contiguous() for x in (m, l, a))
-        kern.bwd(q[:, :, rows], k_all, v_all, o[:, :, rows], do[:, :, rows], mi, li, ai,
-                 dq[:, :, rows], sm_scale, theta, c * C, dk_acc, dv_acc, algo)
-    dk = _reduce_scatter_sequence(dk_acc, group, world).to(k.dtype)
-    dv = _reduce_scatter_sequence(dv_acc, group, world).to(v.dtype)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    S = 2 * world * C
+    per_head = B * S * D * (2 * k.element_size() + 2 * 4)
+    for h0, h1 in _head_groups(hkv, per_head, budget or GROUP_BUDGET):
+        hs, n = slice(h0 * g, h1 * g), h1 - h0
+        k_all = _all_gather_sequence(k[:, h0:h1], group, world)
+        v_all = _all_gather_sequence(v[:, h0:h1], group, world)
+        dk_acc = torch.zeros(2, world, B, n, C, D, dtype=torch.float32, device=q.device)
+        dv_acc = torch.zeros_like(dk_acc)
+        for i, c in enumerate(zigzag_chunks(rank, world)):
+            rows = slice(i * C, (i + 1) * C)
+            mi, li, ai = (x[:, hs, rows].contiguous() for x in (m, l, a))
+            kern.bwd(q[:, hs, rows], k_all, v_all, o[:, hs, rows], do[:, hs, rows], mi, li, ai,
+                     dq[:, hs, rows], sm_scale, theta, c * C, dk_acc, dv_acc, algo, C)
+        del k_all, v_all
+        for acc, out in ((dk_acc, dk), (dv_acc, dv)):
+            for half in range(2):  # the rank's first and second chunk
+                mine = torch.empty(B, n, C, D, dtype=torch.float32, device=q.device)
+                src = acc[half].view(world * B, n, C, D)  # ranks along dim 0, no copy
+                dist.reduce_scatter_tensor(mine, src, op=dist.ReduceOp.SUM, group=group)
+                out[:, h0:h1, half * C:(half + 1) * C] = mine.to(out.dtype)
+        del dk_acc, dv_acc
     return dq, dk, dv
 
 

@@ -132,8 +132,21 @@ struct BwdArgs {
   // workspace views
   float* delta;  // [B,H,S]  rowsum(dO * O)
   float* lse;    // [B,H,S]  m + log(l)
-  float* dk32;   // [B,Hkv,Sk,D] fp32 accumulators
-  float* dv32;   // [B,Hkv,Sk,D]
+  float* dk32;   // [B,Hkv,Sk,D] fp32 accumulators (or the owner-major chunk
+  float* dv32;   // layout, acc_chunk > 0: see accum_row)
+  int acc_chunk; // 0, or the chunk rows C of the owner-major layout
 };
+
+// Row (in units of D elements) of key `key` of (b, kv head) `bhk` in the fp32
+// dk / dv accumulators: [B*Hkv][Sk] rows, or, with C = acc_chunk > 0, the
+// zig-zag owner-major layout [2][N][B*Hkv][C] of a sequence of 2N chunks of C
+// rows (Sk = 2 N C): chunk c < N at [0][c], chunk c >= N at [1][2N-1-c].
+__device__ __forceinline__ int64_t accum_row(int key, int bhk, int BHkv, int Sk, int C) {
+  if (C == 0) return (int64_t)bhk * Sk + key;
+  const int n = Sk / (2 * C);  // ranks
+  const int c = key / C;
+  const int pos = c < n ? c : 3 * n - 1 - c;
+  return ((int64_t)pos * BHkv + bhk) * C + (key - c * C);
+}
 
 }  // namespace corope

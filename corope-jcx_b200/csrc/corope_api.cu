@@ -122,6 +122,11 @@ static int check_chunk(const corope_chunk_t* c, int seq_len) {
   if (c->q_row0 + seq_len > (int64_t)c->kv_len || c->q_row0 + seq_len > INT32_MAX)
     return fail(COROPE_ERR_INVALID, "kv_len (%d) must cover q_row0 + seq_len (%lld)", c->kv_len,
                 (long long)(c->q_row0 + seq_len));
+  if (c->accum_chunk_rows < 0 ||
+      (c->accum_chunk_rows > 0 && c->kv_len % (2 * c->accum_chunk_rows) != 0))
+    return fail(COROPE_ERR_INVALID,
+                "accum_chunk_rows (%d) must be 0 or divide kv_len (%d) into an even number of "
+                "chunks", c->accum_chunk_rows, c->kv_len);
   return COROPE_OK;
 }
 
@@ -358,6 +363,7 @@ static int bwd_common(const corope_bwd_params_t* p, corope_stream_t stream,
   if (chunk) {
     a.dk32 = chunk->dk_accum;
     a.dv32 = chunk->dv_accum;
+    a.acc_chunk = chunk->accum_chunk_rows;
   } else {
     a.dk32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4));
     a.dv32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4) + align256(kv * 4));

@@ -265,8 +265,8 @@ exact_bwd_kernel(BwdArgs args) {
 
   // phase-2 mapping
   const int kj = threadIdx.x / TPK, sub2 = threadIdx.x % TPK;
-  float* dk32 = args.dk32 + ((int64_t)b * args.Hkv + hk) * args.Sk * D;
-  float* dv32 = args.dv32 + ((int64_t)b * args.Hkv + hk) * args.Sk * D;
+  const int bhk = b * args.Hkv + hk;
+  const int BHkv = args.B * args.Hkv;
 
   const int last_row = args.r0 + min(S - 1, q0 + kBM - 1);  // sequence position
   for (int j0 = 0; j0 <= last_row; j0 += kBN) {
@@ -368,10 +368,11 @@ exact_bwd_kernel(BwdArgs args) {
         for (int i = 0; i < NP2; ++i) {
           const int p = i * TPK + sub2;
           if (p < P) {
-            atomicAdd(dk32 + (int64_t)j * D + 2 * p, dkp[i].x);
-            atomicAdd(dk32 + (int64_t)j * D + 2 * p + 1, dkp[i].y);
-            atomicAdd(dv32 + (int64_t)j * D + 2 * p, dvp[i].x);
-            atomicAdd(dv32 + (int64_t)j * D + 2 * p + 1, dvp[i].y);
+            const int64_t row = accum_row(j, bhk, BHkv, args.Sk, args.acc_chunk) * D;
+            atomicAdd(args.dk32 + row + 2 * p, dkp[i].x);
+            atomicAdd(args.dk32 + row + 2 * p + 1, dkp[i].y);
+            atomicAdd(args.dv32 + row + 2 * p, dvp[i].x);
+            atomicAdd(args.dv32 + row + 2 * p + 1, dvp[i].y);
           }
         }
       }

@@ -101,7 +101,8 @@ struct Params {
   int km_nhw;            // half windows per (b, kv head) in the panels
   int km_rows[2];        // panel rows per slab
   void* dq;              // dQ launch output, element type of q
-  float *dk32, *dv32;    // dK launch accumulators [B, Hkv, Sk, D]
+  float *dk32, *dv32;    // accumulators [B, Hkv, Sk, D] (or the owner-major chunk layout)
+  int acc_chunk;         // 0, or the chunk rows of the owner-major layout (accum_row)
   const float *lse, *delta, *a;  // [B, H, S]
   const float* thetas;
   const float* bias;
@@ -632,8 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       }
     }
     const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
-    float* dk32 = P.dk32 + ((int64_t)b * P.Hkv + hk) * P.Sk * D;
-    float* dv32 = P.dv32 + ((int64_t)b * P.Hkv + hk) * P.Sk * D;
+    const int bhk = b * P.Hkv + hk, BHkv = P.B * P.Hkv;
 
     auto build = [&](int w) -> bool {
       const int buf = w % nb, use = w / nb;
@@ -720,7 +720,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = w * kW + j;
-        if (key < P.Sk && d < D) atomicAdd(dk32 + (int64_t)key * D + d, dk[j]);
+        if (key < P.Sk && d < D)
+          atomicAdd(P.dk32 + accum_row(key, bhk, BHkv, P.Sk, P.acc_chunk) * D + d, dk[j]);
       }
       return true;
     };
@@ -741,8 +742,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       for (int j = 0; j < 16; ++j) {
         const int key = w * kW + j;
         if (key < P.Sk && d < D) {
-          atomicAdd(dv32 + (int64_t)key * D + d, __uint_as_float(g[0][j]));
-          atomicAdd(dk32 + (int64_t)key * D + d, __uint_as_float(g[1][j]));
+          const int64_t row = accum_row(key, bhk, BHkv, P.Sk, P.acc_chunk) * D;
+          atomicAdd(P.dv32 + row + d, __uint_as_float(g[0][j]));
+          atomicAdd(P.dk32 + row + d, __uint_as_float(g[1][j]));
         }
       }
       return true;
@@ -1347,7 +1349,7 @@ __global__ void __launch_bounds__(kThreads, 1) dk3_kernel(const __grid_constant_
       }
     }
     const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
-    float* dk32 = P.dk32 + ((int64_t)b * P.Hkv + hk) * P.Sk * D + gt;
+    const int bhk = b * P.Hkv + hk, BHkv = P.B * P.Hkv;
     for (int w = 0; w <= WL; ++w) {
       const int bf = w & 1;
       if (!wwait(bars[k3::B_CF + bf], (w >> 1) & 1, err, kErrC)) break;
@@ -1393,7 +1395,8 @@ __global__ void __launch_bounds__(kThreads, 1) dk3_kernel(const __grid_constant_
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = w * kW + j;
-        if (key < P.Sk && gt < D) atomicAdd(dk32 + (int64_t)key * D, dk[j]);
+        if (key < P.Sk && gt < D)
+          atomicAdd(P.dk32 + accum_row(key, bhk, BHkv, P.Sk, P.acc_chunk) * D + gt, dk[j]);
       }
     }
     __syncwarp();
@@ -1713,6 +1716,7 @@ cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* ha
   p.dq = a.dq;
   p.dk32 = a.dk32;
   p.dv32 = a.dv32;
+  p.acc_chunk = a.acc_chunk;
   p.lse = a.lse;
   p.delta = a.delta;
   p.a = a.a;

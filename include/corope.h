@@ -171,8 +171,14 @@ size_t corope_bwd_noalloc_scratch_bytes(void);
 typedef struct {
   int64_t q_row0;      /* sequence position of row 0 of q; a multiple of 128 */
   int32_t kv_len;      /* rows of k and v; at least q_row0 + seq_len */
-  int32_t reserved;    /* 0 */
-  float *dk_accum;     /* backward: fp32 [B, kv_heads, kv_len, D], contiguous;
+  int32_t accum_chunk_rows; /* layout of dk_accum / dv_accum: 0 = [B, kv_heads,
+                          kv_len, D]; C > 0 = the zig-zag owner-major layout of a
+                          sequence cut into 2N chunks of C rows (kv_len = 2 N C):
+                          [2][N][B][kv_heads][C][D], where [0][r] holds chunk r
+                          and [1][r] chunk 2N-1-r, the two chunks rank r owns, so
+                          that a reduce-scatter of each half hands every rank its
+                          keys' sums with no reordering copy */
+  float *dk_accum;     /* backward: fp32, contiguous in the layout above;
                           the call ADDS this chunk's dk (zero it once first) */
   float *dv_accum;     /* backward: the same for dv */
 } corope_chunk_t;
@@ -224,7 +230,7 @@ size_t corope_params_size(int which);
 /* ABI version of this header (COROPE_ABI_VERSION). */
 int corope_abi_version(void);
 
-#define COROPE_ABI_VERSION 3
+#define COROPE_ABI_VERSION 4
 
 #ifdef __cplusplus
 }

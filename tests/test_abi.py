@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_struct_layout():
     lib = _lib.load_library()
-    assert lib.corope_abi_version() == 3
+    assert lib.corope_abi_version() == 4
     assert lib.corope_params_size(0) == ctypes.sizeof(_lib.FwdParams)
     assert lib.corope_params_size(1) == ctypes.sizeof(_lib.BwdParams)
 

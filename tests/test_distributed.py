@@ -85,10 +85,14 @@ class _OracleChunks:
                 o[b, h], m[b, h], l[b, h], a[b, h] = ro.to(o.dtype), rm, rl, ra
 
     @staticmethod
-    def bwd(q, k, v, o, do, m, l, a, dq, sm, theta, q_row0, dk_acc, dv_acc, algo):
+    def bwd(q, k, v, o, do, m, l, a, dq, sm, theta, q_row0, dk_acc, dv_acc, algo,
+            accum_chunk_rows):
         from oracle import corope_oracle as O
+        from CoROPE.context_parallel import accum_slot
         B, H, n, _ = q.shape
         g, S = H // k.shape[1], k.shape[2]
+        C = accum_chunk_rows
+        world = S // (2 * C)
         rows = torch.arange(q_row0, q_row0 + n)
         for b in range(B):
             for h in range(H):
@@ -97,8 +101,11 @@ class _OracleChunks:
                                              _OracleChunks._full(do[b, h], rows, S), rows, sm,
                                              theta)
                 dq[b, h] = rq.to(dq.dtype)
-                dk_acc[b, h // g] += rk.float()
-                dv_acc[b, h // g] += rv.float()
+                # the owner-major layout [2, world, B, Hkv, C, D]
+                for c in range(2 * world):
+                    half, r = accum_slot(c, world)
+                    dk_acc[half, r, b, h // g] += rk[c * C:(c + 1) * C].float()
+                    dv_acc[half, r, b, h // g] += rv[c * C:(c + 1) * C].float()
 
 
 def _cp_worker(rank, world, port, out):
@@ -110,16 +117,20 @@ def _cp_worker(rank, world, port, out):
     try:
         from oracle import corope_oracle as O
         from CoROPE import context_parallel as cp
-        B, H, Hkv, S, D, sm, theta = 1, 2, 1, 2 * world * 128, 8, 0.3, 500.0
+        B, H, Hkv, S, D, sm, theta = 1, 4, 2, 2 * world * 128, 8, 0.3, 500.0
         g = torch.Generator().manual_seed(11)
         q = torch.randn(B, H, S, D, generator=g, dtype=torch.float64)
         k = torch.randn(B, Hkv, S, D, generator=g, dtype=torch.float64)
         v = torch.randn(B, Hkv, S, D, generator=g, dtype=torch.float64)
         do = torch.randn(B, H, S, D, generator=g, dtype=torch.float64)
         mine = [cp.shard_sequence(x, rank, world) for x in (q, k, v, do)]
-        saved, o = cp.co_rope_forward_cp(*mine[:3], sm, theta=theta, kernels=_OracleChunks)
+        # a budget of one kv head: two kv-head groups in each pass
+        one = B * S * D * (2 * 8 + 2 * 4)
+        saved, o = cp.co_rope_forward_cp(*mine[:3], sm, theta=theta, kernels=_OracleChunks,
+                                         budget=one)
         dq, dk, dv = cp.co_rope_backward_cp(saved, mine[3], sm, theta=theta,
-                                            kernels=_OracleChunks)
+                                            kernels=_OracleChunks, budget=one)
+        out["groups"] = len(cp._head_groups(Hkv, B * S * D * (2 * 8 + 2 * 4), one))
         parts = {}
         for name, x in (("o", o), ("a", saved[6]), ("dq", dq), ("dk", dk), ("dv", dv)):
             got = [torch.empty_like(x) for _ in range(world)]
@@ -143,8 +154,9 @@ def _cp_worker(rank, world, port, out):
 
 def test_sequence_sharded_forward_backward_gloo():
     """Zig-zag sequence sharding over 2 ranks (gloo): K/V all-gather, per-rank
-    query chunks, dk/dv reduce-scatter -- with the oracle standing in for the
-    chunk kernels -- reproduces the whole-sequence forward and gradients."""
+    query chunks, owner-major dk/dv accumulators and their reduce-scatter, in
+    two kv-head groups -- with the oracle standing in for the chunk kernels --
+    reproduces the whole-sequence forward and gradients."""
     world = 2
     port = _free_port()
     ctx = mp.get_context("spawn")
@@ -156,6 +168,6 @@ def test_sequence_sharded_forward_backward_gloo():
         for p in procs:
             p.join(timeout=300)
         assert all(p.exitcode == 0 for p in procs)
-        assert out["roundtrip"]
+        assert out["roundtrip"] and out["groups"] == 2
         assert out["o"] < 1e-12 and out["a"] < 1e-6 and out["dq"] < 1e-12
         assert out["dk"] < 1e-6 and out["dv"] < 1e-6
