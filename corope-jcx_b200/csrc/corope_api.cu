@@ -122,11 +122,11 @@ static int check_chunk(const corope_chunk_t* c, int seq_len) {
   if (c->q_row0 + seq_len > (int64_t)c->kv_len || c->q_row0 + seq_len > INT32_MAX)
     return fail(COROPE_ERR_INVALID, "kv_len (%d) must cover q_row0 + seq_len (%lld)", c->kv_len,
                 (long long)(c->q_row0 + seq_len));
-  if (c->accum_chunk_rows < 0 ||
+  if (c->accum_chunk_rows < 0 || c->accum_chunk_rows % 16 != 0 ||
       (c->accum_chunk_rows > 0 && c->kv_len % (2 * c->accum_chunk_rows) != 0))
     return fail(COROPE_ERR_INVALID,
-                "accum_chunk_rows (%d) must be 0 or divide kv_len (%d) into an even number of "
-                "chunks", c->accum_chunk_rows, c->kv_len);
+                "accum_chunk_rows (%d) must be 0 or a multiple of 16 dividing kv_len (%d) into "
+                "an even number of chunks", c->accum_chunk_rows, c->kv_len);
   return COROPE_OK;
 }
 

@@ -364,11 +364,11 @@ exact_bwd_kernel(BwdArgs args) {
         }
       }
       if (j < args.Sk) {
+        const int64_t row = accum_row(j, bhk, BHkv, args.Sk, args.acc_chunk) * D;
 #pragma unroll
         for (int i = 0; i < NP2; ++i) {
           const int p = i * TPK + sub2;
           if (p < P) {
-            const int64_t row = accum_row(j, bhk, BHkv, args.Sk, args.acc_chunk) * D;
             atomicAdd(args.dk32 + row + 2 * p, dkp[i].x);
             atomicAdd(args.dk32 + row + 2 * p + 1, dkp[i].y);
             atomicAdd(args.dv32 + row + 2 * p, dvp[i].x);

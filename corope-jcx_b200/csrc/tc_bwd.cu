@@ -717,12 +717,11 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         mbar_arrive(&bars[B_CE + hh]);
       }
       const int d = gt;
+      // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys)
+      float* row0 = P.dk32 + accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + d;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int key = w * kW + j;
-        if (key < P.Sk && d < D)
-          atomicAdd(P.dk32 + accum_row(key, bhk, BHkv, P.Sk, P.acc_chunk) * D + d, dk[j]);
-      }
+      for (int j = 0; j < 16; ++j)
+        if (w * kW + j < P.Sk && d < D) atomicAdd(row0 + j * D, dk[j]);
       return true;
     };
 
@@ -738,13 +737,13 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       tc_fence_before();
       mbar_arrive(&bars[B_CE2]);
       const int d = gt;
+      // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys)
+      const int64_t row0 = accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + d;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int key = w * kW + j;
-        if (key < P.Sk && d < D) {
-          const int64_t row = accum_row(key, bhk, BHkv, P.Sk, P.acc_chunk) * D;
-          atomicAdd(P.dv32 + row + d, __uint_as_float(g[0][j]));
-          atomicAdd(P.dk32 + row + d, __uint_as_float(g[1][j]));
+        if (w * kW + j < P.Sk && d < D) {
+          atomicAdd(P.dv32 + row0 + j * D, __uint_as_float(g[0][j]));
+          atomicAdd(P.dk32 + row0 + j * D, __uint_as_float(g[1][j]));
         }
       }
       return true;
@@ -899,23 +898,35 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&bars[B_GE]);
-      float b1[4], b2[4], d1[4], d2[4];
+      // two keys per packed fp32x2 FMA.  Value: b_m = 2u b_{m+1} + (G_m -
+      // b_{m+2}); derivative tracked halved, e = d / 2:
+      // e_m = 2u e_{m+1} + (b_{m+1} - e_{m+2}) -- two FMAs per step each
+      const float2 neg1 = make_float2(-1.f, -1.f), neg2 = make_float2(-2.f, -2.f);
+      const float2 u2[2] = {make_float2(2.f * uj[0], 2.f * uj[1]), make_float2(2.f * uj[2], 2.f * uj[3])};
+      const float2 u1[2] = {make_float2(uj[0], uj[1]), make_float2(uj[2], uj[3])};
+      float2 b1[2], b2[2], e1[2], e2[2];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) { b1[j] = b2[j] = d1[j] = d2[j] = 0.f; }
+      for (int j = 0; j < 2; ++j) {
+        b1[j] = b2[j] = e1[j] = e2[j] = make_float2(0.f, 0.f);
+      }
 #pragma unroll
       for (int m = kM - 1; m >= 0; --m) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float a = __uint_as_float(g[m >> 1][m & 1][j]);
-          const float u2 = 2.0f * uj[j];
+        for (int j = 0; j < 2; ++j) {
+          const float2 a = make_float2(__uint_as_float(g[m >> 1][m & 1][2 * j]),
+                                       __uint_as_float(g[m >> 1][m & 1][2 * j + 1]));
+          const float2 t = __ffma2_rn(neg1, b2[j], a);
           if (m > 0) {
-            const float dn = fmaf(u2, d1[j], fmaf(2.0f, b1[j], -d2[j]));
-            const float bn = fmaf(u2, b1[j], a - b2[j]);
-            d2[j] = d1[j]; d1[j] = dn;
+            const float2 en = __ffma2_rn(u2[j], e1[j], __ffma2_rn(neg1, e2[j], b1[j]));
+            const float2 bn = __ffma2_rn(u2[j], b1[j], t);
+            e2[j] = e1[j]; e1[j] = en;
             b2[j] = b1[j]; b1[j] = bn;
           } else {
-            f[j] = fmaf(uj[j], b1[j], a - b2[j]);
-            fd[j] = fmaf(uj[j], d1[j], b1[j] - d2[j]);
+            const float2 r = __ffma2_rn(u1[j], b1[j], t);
+            // l' = u d_1 + b_1 - d_2 = 2 u e_1 + (b_1 - 2 e_2)
+            const float2 rd = __ffma2_rn(u2[j], e1[j], __ffma2_rn(neg2, e2[j], b1[j]));
+            f[2 * j] = r.x; f[2 * j + 1] = r.y;
+            fd[2 * j] = rd.x; fd[2 * j + 1] = rd.y;
           }
         }
       }
@@ -1392,12 +1403,11 @@ __global__ void __launch_bounds__(kThreads, 1) dk3_kernel(const __grid_constant_
       }
       tc_fence_before();
       mbar_arrive(&bars[k3::B_CE + bf]);
+      // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys)
+      float* row0 = P.dk32 + accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + gt;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int key = w * kW + j;
-        if (key < P.Sk && gt < D)
-          atomicAdd(P.dk32 + accum_row(key, bhk, BHkv, P.Sk, P.acc_chunk) * D + gt, dk[j]);
-      }
+      for (int j = 0; j < 16; ++j)
+        if (w * kW + j < P.Sk && gt < D) atomicAdd(row0 + j * D, dk[j]);
     }
     __syncwarp();
     regs_inc<128>();

@@ -173,7 +173,8 @@ typedef struct {
   int32_t kv_len;      /* rows of k and v; at least q_row0 + seq_len */
   int32_t accum_chunk_rows; /* layout of dk_accum / dv_accum: 0 = [B, kv_heads,
                           kv_len, D]; C > 0 = the zig-zag owner-major layout of a
-                          sequence cut into 2N chunks of C rows (kv_len = 2 N C):
+                          sequence cut into 2N chunks of C rows (C a multiple
+                          of 16, kv_len = 2 N C):
                           [2][N][B][kv_heads][C][D], where [0][r] holds chunk r
                           and [1][r] chunk 2N-1-r, the two chunks rank r owns, so
                           that a reduce-scatter of each half hands every rank its
