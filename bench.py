@@ -60,20 +60,17 @@ UNIT = "TFLOP/s"
 CPU_SAMPLE_ROWS = 48
 
 # DRAM traffic of one backward call (dram__bytes_read.sum + dram__bytes_write.sum
-# summed over its kernels) from ncu captures of B=1,H=8,S=2048,D=128, scaled to
-# this workload.  Exact kernel: by query rows x heads (x32),
-# profiles/exact_bwd_b1h8s2048d128.md.  Tensor-core kernels: dominated by the
-# dQ -> dK hand-off and the dQ kernel's panel reads, 411.9 MB over 8 x 1088
-# (b, h, query tile, window) blocks, i.e. 47.3 KB per block, times the
-# 128 x 4224 blocks of this workload;
-# profiles/tc_bwd_b1h8s2048d128.md.
+# summed over its kernels).  Exact kernel: an ncu capture of B=1,H=8,S=2048,D=128
+# scaled by query rows x heads (x32).  Tensor-core kernels: a capture of half the
+# bench workload (B=2,H=32,S=4096,D=128: pre 0.14 GB, panels 0.67 GB, dQ kernel
+# 2.62 GB, dK kernel 1.50 GB, conversion 0.37 GB), twice that here.
 NCU_TRAFFIC_BYTES = {("bench", "exact"): 33.78e6 * 32,
-                     ("bench", "tensor"): 411.9e6 / (8 * 1088) * (128 * 4224)}
-# The pipe that binds the dominant kernel (ncu, small case of the same kernel):
-# issue slots of the CUDA-core work around the tensor-core GEMMs
+                     ("bench", "tensor"): 2 * 5.3015e9}
+# The pipe that binds the dominant kernel (ncu, B=1,H=8,S=2048,D=128 of the same
+# kernel): instruction issue of the CUDA-core work around the tensor-core GEMMs
 ROOFLINE_BINDING = {("bench", "tensor"): {"resource": "instruction issue",
-                                          "issue_active_pct": 59.3, "tensor_pipe_pct": 13.0,
-                                          "kernel": "dQ kernel (50% of the step)"}}
+                                          "issue_active_pct": 53.2, "tensor_pipe_pct": 14.9,
+                                          "kernel": "dQ kernel (52% of the step)"}}
 
 
 def causal_pairs(B, H, S):

@@ -282,20 +282,21 @@ def _alloc_workspace(nbytes, least, device):
         return torch.empty(least, dtype=torch.uint8, device=device), least
 
 
-def min_slices(units, seq_len):
-    """Fewest (b, h) slices the library runs per hand-off launch pair: 16, or
-    fewer when they already make 512 CTAs of 128 query rows, or all units."""
+def floor_slices(units, seq_len, ctas=1024):
+    """(b, h) slices whose hand-off launches make at least ``ctas`` CTAs of 128
+    query rows (about 7 waves of 148 SMs), or all units."""
     qtiles = (seq_len + 127) // 128
-    return min(units, 16, (512 + qtiles - 1) // qtiles)
+    return min(units, (ctas + qtiles - 1) // qtiles)
 
 
 def auto_workspace_bytes(lib, p, device, chunk=None):
     """The workspace "auto" gives corope_bwd: the full size when it fits in
     AUTO_WORKSPACE_BUDGET (4 GiB), else the minimum plus the scaled-key
     panels plus as many whole (b, h) hand-off slices as fit there -- but never
-    fewer than one slice group of the library's hand-off launches (long
-    sequences: 2 slices of 1.1 GB at S=32768), since below that the dK kernel
-    recomputes the per-pair work instead.  The budget is fixed, not a share of
+    fewer than make launches of 1024 CTAs (long sequences: 4 slices of 1.1 GB
+    at S=32768, 8.1 GB in all, within 3% of the whole 38 GB region's speed;
+    below that the launch tails cost more, and without a hand-off the dK
+    kernel recomputes the per-pair work).  The budget is fixed, not a share of
     free memory: asking the driver for free memory would cost a round trip on
     every backward, and a fixed request lets torch's cache serve it again."""
     if chunk is None:
@@ -312,7 +313,7 @@ def auto_workspace_bytes(lib, p, device, chunk=None):
     budget = AUTO_WORKSPACE_BUDGET
     if full > budget and full > least + panels:
         per = (full - least - panels) // units
-        budget = max(budget, least + panels + min_slices(units, p.seq_len) * per)
+        budget = max(budget, least + panels + floor_slices(units, p.seq_len) * per)
     return fit_workspace(full, least, units, budget, panels)
 
 

@@ -91,3 +91,30 @@ def test_auto_workspace_fits_whole_slices():
         least + panels + 2 * per
     assert fit_workspace(full, least, units, least + panels + 10, panels) == least + panels
     assert fit_workspace(full, least, units, least + panels - 1, panels) == least
+
+
+def test_auto_workspace_policy_without_gpu():
+    """The "auto" backward workspace: the whole hand-off region at the bench
+    shape (B=4, H=32, S=4096, D=128 bf16: under 4 GiB), and for one GPU's
+    share of the long-context shape (B=1, H=32, S=32768) the minimum, the
+    panels and the 4 whole hand-off slices that make 1024-CTA launches."""
+    import ctypes
+    from CoROPE import _lib
+    lib = _lib.load_library()
+
+    def params(B, H, S, D, theta):
+        p = _lib.BwdParams()
+        p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, H, S, D
+        p.dtype, p.algo, p.theta, p.sm_scale = _lib.DTYPE_BF16, _lib.ALGO_AUTO, theta, D ** -0.5
+        return p
+
+    p = params(4, 32, 4096, 128, 1e4)
+    full = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
+    assert _lib.auto_workspace_bytes(lib, p, "cuda:0") == full <= _lib.AUTO_WORKSPACE_BUDGET
+    p = params(1, 32, 32768, 128, 5e5)
+    full = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
+    least = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
+    panels = lib.corope_bwd_panel_bytes(ctypes.byref(p))
+    per = (full - least - panels) // 32
+    assert _lib.floor_slices(32, 32768) == 4
+    assert _lib.auto_workspace_bytes(lib, p, "cuda:0") == least + panels + 4 * per
