@@ -165,10 +165,11 @@ template <int KM> struct TK {  // recompute dK launch
 // rebuild Y_m = dl T_m(u).  Quad q = 2 * half + row group holds keys
 // 8 half + 4 group + 0..3, 8 bytes per row.
 constexpr int kHB = 4 * 128 * 8;
-// dl -> f16 pair, saturated at the largest finite f16
+// dl -> f16 pair, saturated at the largest finite f16 (NaN stays NaN)
 __device__ __forceinline__ uint32_t pack_dl(float a, float b) {
-  constexpr float kMax = 65504.f;
-  return sm100::pack_f16(fminf(fmaxf(a, -kMax), kMax), fminf(fmaxf(b, -kMax), kMax));
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
 }
 __device__ __forceinline__ float2 unpack_dl(uint32_t v) {
   return __half22float2(*reinterpret_cast<const __half2*>(&v));
@@ -780,7 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     float da_run = 0.f;  // gate-gradient prefix before the current half
     // this group's keys of the window: i -> key 8 (i >> 2) + 4 rg + (i & 3)
     float zo[8], uo[8], dpo[8];
-    uint32_t csc[PW];    // dQ: ln2 (cos, sin) as f16 pairs for this group's pairs
+    uint32_t csc[PW];    // dQ: (cos, sin) as f16 pairs for this group's pairs
     bool ok = wwait(bars[B_Q], 0, err, kErrQ);
 
     // gates and positions of window w; reads the gate scores and dP
@@ -856,12 +857,12 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             const int c = rg * (PW / 4) + 4 * g + cc;
             sts128(sAV + (c >> 3) * 16384 + sw128_offset(r, c & 7),
                    make_uint4(o[4 * cc], o[4 * cc + 1], o[4 * cc + 2], o[4 * cc + 3]));
-            // staged for the dQ update, already scaled by ln 2
+            // staged for the dQ update
             sts128(s_cs + (4 * g + cc) * 4096,
-                   make_uint4(pack_cs(kLn2 * cs[4 * cc], kLn2 * sn[4 * cc]),
-                              pack_cs(kLn2 * cs[4 * cc + 1], kLn2 * sn[4 * cc + 1]),
-                              pack_cs(kLn2 * cs[4 * cc + 2], kLn2 * sn[4 * cc + 2]),
-                              pack_cs(kLn2 * cs[4 * cc + 3], kLn2 * sn[4 * cc + 3])));
+                   make_uint4(pack_cs(cs[4 * cc], sn[4 * cc]),
+                              pack_cs(cs[4 * cc + 1], sn[4 * cc + 1]),
+                              pack_cs(cs[4 * cc + 2], sn[4 * cc + 2]),
+                              pack_cs(cs[4 * cc + 3], sn[4 * cc + 3])));
           }
         } else {
           tmem_st16(lane_base + tk::AVT + rg * PW + 16 * g, o);
@@ -1003,14 +1004,16 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           sts32f(s_xch + ((hh * 2 + rg) * 128 + r) * 4, sum4);
           mbar_arrive(&bars[B_XCH + hh]);
         }
-        // Y_m = dl T_m(u), packed per term for the group's 4 keys
+        // Y_m = dl T_m(u), packed per term for the group's 4 keys (dQ launch:
+        // times ln 2, the base of the logits, so that X and the dq fold carry it)
         uint32_t y[kM][2];
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
           // Y_m = dl T_m(u) obeys the Chebyshev recurrence itself:
           // Y_{m+1} = 2u Y_m - Y_{m-1}, Y_0 = dl, Y_1 = dl u
+          constexpr float ys = MODE == MODE_DQ ? kLn2 : 1.f;
           const float ua = 2.f * uj[2 * jp], ub = 2.f * uj[2 * jp + 1];
-          float ya0 = dl[2 * jp], yb0 = dl[2 * jp + 1];
+          float ya0 = ys * dl[2 * jp], yb0 = ys * dl[2 * jp + 1];
           float ya1 = ya0 * uj[2 * jp], yb1 = yb0 * uj[2 * jp + 1];
           y[0][jp] = E::pack(ya0, yb0);
           y[1][jp] = E::pack(ya1, yb1);
@@ -1079,7 +1082,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       return true;
     };
 
-    // dq += ln2 R(-(carry + c0) theta) X for this group's 32 pairs
+    // dq += R(-(carry + c0) theta) X for this group's 32 pairs (X carries the
+    // ln 2 of the logits' base: the dQ launch scales Y by it)
     auto dq_update = [&](int w) -> bool {
       if (!wwait(bars[B_XF], w & 1, err, kErrX)) return false;
       tc_fence_after();
@@ -1096,7 +1100,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         for (int i = 0; i < 2; ++i) {
 #pragma unroll
           for (int e2 = 0; e2 < 8; ++e2) {
-            const float2 cs = unpack_cs(csc[8 * (g0 + i) + e2]);  // ln2 cos, ln2 sin
+            const float2 cs = unpack_cs(csc[8 * (g0 + i) + e2]);  // cos, sin
             const float xe = __uint_as_float(xv[i][2 * e2]), xo = __uint_as_float(xv[i][2 * e2 + 1]);
             qv2[i][2 * e2] = __float_as_uint(
                 fmaf(cs.y, xo, fmaf(cs.x, xe, __uint_as_float(qv2[i][2 * e2]))));
