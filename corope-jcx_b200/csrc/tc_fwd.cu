@@ -28,8 +28,11 @@
 //   warp 8     TMA: Q once, K/V tiles of 64 keys (2 stages)
 //   warp 9     UMMA issue of the G GEMM (A operand from tensor memory)
 //   warp 10    UMMA issue of the gate GEMM Q K^T and of P V
-//   warps 12-15 build the K^(m) operand of each window in shared memory
-//              (double-buffered when it fits)
+//   warps 12-15 without panels: build the K^(m) operand of each window in
+//              shared memory (double-buffered when it fits); with panels
+//              (warp 11 then TMA-loads them): the window's gates, in-window
+//              positions and carry, one thread per row, handed to both row
+//              groups through shared memory
 // Registers are re-balanced with setmaxnreg (rows 176, builders 104, the
 // TMA/UMMA warpgroup 56), then a CTA barrier so that no warp returns
 // registers to the pool before every warp holds its share.
@@ -110,11 +113,18 @@ struct Layout {
   static constexpr int SLOT = BAR + NBAR * 8;
   // row-group exchange: [2 groups][128 rows] row max, then [2][128] row sums
   static constexpr int XCH = (SLOT + 16 + 15) & ~15;
-  // builder work items: [kMaxItems][128 threads] x (uint2)
+  // builder work items: [kMaxItems][128 threads] x (uint2); launches with
+  // panels use the region for the gate hand-off of warps 12-15 instead:
+  // u [2 buffers][2 row groups][2 chunks][128 rows] x float4, then the
+  // A-operand carry [2 buffers][128 rows] x float
   static constexpr int MAX_ITEMS = (2 * 8 * 8 * kM + 127) / 128;
   static constexpr int ITEMS = XCH + 4 * 128 * 4;
+  static constexpr int GU = ITEMS;
+  static constexpr int GC = GU + 2 * 2 * 2 * 128 * 16;
+  static constexpr int REGION = MAX_ITEMS * 128 * 8 > GC + 2 * 128 * 4 - ITEMS
+                                    ? MAX_ITEMS * 128 * 8 : GC + 2 * 128 * 4 - ITEMS;
   // K^(m) buffers [2 halves][nb][b_buf_bytes] follow, 1024-aligned
-  static constexpr int BOP = (ITEMS + MAX_ITEMS * 128 * 8 + 1023) & ~1023;
+  static constexpr int BOP = (ITEMS + REGION + 1023) & ~1023;
   // tensor-memory columns
   static constexpr uint32_t GW = 8 * kM;  // columns of one G half
   static constexpr uint32_t T_O = 0;
@@ -135,11 +145,27 @@ enum {
   B_BF = 11,  // [half][buffer] -> B_BF + 2 * half + buffer
   B_BE = 15,  // [half][buffer]
   B_AV = 19, B_P = 20, B_O = 21, B_DRAIN = 22, B_DRAIN2 = 23,
-  B_XM = 24, B_XL = 25  // row-group exchanges: window row max, final row sums
+  B_XM = 24, B_XL = 25,  // row-group exchanges: window row max, final row sums
+  B_GT = 26              // [buffer]: gates of a window ready (panel launches)
 };
 
 using tcx::ElemTraits;
 using tcx::sigmoid_f;
+
+// Gates of one window for row t (keys j0 .. j0 + 15, descending): the
+// in-window positions uu[jj] = (gate sum of the window's keys after jj) / c0
+// - 1, and the window's gate sum (returned).  Keys past t have gate 0.
+__device__ __forceinline__ float fwd_window_gates(const uint32_t (&sraw)[16], int j0, int t,
+                                                  float (&uu)[16]) {
+  float acc = 0.f;
+#pragma unroll
+  for (int jj = 15; jj >= 0; --jj) {
+    const float z = (j0 + jj <= t) ? sigmoid_f(__uint_as_float(sraw[jj])) : 0.f;
+    uu[jj] = fmaf(acc, 1.0f / kC0, -1.0f);
+    acc += z;
+  }
+  return acc;
+}
 
 // KMT: the K^(m) operands come from precomputed panels in global memory
 // (tcx::panel_kernel) by TMA, one copy per slab and half window, instead of
@@ -188,6 +214,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
     mbar_init(&bars[B_P], 256);
     mbar_init(&bars[B_XM], 256);
     mbar_init(&bars[B_XL], 256);
+    mbar_init(&bars[B_GT], 128);
+    mbar_init(&bars[B_GT + 1], 128);
     mbar_init(&bars[B_O], 1);
     mbar_init(&bars[B_DRAIN], 1);
     mbar_init(&bars[B_DRAIN2], 1);
@@ -306,36 +334,71 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         mma_commit(&bars[B_DRAIN2]);
         mbar_wait(&bars[B_DRAIN2], 0, err, kErrDrain);
       }
+    } else if (warp == 11 && KMT) {
+      // ------------------------------------------------- K^(m) panel loads
+      if (lane == 0) {
+        prefetch_tmap(&P.tm_km[0]);
+        if (NS > 1) prefetch_tmap(&P.tm_km[1]);
+        const uint32_t bytes = (P.km_rows[0] + (NS > 1 ? P.km_rows[1] : 0)) * 128;
+        const int panel0 = (b * P.Hkv + hk) * P.km_nhw;
+        int last[4] = {-1, -1, -1, -1};  // [half][buffer]: last use issued
+        bool ok = true;
+        for (int w = W0; ok && w >= 0; --w) {
+          const int k = W0 - w, buf = k % nb, use = k / nb;
+          for (int hh = 0; hh < 2; ++hh) {
+            const int i = 2 * hh + buf;
+            if (use > 0 && !(ok = mbar_wait(&bars[B_BE + i], (use - 1) & 1, err, kErrBEmpty))) break;
+            mbar_expect_tx(&bars[B_BF + i], bytes);
+            uint8_t* dst = smem + L::BOP + (hh * nb + buf) * P.b_buf_bytes;
+            for (int s = 0; s < NS; ++s)
+              tma_load_3d(dst + P.b_slab_off[s], &P.tm_km[s], &bars[B_BF + i], 0, 0,
+                          panel0 + 2 * w + hh);
+            last[i] = use;
+          }
+        }
+        // no copy may still be in flight when the CTA exits
+        for (int i = 0; i < 4; ++i)
+          if (last[i] >= 0) mbar_wait(&bars[B_BF + i], last[i] & 1, err, kErrDrain);
+      }
     }
     __syncwarp();
     regs_inc<128>();
   } else if (warp >= 12 && KMT) {
     regs_dec<kBldRegs>();
     named_bar(1, kThreads);
-    // ------------------------------------------------- K^(m) panel loads
-    if (warp == 12 && lane == 0) {
-      prefetch_tmap(&P.tm_km[0]);
-      if (NS > 1) prefetch_tmap(&P.tm_km[1]);
-      const uint32_t bytes = (P.km_rows[0] + (NS > 1 ? P.km_rows[1] : 0)) * 128;
-      const int panel0 = (b * P.Hkv + hk) * P.km_nhw;
-      int last[4] = {-1, -1, -1, -1};  // [half][buffer]: last use issued
-      bool ok = true;
-      for (int w = W0; ok && w >= 0; --w) {
-        const int k = W0 - w, buf = k % nb, use = k / nb;
-        for (int hh = 0; hh < 2; ++hh) {
-          const int i = 2 * hh + buf;
-          if (use > 0 && !(ok = mbar_wait(&bars[B_BE + i], (use - 1) & 1, err, kErrBEmpty))) break;
-          mbar_expect_tx(&bars[B_BF + i], bytes);
-          uint8_t* dst = smem + L::BOP + (hh * nb + buf) * P.b_buf_bytes;
-          for (int s = 0; s < NS; ++s)
-            tma_load_3d(dst + P.b_slab_off[s], &P.tm_km[s], &bars[B_BF + i], 0, 0,
-                        panel0 + 2 * w + hh);
-          last[i] = use;
-        }
-      }
-      // no copy may still be in flight when the CTA exits
-      for (int i = 0; i < 4; ++i)
-        if (last[i] >= 0) mbar_wait(&bars[B_BF + i], last[i] & 1, err, kErrDrain);
+    // ------------------------------------------------- gates (panel launches)
+    // One thread per row: the window's gates and in-window positions and the
+    // running carry, handed to both row groups through shared memory (the
+    // row groups would otherwise each compute all 16 gates of the row).
+    const int r = tid - 384;
+    const int t = q0 + r;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t s_gu = smem_u32(smem + L::GU), s_gc = smem_u32(smem + L::GC);
+    float carry = 0.f, carry_c = 0.f;  // compensated, as in the row code
+    for (int w = W0; w >= 0; --w) {
+      const int buf = w & 1;
+      if (!wwait(bars[B_SG + buf], ((W0 - w) >> 1) & 1, err, kErrSg)) break;
+      tc_fence_after();
+      uint32_t sraw[16];
+      tmem_ld16(lane_base + ((w & 1) ? L::T_SG1 : L::T_SG0), sraw);
+      tmem_wait_ld();
+      float uu[16];
+      const float acc = fwd_window_gates(sraw, w * kW, t, uu);
+      // group g's keys i -> 8 (i >> 2) + 4 g + (i & 3): chunk c = i >> 2
+#pragma unroll
+      for (int g = 0; g < 2; ++g)
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          sts128f(s_gu + (((buf * 2 + g) * 2 + c) * 128 + r) * 16,
+                  make_float4(uu[8 * c + 4 * g], uu[8 * c + 4 * g + 1], uu[8 * c + 4 * g + 2],
+                              uu[8 * c + 4 * g + 3]));
+      const float y = acc - carry_c;
+      const float carry_next = carry + y;
+      carry_c = (carry_next - carry) - y;
+      carry = carry_next;
+      sts32f(s_gc + (buf * 128 + r) * 4, carry - carry_c);
+      tc_fence_before();
+      mbar_arrive(&bars[B_GT + buf]);
     }
     __syncwarp();
     regs_inc<128>();
@@ -448,6 +511,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
     // S/16 windows drifts by ~1e-2 (an angle error of that size in the fastest
     // rotation).  carry - carry_c is the sum to ~1 ulp.
     float carry = 0.f, carry_c = 0.f;
+    float a_total = 0.f;  // gate sum of all keys (the saved A)
+    const uint32_t s_gu = smem_u32(smem + L::GU), s_gc = smem_u32(smem + L::GC);
     float m_used = -1e30f, m_true = -INFINITY;
     float lsum = 0.f;                      // this group's keys
     bool ok = wwait(bars[B_Q], 0, err, kErrQ);
@@ -538,33 +603,41 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       const int k = W0 - w;
       const int j0 = w * kW;
       const uint32_t sg = (w & 1) ? L::T_SG1 : L::T_SG0;
-      // gates of the window
-      if (!(ok = wwait(bars[B_SG + (w & 1)], ((W0 - w) >> 1) & 1, err, kErrSg))) break;
-      tc_fence_after();
-      uint32_t sraw[16];
-      tmem_ld16(lane_base + sg, sraw);
-      tmem_wait_ld();
-      float uu[16];
-      float acc = 0.f;
-#pragma unroll
-      for (int jj = 15; jj >= 0; --jj) {
-        const float z = (j0 + jj <= t) ? sigmoid_f(__uint_as_float(sraw[jj])) : 0.f;
-        uu[jj] = fmaf(acc, 1.0f / kC0, -1.0f);
-        acc += z;
-      }
-      // this group's keys: i -> key 8 (i >> 2) + 4 rg + (i & 3)
+      // gates of the window: this group's keys i -> key 8 (i >> 2) + 4 rg + (i & 3)
       float uo[8];
+      float carry_a;  // gate sum of the keys after the next window (its A operand)
+      if (KMT) {
+        // from warps 12-15
+        const int buf = w & 1;
+        if (!(ok = wwait(bars[B_GT + buf], ((W0 - w) >> 1) & 1, err, kErrSg))) break;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int kk = 8 * (i >> 2) + (i & 3);
-        uo[i] = rg ? uu[kk + 4] : uu[kk];
+        for (int c = 0; c < 2; ++c) {
+          const float4 v = lds128f(s_gu + (((buf * 2 + rg) * 2 + c) * 128 + r) * 16);
+          uo[4 * c] = v.x; uo[4 * c + 1] = v.y; uo[4 * c + 2] = v.z; uo[4 * c + 3] = v.w;
+        }
+        carry_a = lds32f(s_gc + (buf * 128 + r) * 4);
+      } else {
+        if (!(ok = wwait(bars[B_SG + (w & 1)], ((W0 - w) >> 1) & 1, err, kErrSg))) break;
+        tc_fence_after();
+        uint32_t sraw[16];
+        tmem_ld16(lane_base + sg, sraw);
+        tmem_wait_ld();
+        float uu[16];
+        const float acc = fwd_window_gates(sraw, j0, t, uu);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int kk = 8 * (i >> 2) + (i & 3);
+          uo[i] = rg ? uu[kk + 4] : uu[kk];
+        }
+        const float y = acc - carry_c;
+        const float carry_next = carry + y;
+        carry_c = (carry_next - carry) - y;
+        carry = carry_next;
+        carry_a = carry - carry_c;
       }
-      const float y = acc - carry_c;
-      const float carry_next = carry + y;
-      const float carry_c_next = (carry_next - carry) - y;
       // A operand of the next window (its buffer was last read by G(w+1),
       // which completed before this row group loaded G(w+1))
-      if (w > 0) build_a(carry_next - carry_c_next, ((w - 1) & 1) ? L::T_AV1 : L::T_AV0);
+      if (w > 0) build_a(carry_a, ((w - 1) & 1) ? L::T_AV1 : L::T_AV0);
       float lg[8];
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
@@ -631,8 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars[B_P]);
-      carry = carry_next;
-      carry_c = carry_c_next;
+      a_total = carry_a;
     }
     // epilogue: row sum of both groups, then this group's output columns
     if (ok) ok = wwait(bars[B_O], W0 & 1, err, kErrO);
@@ -667,7 +739,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         const float Lv = ltot * exp2f(m_used - m_true);
         if (P.m) P.m[ri] = M;
         if (P.l) P.l[ri] = Lv;
-        if (P.a) P.a[ri] = carry - carry_c;
+        if (P.a) P.a[ri] = a_total;
         if (P.lse) P.lse[ri] = M + logf(Lv);
       }
     }
