@@ -21,6 +21,45 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kSmemLimit = 232448;  // opt-in dynamic shared memory per block
 
+// Key slots of a half window.  The G GEMM's columns, the scaled-key panels and
+// the row groups see the 8 keys of a half window in slot order: slot s holds
+// key slot_key(s) of the half, and row group g takes slots 4g .. 4g + 3 --
+// key pairs (0, 1) and (6, 7) for group 0, (2, 3) and (4, 5) for group 1 --
+// so that with the per-offset term counts below both groups and both key
+// pairs of a group run similar numbers of terms.
+__host__ __device__ constexpr int slot_key(int s) { return s < 2 ? s : s < 4 ? s + 4 : s - 2; }
+
+// Per-offset expansions (launches with scaled-key panels).  Key o of a window
+// (0 .. 15, ascending) sits at a_tj = C_t + s_o with s_o, the gate sum of the
+// window's keys after it, in [0, 15 - o]: its expansion is centred at
+// C_t + c_o with half-width c_o = (15 - o) / 2 instead of the window's c0, so
+// it needs fewer terms the later the key.  The term counts keep the
+// truncation error of the value (and, for the 16-term backward, of its
+// position derivative, for which the last key keeps c = 1/2) at or below that
+// of the uniform expansion at c0.  The shift from the window centre,
+// exp(i (c0 - c_o) theta_p), is folded into the panels.
+__host__ __device__ constexpr int offset_terms(int km, int o) {
+  return km == 16 ? (o < 2 ? 16 : o == 2 ? 15 : o < 5 ? 14 : o == 5 ? 13 : o < 8 ? 12
+                     : o == 8 ? 11 : o == 9 ? 10 : o == 10 ? 9 : o == 11 ? 8 : o == 12 ? 7
+                     : o == 13 ? 6 : 5)
+                  : (o < 2 ? 14 : o < 4 ? 13 : o == 4 ? 12 : o < 7 ? 11 : o == 7 ? 10
+                     : o == 8 ? 9 : o < 11 ? 8 : o == 11 ? 7 : o == 12 ? 6 : o == 13 ? 5
+                     : o == 14 ? 4 : 1);
+}
+__host__ __device__ constexpr float offset_halfwidth(int km, int o) {
+  return km == 16 && o == 15 ? 0.5f : 0.5f * (15 - o);
+}
+__host__ __device__ constexpr float offset_inv_halfwidth(int km, int o) {
+  return offset_halfwidth(km, o) > 0.f ? 1.0f / offset_halfwidth(km, o) : 0.f;
+}
+// Terms a row group runs for position j (0..3) of half hh: the larger count
+// of the two groups' keys there (the smaller one's extra terms are zero).
+__host__ __device__ constexpr int position_terms(int km, int hh, int j) {
+  return offset_terms(km, 8 * hh + slot_key(j)) > offset_terms(km, 8 * hh + slot_key(4 + j))
+             ? offset_terms(km, 8 * hh + slot_key(j))
+             : offset_terms(km, 8 * hh + slot_key(4 + j));
+}
+
 template <typename T> struct ElemTraits;
 template <> struct ElemTraits<__nv_bfloat16> {
   static constexpr bool kBf16 = true;
@@ -101,7 +140,7 @@ inline bool encode_panels(CUtensorMap* m, const void* ptr, int dtype, int rows, 
 
 // Bessel function of the first kind, integer order, by its power series
 // (|x| <= 8 here, where the series converges quickly in double precision).
-inline double bessel_j(int m, double x) {
+__host__ __device__ inline double bessel_j(int m, double x) {
   double term = 1.0;
   for (int i = 1; i <= m; ++i) term *= (x / 2.0) / i;
   double sum = term;
@@ -109,7 +148,7 @@ inline double bessel_j(int m, double x) {
   for (int k = 1; k < 80; ++k) {
     term *= q / (k * (double)(k + m));
     sum += term;
-    if (std::fabs(term) < 1e-18 * std::fabs(sum) + 1e-300) break;
+    if (fabs(term) < 1e-18 * fabs(sum) + 1e-300) break;
   }
   return sum;
 }
@@ -119,6 +158,21 @@ inline double bessel_j(int m, double x) {
 // K-step s (16 head dims) reads (8 keys per term, rounded to 16 rows).
 template <int KM = kM>
 inline void fill_coefficients(float (*coef)[64], int* nrow, int D, float theta, float sm_scale) {
+  // KM x D/2 Bessel functions per call (tens of microseconds of host time,
+  // several times per backward call): kept per (KM, D, theta, sm_scale)
+  struct Entry { int D; float theta, sm_scale; int nrow[8]; float coef[KM][64]; };
+  static std::mutex mu;
+  static Entry cache[8];
+  static int ncache = 0;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    for (int i = 0; i < ncache; ++i)
+      if (cache[i].D == D && cache[i].theta == theta && cache[i].sm_scale == sm_scale) {
+        std::memcpy(nrow, cache[i].nrow, sizeof(cache[i].nrow));
+        std::memcpy(coef, cache[i].coef, sizeof(cache[i].coef));
+        return;
+      }
+  }
   const int NP = D / 2;
   int kd[KM];
   for (int m = 0; m < KM; ++m) {
@@ -139,6 +193,61 @@ inline void fill_coefficients(float (*coef)[64], int* nrow, int D, float theta, 
     nm = (nm + 1) & ~1;
     nrow[s] = (s < D / 16) ? 8 * nm : 0;
   }
+  std::lock_guard<std::mutex> g(mu);
+  Entry& e = cache[ncache < 8 ? ncache++ : 7];
+  e.D = D;
+  e.theta = theta;
+  e.sm_scale = sm_scale;
+  std::memcpy(e.nrow, nrow, sizeof(e.nrow));
+  std::memcpy(e.coef, coef, sizeof(e.coef));
+}
+
+// The same K extents for the per-offset expansions of the panels: term m of
+// key offset o has coefficient eps_m J_m(c_o theta_p) for m below the
+// offset's count, zero above.
+// The scan evaluates 16 x KM x D/2 Bessel functions (about a millisecond of
+// host time), so its result is kept per (KM, D, theta).
+template <int KM>
+inline void fill_offset_rows(int* nrow, int D, float theta) {
+  struct Entry { int D; float theta; int nrow[8]; };
+  static std::mutex mu;
+  static Entry cache[16];
+  static int ncache = 0;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    for (int i = 0; i < ncache; ++i)
+      if (cache[i].D == D && cache[i].theta == theta) {
+        std::memcpy(nrow, cache[i].nrow, sizeof(cache[i].nrow));
+        return;
+      }
+  }
+  const int NP = D / 2;
+  int kd[KM];
+  for (int m = 0; m < KM; ++m) {
+    int need = 0;
+    for (int o = 0; o < 16; ++o) {
+      if (m >= offset_terms(KM, o)) continue;
+      for (int q = 0; q < NP; ++q) {
+        const double th = 1.0 / std::pow((double)theta, (double)(2 * q) / (double)D);
+        const double beta =
+            (m == 0 ? 1.0 : 2.0) * bessel_j(m, (double)offset_halfwidth(KM, o) * th);
+        if (std::fabs(beta) > 2e-6) need = std::max(need, q + 1);
+      }
+    }
+    kd[m] = std::max(1, (2 * need + 15) / 16);
+  }
+  for (int m = KM - 2; m >= 0; --m) kd[m] = std::max(kd[m], kd[m + 1]);
+  for (int s = 0; s < 8; ++s) {
+    int nm = 0;
+    for (int m = 0; m < KM; ++m) nm += kd[m] > s;
+    nm = (nm + 1) & ~1;
+    nrow[s] = (s < D / 16) ? 8 * nm : 0;
+  }
+  std::lock_guard<std::mutex> g(mu);
+  Entry& e = cache[ncache < 16 ? ncache++ : 15];
+  e.D = D;
+  e.theta = theta;
+  std::memcpy(e.nrow, nrow, sizeof(e.nrow));
 }
 
 // ------------------------------------------------------------------
@@ -221,6 +330,142 @@ inline size_t panel_bytes(int B, int Hkv, int S, int D, float theta, float sm_sc
   p.B = B; p.Hkv = Hkv; p.S = S;
   p.nhw = 2 * ((S + kW - 1) / kW);
   return (size_t)panel_count(B, Hkv, S) * (p.rows[0] + p.rows[1]) * 128;
+}
+
+
+// ------------------------------------------------------------------
+// Scaled-key panels of the per-offset expansions (the forward's).  Term m
+// of the key at offset o of its window is
+//   eps_m J_m(c_o theta_p) * sm_scale * log2(e) * (-i)^m * exp(i (c0 - c_o) theta_p)
+// times the key's pair p (zero from the offset's term count on).  Those
+// complex coefficients depend on the call's theta and scale only: one small
+// launch writes them, [16 offsets][16 terms][64 pairs] x float2, behind the
+// panels in the workspace, and the panel launch reads them from there.
+constexpr size_t kOffsetCoefBytes = (size_t)16 * kPanelTerms * 64 * 8;
+
+struct OffsetPanelArgs {
+  const void* k;
+  int64_t ks[3];
+  int B, Hkv, S;
+  int nhw;          // half windows per (b, hk): 2 * ceil(S / 16)
+  int rows[2];      // panel rows per slab (the slab's first K step's count)
+  int nrow[8];      // rows each K step reads (multiples of 16)
+  void* out[2];     // slab panels
+  float2* cf;       // [16][kPanelTerms][64] complex coefficients
+  int km;           // most terms of any offset
+  float scale;      // sm_scale * log2(e)
+  double th[64];    // theta_p
+};
+
+// J_0(x) .. J_{n-1}(x) (n <= 16, 0 <= x <= 8) by Miller's backward recurrence
+// J_{k-1} = (2k / x) J_k - J_{k+1} from k = 32, normalised by
+// J_0 + 2 (J_2 + J_4 + ...) = 1.
+__device__ inline void bessel_j_all(double x, int n, double* out) {
+  if (x == 0.0) {
+    for (int m = 0; m < n; ++m) out[m] = m == 0 ? 1.0 : 0.0;
+    return;
+  }
+  const double r = 2.0 / x;
+  double jp = 0.0, j = 1e-30, norm = 0.0;
+  for (int k = 32; k >= 1; --k) {
+    const double jm = k * r * j - jp;  // J_{k-1}
+    jp = j;
+    j = jm;
+    if (k - 1 < n) out[k - 1] = j;
+    if (((k - 1) & 1) == 0) norm += (k - 1 == 0 ? 1.0 : 2.0) * j;
+    if (fabs(j) > 1e200) {  // keep the unnormalised values in range
+      j *= 1e-200; jp *= 1e-200; norm *= 1e-200;
+      for (int m = k - 1; m < n; ++m) out[m] *= 1e-200;
+    }
+  }
+  const double inv = 1.0 / norm;
+  for (int m = 0; m < n; ++m) out[m] *= inv;
+}
+
+// One thread per (offset o = blockIdx.x, pair p = threadIdx.x).
+static __global__ void __launch_bounds__(64) offset_coef_kernel(const __grid_constant__ OffsetPanelArgs A) {
+  const int o = blockIdx.x, p = threadIdx.x;
+  const double c = offset_halfwidth(A.km, o);
+  const int n = offset_terms(A.km, o);
+  double jv[kPanelTerms];
+  bessel_j_all(c * A.th[p], n, jv);
+  double sn, cs;
+  sincos((kC0 - c) * A.th[p], &sn, &cs);
+  for (int m = 0; m < kPanelTerms; ++m) {
+    const double be = m < n ? (m == 0 ? 1.0 : 2.0) * jv[m] * A.scale : 0.0;
+    // (-i)^m exp(i phi) = exp(i (phi - m pi / 2))
+    double re, im;
+    switch (m & 3) {
+      case 0: re = cs; im = sn; break;
+      case 1: re = sn; im = -cs; break;
+      case 2: re = -cs; im = -sn; break;
+      default: re = -sn; im = cs; break;
+    }
+    A.cf[((size_t)o * kPanelTerms + m) * 64 + p] = make_float2((float)(be * re), (float)(be * im));
+  }
+}
+
+// Row r of K step s (16 elements = two 16-byte chunks) of half window hw
+// holds term m = r / 8 of the key in slot r % 8 (key slot_key(r % 8) of the
+// half): its complex coefficient times the key's pair.  Rows a K step does not
+// read (past nrow[s]) and keys past S are zero.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) offset_panel_kernel(const __grid_constant__ OffsetPanelArgs A) {
+  using E = ElemTraits<T>;
+  const int hw = blockIdx.x, bh = blockIdx.y;
+  const int b = bh / A.Hkv, hk = bh % A.Hkv;
+  const T* kb = static_cast<const T*>(A.k) + b * A.ks[0] + hk * A.ks[1];
+  const int o0 = 8 * (hw & 1);  // window offset of the half's first key
+#pragma unroll
+  for (int s = 0; s < D / 64; ++s) {
+    const int rows = A.rows[s];
+    uint4* out = static_cast<uint4*>(A.out[s]) + ((int64_t)bh * A.nhw + hw) * rows * 8;
+    for (int it = threadIdx.x; it < rows * 8; it += 128) {
+      const int r = it >> 3, c = it & 7, m = r >> 3, slot = r & 7;
+      const int kk = slot_key(slot);
+      const int key = 8 * hw + kk;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < A.nrow[4 * s + (c >> 1)] && key < A.S && m < kPanelTerms) {
+        const uint4 kv =
+            *reinterpret_cast<const uint4*>(kb + (int64_t)key * A.ks[2] + 64 * s + 8 * c);
+        const float4* cp = reinterpret_cast<const float4*>(
+            A.cf + ((size_t)(o0 + kk) * kPanelTerms + m) * 64 + 32 * s + 4 * c);
+        const float4 c01 = __ldg(cp), c23 = __ldg(cp + 1);
+        const float cr[4] = {c01.x, c01.z, c23.x, c23.z}, ci[4] = {c01.y, c01.w, c23.y, c23.w};
+        const uint32_t in[4] = {kv.x, kv.y, kv.z, kv.w};
+        uint32_t ov[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float kl = E::lo(in[e]), kh = E::hi(in[e]);
+          ov[e] = E::pack(kl * cr[e] - kh * ci[e], kl * ci[e] + kh * cr[e]);
+        }
+        v = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+      }
+      out[it] = v;
+    }
+  }
+}
+
+// Fill the arguments of the per-offset panels (KM: most terms of any
+// offset) and return the workspace bytes they take: both slabs' panels, then
+// the coefficient table (0 when the head dim has none).
+template <int KM>
+inline size_t offset_panel_bytes(int B, int Hkv, int S, int D, float theta, float sm_scale,
+                                 OffsetPanelArgs* a = nullptr) {
+  OffsetPanelArgs local;
+  OffsetPanelArgs& p = a ? *a : local;
+  std::memset(&p, 0, sizeof(p));
+  fill_offset_rows<KM>(p.nrow, D, theta);
+  p.rows[0] = p.nrow[0];
+  p.rows[1] = D == 128 ? p.nrow[4] : 0;
+  p.B = B; p.Hkv = Hkv; p.S = S;
+  p.nhw = 2 * ((S + kW - 1) / kW);
+  p.km = KM;
+  p.scale = sm_scale * kLog2e;
+  for (int q = 0; q < 64; ++q)
+    p.th[q] = q < D / 2 ? 1.0 / std::pow((double)theta, (double)(2 * q) / (double)D) : 0.0;
+  const size_t panels = (size_t)panel_count(B, Hkv, S) * (p.rows[0] + p.rows[1]) * 128;
+  return panels > 0 ? panels + kOffsetCoefBytes : 0;
 }
 
 }  // namespace tcx

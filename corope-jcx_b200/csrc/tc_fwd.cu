@@ -16,7 +16,10 @@
 // keep the expansion error below 1.1e-3 at the highest frequency (w = 7.5)
 // and far below it elsewhere -- under the rounding of the 16-bit GEMM
 // operands; coefficients below 2e-6 are pruned, which shortens the K extent
-// of the high-m terms.
+// of the high-m terms.  With the scaled-key panels each key offset of the
+// window has its own expansion (tcx::offset_terms): key o only spans
+// positions C_t .. C_t + 15 - o, so later keys need fewer terms (79 instead
+// of 112 Clenshaw steps per row thread and window).
 //
 // Roles per CTA (128 query rows of one (b, h), 512 threads):
 //   warps 0-7  two row warpgroups sharing every row (group g: keys 4g..4g+3
@@ -39,6 +42,7 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -151,17 +155,21 @@ enum {
 
 using tcx::ElemTraits;
 using tcx::sigmoid_f;
+using tcx::slot_key;
 
 // Gates of one window for row t (keys j0 .. j0 + 15, descending): the
 // in-window positions uu[jj] = (gate sum of the window's keys after jj) / c0
 // - 1, and the window's gate sum (returned).  Keys past t have gate 0.
+// PER_OFFSET (panel launches): positions scaled by each key offset's own
+// half-width, uu[jj] = acc / c_jj - 1.
+template <bool PER_OFFSET>
 __device__ __forceinline__ float fwd_window_gates(const uint32_t (&sraw)[16], int j0, int t,
                                                   float (&uu)[16]) {
   float acc = 0.f;
 #pragma unroll
   for (int jj = 15; jj >= 0; --jj) {
     const float z = (j0 + jj <= t) ? sigmoid_f(__uint_as_float(sraw[jj])) : 0.f;
-    uu[jj] = fmaf(acc, 1.0f / kC0, -1.0f);
+    uu[jj] = fmaf(acc, PER_OFFSET ? tcx::offset_inv_halfwidth(kM, jj) : 1.0f / kC0, -1.0f);
     acc += z;
   }
   return acc;
@@ -383,15 +391,15 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       tmem_ld16(lane_base + ((w & 1) ? L::T_SG1 : L::T_SG0), sraw);
       tmem_wait_ld();
       float uu[16];
-      const float acc = fwd_window_gates(sraw, w * kW, t, uu);
-      // group g's keys i -> 8 (i >> 2) + 4 g + (i & 3): chunk c = i >> 2
+      const float acc = fwd_window_gates<true>(sraw, w * kW, t, uu);
+      // group g's keys i -> 8 (i >> 2) + slot_key(4 g + (i & 3)): chunk c = i >> 2
 #pragma unroll
       for (int g = 0; g < 2; ++g)
 #pragma unroll
         for (int c = 0; c < 2; ++c)
           sts128f(s_gu + (((buf * 2 + g) * 2 + c) * 128 + r) * 16,
-                  make_float4(uu[8 * c + 4 * g], uu[8 * c + 4 * g + 1], uu[8 * c + 4 * g + 2],
-                              uu[8 * c + 4 * g + 3]));
+                  make_float4(uu[8 * c + slot_key(4 * g)], uu[8 * c + slot_key(4 * g + 1)],
+                              uu[8 * c + slot_key(4 * g + 2)], uu[8 * c + slot_key(4 * g + 3)]));
       const float y = acc - carry_c;
       const float carry_next = carry + y;
       carry_c = (carry_next - carry) - y;
@@ -434,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
           for (int q = 0; q < 7; ++q)
             if (it >= item_end[q]) { s2 = q + 1; base = item_end[q]; }
           const int local = it - base;
-          const int r = local >> 1, c = 2 * s2 + (local & 1), m = r >> 3, j = r & 7;
+          const int r = local >> 1, c = 2 * s2 + (local & 1), m = r >> 3, j = slot_key(r & 7);
           const uint32_t kofs = (c >> 3) * 8192 + j * 128 + (((c & 7) ^ j) << 4);
           const uint32_t cofs = (m * NP + 4 * c) * 4;
           const uint32_t bofs = P.b_slab_off[c >> 3] + sw128_offset(r, c & 7);
@@ -563,15 +571,26 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       mbar_arrive(&bars[B_AV]);
     };
 
-    // Clenshaw combine of this group's 4 keys of one G half:
-    // f_j = sum_m T_m(u_j) G_m, G columns 16 c + 8 (m & 1) + key (m = 2c + (m & 1)).
+    // Clenshaw combine of this group's 4 keys (slots 4 rg + j) of G half HH:
+    // f_j = sum_m T_m(u_j) G_m, G columns 16 c + 8 (m & 1) + slot (m = 2c + (m & 1)).
+    // Position j runs NT(j) terms: all kM, or with the panels' per-offset
+    // expansions the larger count of the two groups' keys at that position.
     // All loads go out before one wait; the half's G region is then released.
-    auto combine = [&](uint32_t gcol, const float (&uj)[4], float (&f)[4], int ge_bar) {
+    auto combine = [&](auto hh_tag, uint32_t gcol, const float (&uj)[4], float (&f)[4],
+                       int ge_bar) {
+      constexpr int HH = decltype(hh_tag)::value;
+      constexpr int NT0 = KMT ? tcx::position_terms(kM, HH, 0) : kM;
+      constexpr int NT1 = KMT ? tcx::position_terms(kM, HH, 1) : kM;
+      constexpr int NT2 = KMT ? tcx::position_terms(kM, HH, 2) : kM;
+      constexpr int NT3 = KMT ? tcx::position_terms(kM, HH, 3) : kM;
+      constexpr int NT[4] = {NT0, NT1, NT2, NT3};
+      constexpr int NMAX = NT0 > NT1 ? (NT0 > NT2 ? (NT0 > NT3 ? NT0 : NT3) : (NT2 > NT3 ? NT2 : NT3))
+                                     : (NT1 > NT2 ? (NT1 > NT3 ? NT1 : NT3) : (NT2 > NT3 ? NT2 : NT3));
       uint32_t g[kM / 2][2][4];
 #pragma unroll
-      for (int c = 0; c < kM / 2; ++c) {
+      for (int c = 0; c < (NMAX + 1) / 2; ++c) {
         tmem_ld4(lane_base + gcol + 16 * c + 4 * rg, g[c][0]);
-        tmem_ld4(lane_base + gcol + 16 * c + 8 + 4 * rg, g[c][1]);
+        if (2 * c + 1 < NMAX) tmem_ld4(lane_base + gcol + 16 * c + 8 + 4 * rg, g[c][1]);
       }
       tmem_wait_ld();
       tc_fence_before();
@@ -580,9 +599,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
 #pragma unroll
       for (int j = 0; j < 4; ++j) { b1[j] = 0.f; b2[j] = 0.f; }
 #pragma unroll
-      for (int m = kM - 1; m >= 0; --m) {
+      for (int m = NMAX - 1; m >= 0; --m) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
+          if (m >= NT[j]) continue;
           const float a = __uint_as_float(g[m >> 1][m & 1][j]);
           if (m > 0) {
             const float bn = fmaf(2.0f * uj[j], b1[j], a - b2[j]);
@@ -603,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       const int k = W0 - w;
       const int j0 = w * kW;
       const uint32_t sg = (w & 1) ? L::T_SG1 : L::T_SG0;
-      // gates of the window: this group's keys i -> key 8 (i >> 2) + 4 rg + (i & 3)
+      // gates of the window: this group's keys i -> key 8 (i >> 2) + slot_key(4 rg + (i & 3))
       float uo[8];
       float carry_a;  // gate sum of the keys after the next window (its A operand)
       if (KMT) {
@@ -623,12 +643,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         tmem_ld16(lane_base + sg, sraw);
         tmem_wait_ld();
         float uu[16];
-        const float acc = fwd_window_gates(sraw, j0, t, uu);
+        const float acc = fwd_window_gates<false>(sraw, j0, t, uu);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int kk = 8 * (i >> 2) + (i & 3);
-          uo[i] = rg ? uu[kk + 4] : uu[kk];
-        }
+        for (int i = 0; i < 8; ++i)
+          uo[i] = rg ? uu[8 * (i >> 2) + slot_key(4 + (i & 3))] : uu[8 * (i >> 2) + slot_key(i & 3)];
         const float y = acc - carry_c;
         const float carry_next = carry + y;
         carry_c = (carry_next - carry) - y;
@@ -646,7 +664,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         float uj[4], f[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) uj[j] = hh ? uo[4 + j] : uo[j];
-        combine(hh ? L::T_G1 : L::T_G0, uj, f, B_GE + hh);
+        if (hh == 0)
+          combine(std::integral_constant<int, 0>(), L::T_G0, uj, f, B_GE);
+        else
+          combine(std::integral_constant<int, 1>(), L::T_G1, uj, f, B_GE + 1);
         if (hh == 0) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) lg[j] = f[j];
@@ -661,7 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
       float mx = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int kj = j0 + 8 * (i >> 2) + 4 * rg + (i & 3);
+        const int kj = j0 + 8 * (i >> 2) + (rg ? slot_key(4 + (i & 3)) : slot_key(i & 3));
         if (HAS_BIAS && kj <= t) lg[i] = fmaf(P.bias[(int64_t)t * P.bias_rs + kj], kLog2e, lg[i]);
         lg[i] = (kj <= t) ? lg[i] : -INFINITY;
         mx = fmaxf(mx, lg[i]);
@@ -698,9 +719,13 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
         lsum += p0 + p1;
         pk[i] = E::pack(p0, p1);
       }
-      // P over the gate columns (keys 2i, 2i+1 in word i)
-      tmem_st2(lane_base + sg + 2 * rg, pk[0], pk[1]);
-      tmem_st2(lane_base + sg + 4 + 2 * rg, pk[2], pk[3]);
+      // P over the gate columns (keys 2i, 2i+1 in word i): this group's key
+      // pairs are slots (4 rg, 4 rg + 1) and (4 rg + 2, 4 rg + 3) of each half
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int key = 8 * (i >> 1) + (rg ? slot_key(4 + 2 * (i & 1)) : slot_key(2 * (i & 1)));
+        tmem_st1(lane_base + sg + key / 2, pk[i]);
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars[B_P]);
@@ -790,31 +815,38 @@ static cudaError_t launch_k(const Params& p, int smem, dim3 grid, cudaStream_t s
   return cudaGetLastError();
 }
 
-// With a workspace of tcx::panel_bytes<kM> bytes the K^(m) operands are
-// written once by tcx::panel_kernel and loaded by TMA; without one the
-// forward kernel's builder warps make them from the K tiles.
+// With a workspace of tcx::offset_panel_bytes<kM> bytes the K^(m) operands
+// are written once by tcx::offset_panel_kernel (per-offset expansions, from
+// the coefficients tcx::offset_coef_kernel puts behind them) and loaded by
+// TMA; without one the forward kernel's builder warps make them from the K
+// tiles (one expansion per window).
 template <typename T, int D>
 static cudaError_t launch_t(Params& p, const FwdArgs& a, cudaStream_t st, void* ws,
                             size_t ws_bytes) {
+  static tcx::OffsetPanelArgs pa;  // guarded by the caller's lock
+  const size_t need = tcx::offset_panel_bytes<kM>(a.B, a.Hkv, a.Sk, D, a.theta, a.sm_scale, &pa);
+  const bool kmt = ws && need > 0 && ws_bytes >= need;
+  if (kmt)  // the per-offset expansions' K extents
+    for (int s = 0; s < 8; ++s) p.nrow[s] = pa.nrow[s];
   const int smem = plan_buffers<D>(p);
   if (smem > kSmemLimit) return cudaErrorInvalidValue;
   dim3 grid((a.S + kBM - 1) / kBM, a.H, a.B);
-  static tcx::PanelArgs pa;  // guarded by the caller's lock
-  const size_t need = tcx::panel_bytes<kM>(a.B, a.Hkv, a.Sk, D, a.theta, a.sm_scale, &pa);
-  const bool kmt = ws && need > 0 && ws_bytes >= need;
   if (kmt) {
     const int64_t np = tcx::panel_count(a.B, a.Hkv, a.Sk);
     pa.k = a.k;
     for (int i = 0; i < 3; ++i) pa.ks[i] = a.ks[i];
     pa.out[0] = ws;
     pa.out[1] = static_cast<uint8_t*>(ws) + np * pa.rows[0] * 128;
+    // the coefficient table behind both slabs' panels (16-byte aligned: rows are 128 B)
+    pa.cf = reinterpret_cast<float2*>(static_cast<uint8_t*>(ws) + np * (pa.rows[0] + pa.rows[1]) * 128);
     for (int s = 0; s < D / 64; ++s)
       if (!tcx::encode_panels(&p.tm_km[s], pa.out[s], E_dtype<T>(), pa.rows[s], np))
         return cudaErrorInvalidValue;
     p.km_nhw = pa.nhw;
     p.km_rows[0] = pa.rows[0];
     p.km_rows[1] = pa.rows[1];
-    tcx::panel_kernel<T, D><<<dim3(pa.nhw, a.B * a.Hkv), 128, 0, st>>>(pa);
+    tcx::offset_coef_kernel<<<16, 64, 0, st>>>(pa);
+    tcx::offset_panel_kernel<T, D><<<dim3(pa.nhw, a.B * a.Hkv), 128, 0, st>>>(pa);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -842,7 +874,7 @@ bool tc_fwd_supported(const FwdArgs& a, int dtype) {
 }
 
 size_t tc_fwd_workspace_bytes(const FwdArgs& a) {
-  return tcx::panel_bytes<tc::kM>(a.B, a.Hkv, a.Sk, a.D, a.theta, a.sm_scale);
+  return tcx::offset_panel_bytes<tc::kM>(a.B, a.Hkv, a.Sk, a.D, a.theta, a.sm_scale);
 }
 
 cudaError_t tc_fwd_launch(const FwdArgs& a, int dtype, cudaStream_t st, void* ws,

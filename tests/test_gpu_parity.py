@@ -531,8 +531,9 @@ def test_query_chunk_argument_checks():
                                               (128, 1, 5e5, False), (128, 2, 1e4, True)])
 def test_forward_panels_equal_in_kernel_builders(D, hkv, theta, bias):
     """The tensor-core forward with its scaled-key panels (written once per
-    call, loaded by TMA) and without them (built in every CTA) gets the same
-    operand bits, so O, M, L, A agree bit for bit."""
+    call, loaded by TMA; per-key-offset expansions) and without them (built in
+    every CTA; one expansion per window) agree: A bit for bit (the same gate
+    arithmetic), O, M, L within the expansions' truncation error."""
     from CoROPE import _lib
     B, H, S = 2, 4, 700
     (q, k, v, _), _ = inputs(B, H, S, D, 91, torch.bfloat16, hkv=hkv)
@@ -546,8 +547,11 @@ def test_forward_panels_equal_in_kernel_builders(D, hkv, theta, bias):
         outs.append((o, m, l, a))
     torch.cuda.synchronize()
     assert _lib.take_device_error() == 0
-    for x, y in zip(*outs):
-        assert torch.equal(x, y)
+    (o1, m1, l1, a1), (o2, m2, l2, a2) = outs
+    assert torch.equal(a1, a2)
+    assert maxabs(o1, o2) < 2e-2  # bf16 outputs: one ulp at |O| ~ 2 is 1.6e-2
+    assert maxabs(m1, m2) < 2e-2
+    assert ((l1 - l2).abs() / l2.abs()).max().item() < 2e-2
 
 
 @pytest.mark.parametrize("D", [64, 128])
