@@ -135,6 +135,8 @@ struct BwdArgs {
   float* dk32;   // [B,Hkv,Sk,D] fp32 accumulators (or the owner-major chunk
   float* dv32;   // layout, acc_chunk > 0: see accum_row)
   int acc_chunk; // 0, or the chunk rows C of the owner-major layout
+  float2* coef;  // tensor-core path: the dQ kernel's per-offset expansion
+                 // coefficients [16][16][64] (complex), written per call
 };
 
 // Row (in units of D elements) of key `key` of (b, kv head) `bhk` in the fp32

@@ -22,6 +22,7 @@ bool tc_bwd_supported(const BwdArgs& a, int dtype);
 cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* handoff,
                           size_t handoff_bytes, void* panels);
 size_t tc_bwd_panel_bytes(const BwdArgs& a);
+size_t tc_bwd_coef_bytes();
 bool tc_flash_supported(const FwdArgs& a, int dtype);
 cudaError_t tc_flash_launch(const FwdArgs& a, int dtype, bool causal, cudaStream_t st);
 int tcf_take_device_error();
@@ -177,12 +178,22 @@ static int fwd_common(const corope_fwd_params_t* p, corope_stream_t stream, bool
 
 static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
-// Minimum workspace: delta and lse rows, fp32 dk / dv accumulators (a query
-// chunk accumulates into the caller's dk_accum / dv_accum instead).
+// The tensor-core backward's expansion coefficients (tc_bwd_coef_bytes) when
+// that path can run for these parameters, else 0.
+static size_t bwd_coef_ws(const corope_bwd_params_t* p) {
+  if ((p->head_dim != 64 && p->head_dim != 128) || p->algo == COROPE_ALGO_EXACT ||
+      (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16))
+    return 0;
+  return align256(tc_bwd_coef_bytes());
+}
+
+// Minimum workspace: delta and lse rows, the tensor-core path's expansion
+// coefficients, fp32 dk / dv accumulators (a query chunk accumulates into the
+// caller's dk_accum / dv_accum instead).
 static size_t bwd_ws(const corope_bwd_params_t* p, bool chunk = false) {
   const size_t rows = (size_t)p->batch * p->heads * p->seq_len;
   const size_t kv = (size_t)p->batch * p->kv_heads * p->seq_len * p->head_dim;
-  return 2 * align256(rows * 4) + (chunk ? 0 : 2 * align256(kv * 4));
+  return 2 * align256(rows * 4) + bwd_coef_ws(p) + (chunk ? 0 : 2 * align256(kv * 4));
 }
 
 // Optional hand-off region after it (tensor-core backward only): the dQ
@@ -360,13 +371,15 @@ static int bwd_common(const corope_bwd_params_t* p, corope_stream_t stream,
   char* ws = static_cast<char*>(p->workspace);
   a.delta = reinterpret_cast<float*>(ws);
   a.lse = reinterpret_cast<float*>(ws + align256(rows * 4));
+  const size_t coef = bwd_coef_ws(p);
+  a.coef = coef ? reinterpret_cast<float2*>(ws + 2 * align256(rows * 4)) : nullptr;
   if (chunk) {
     a.dk32 = chunk->dk_accum;
     a.dv32 = chunk->dv_accum;
     a.acc_chunk = chunk->accum_chunk_rows;
   } else {
-    a.dk32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4));
-    a.dv32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4) + align256(kv * 4));
+    a.dk32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4) + coef);
+    a.dv32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4) + coef + align256(kv * 4));
   }
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

@@ -12,9 +12,10 @@
 // the process exits.  The caller still passes every input and output.
 //
 // Limits and rules:
-//   * the backward's scratch (two fp32 rows [B,H,S] plus fp32 dk/dv
-//     accumulators [B,Hkv,S,D]) must fit in 64 MiB, otherwise the call
-//     returns COROPE_ERR_WORKSPACE and does nothing;
+//   * the backward's scratch (two fp32 rows [B,H,S], the tensor-core path's
+//     128 KiB table of expansion coefficients, and fp32 dk/dv accumulators
+//     [B,Hkv,S,D]) must fit in 64 MiB, otherwise the call returns
+//     COROPE_ERR_WORKSPACE and does nothing;
 //   * the first call on each device looks up the array's device address with
 //     cudaGetSymbolAddress (with that device current) and caches it; make
 //     that first call before any stream capture;

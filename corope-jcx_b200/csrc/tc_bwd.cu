@@ -45,6 +45,7 @@
 // TMA/UMMA warpgroup 56 (2 x 176 + 104 + 56 = 4 x 128, the launch budget).
 // Every wait is bounded as in the forward.
 #include <cstring>
+#include <type_traits>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -74,6 +75,7 @@ using tcx::kLog2e;
 using tcx::kSmemLimit;
 using tcx::kW;
 using tcx::sigmoid_f;
+using tcx::bwd_slot_key;
 
 // Head dims 64 and 128.  Shared-memory tiles are always laid out for 128
 // (two 64-element slabs); with 64 the second slab of Q, dO and the A rows is
@@ -117,6 +119,7 @@ struct Params {
   int b_buf_bytes;
   int max_items;   // K^(m) item descriptors per builder thread
   int bop;         // shared-memory offset of the K^(m) buffers
+  float2* cf;           // dQ launch: per-offset expansion coefficients [16][16][64]
   uint8_t* handoff;     // dQ launch -> dK launch, per (b, h, query tile, window) block
   int64_t blocks_bh;    // hand-off blocks per (b, h)
   int bh0;              // first (b, h) of this launch (blockIdx.y counts from it)
@@ -138,8 +141,9 @@ template <int MODE, int KM> struct SmemTail {
   static constexpr int BAR = TH + NPX * 4;
   static constexpr int NBAR = 40;
   static constexpr int SLOT = BAR + NBAR * 8;
-  static constexpr int XCH = (SLOT + 16 + 15) & ~15;  // gate-gradient sums [half][group][128]
-  static constexpr int ITEMS = XCH + 2 * 2 * 128 * 4;  // then the K^(m) buffers at Params::bop
+  // gate-gradient key-pair sums of a window [group][128 rows] x float4
+  static constexpr int XCH = (SLOT + 16 + 15) & ~15;
+  static constexpr int ITEMS = XCH + 2 * 128 * 16;  // then the K^(m) buffers at Params::bop
 };
 
 // tensor memory columns (GW = 8 KM: one G half, terms x keys)
@@ -162,8 +166,8 @@ template <int KM> struct TK {  // recompute dK launch
 // Hand-off block (one per (b, h, query tile, window), 128 rows x 16 keys):
 // dl = P (dP - delta) of each (row, key) as f16, which the dK launch needs,
 // with the in-window positions u (recomputed there from the gates), to
-// rebuild Y_m = dl T_m(u).  Quad q = 2 * half + row group holds keys
-// 8 half + 4 group + 0..3, 8 bytes per row.
+// rebuild Y_m = dl T_m(u).  Quad q = 2 * half + row group holds the keys in
+// slots 4 group + 0..3 of the half (tcx::bwd_slot_key), 8 bytes per row.
 constexpr int kHB = 4 * 128 * 8;
 // dl -> f16 pair, saturated at the largest finite f16 (NaN stays NaN)
 __device__ __forceinline__ uint32_t pack_dl(float a, float b) {
@@ -192,7 +196,9 @@ __device__ __forceinline__ float rcp_approx(float x) {
 __device__ __forceinline__ float gate_sigmoid(float s) {
   return rcp_approx(__fadd_rn(1.0f, ex2_approx(__fmul_rn(s, -kLog2e))));
 }
-template <bool MASKED>
+// PER_OFFSET (dQ launch with panels): each key offset's own expansion,
+// u_j = (sum_{i>j} z_i) / c_j - 1 (tcx::offset_halfwidth).
+template <bool MASKED, bool PER_OFFSET = false>
 __device__ __forceinline__ float window_gates(const uint32_t (&sraw)[16], int j0, int t,
                                               bool row_ok, float (&z)[16], float (&uu)[16]) {
 #pragma unroll
@@ -203,7 +209,7 @@ __device__ __forceinline__ float window_gates(const uint32_t (&sraw)[16], int j0
   float suf = 0.f;  // in-window suffix after key jj
 #pragma unroll
   for (int jj = 15; jj >= 0; --jj) {
-    uu[jj] = __fmaf_rn(suf, 1.0f / kC0, -1.0f);
+    uu[jj] = __fmaf_rn(suf, PER_OFFSET ? tcx::offset_inv_halfwidth(16, jj) : 1.0f / kC0, -1.0f);
     suf = __fadd_rn(suf, z[jj]);
   }
   return suf;
@@ -238,7 +244,7 @@ enum {
   B_XF = 25, B_XFREE = 26, B_YTFREE = 27,        // dQ launch
   B_CF = 28, B_CE = 30, B_YFREE = 32,            // dK launch: [half] x 2
   B_DRAIN11 = 33, B_DRAIN5 = 34, B_DRAIN6 = 35,
-  B_XCH = 36,                                    // [half]
+  B_XCH = 36,                                    // gate-gradient pair sums (dQ launch)
   B_CF2 = 38, B_CE2 = 39                         // dQ launch: dV / dK_gate GEMMs
 };
 
@@ -274,6 +280,13 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
   // gate/dP accumulators: double-buffered in the dQ launch, single in the dK
   // launch (its tensor memory holds the A operand and two C regions)
   constexpr int NSD = MODE == MODE_DQ ? tq::NSD : 1;
+  // the dQ launch uses the per-offset expansions (tcx::offset_terms): key
+  // pairs of window keys 0..7 run 16 terms, those of keys 8..15 eleven (the
+  // larger count of their keys), in both halves (tcx::bwd_slot_key); the
+  // recompute dK launch one expansion per window
+  constexpr bool POFF = MODE == MODE_DQ;
+  constexpr int NPT0 = kM, NPT1 = POFF ? 11 : kM;
+  static_assert(!POFF || (tcx::offset_terms(16, 8) <= NPT1 && kM == 16), "pair term counts");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -604,9 +617,15 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           for (int q = 0; q < 7; ++q)
             if (it >= item_end[q]) { s2 = q + 1; base = item_end[q]; }
           const int local = it - base;
-          const int r = local >> 1, c = 2 * s2 + (local & 1), m = r >> 3, j = r & 7;
-          const uint32_t kofs = (c >> 3) * 2048 + j * 128 + (((c & 7) ^ j) << 4);
-          const uint32_t cofs = (m * NPX + 4 * c) * 4;
+          // key row of half 0 (bwd_slot_key(0, slot) & 7 < 4: half 1's row is
+          // 4 further, with its swizzled chunk index's bit 2 flipped)
+          const int r = local >> 1, c = 2 * s2 + (local & 1), m = r >> 3, j = bwd_slot_key(0, r & 7);
+          const uint32_t kofs = (c >> 3) * 2048 + j * 128 + (((c & 7) ^ (j & 7)) << 4);
+          // dQ launch: the per-offset complex coefficients of half 0's key
+          // (P.cf, float2 index; half 1's key is 4 further: + 4 * 16 * 64);
+          // dK launch: the window expansion's coefficient quad in shared memory
+          const uint32_t cofs = MODE == MODE_DQ ? (uint32_t)((j * kMB + m) * 64 + 4 * c)
+                                                : (uint32_t)((m * NPX + 4 * c) * 4);
           const uint32_t bofs = P.b_slab_off[c >> 3] + sw128_offset(r, c & 7);
           const uint32_t flags = (m & 1) | ((m & 2) ? 2u : 0u) | (((m + 1) & 2) ? 4u : 0u);
           d = make_uint2(kofs | (cofs << 16), bofs | (flags << 16));
@@ -644,23 +663,38 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       for (int hh = 0; hh < 2; ++hh) {
         if (use > 0 && !wwait(bars[B_BE + 2 * hh + buf], (use - 1) & 1, err, kErrBEmpty))
           return false;
-        const uint32_t kt = sK + st * NS * 2048 + hh * 1024;
+        const uint32_t kt = sK + st * NS * 2048;
         const uint32_t bt = sB + (hh * nb + buf) * P.b_buf_bytes;
 #pragma unroll 1
         for (int i0 = 0; i0 < my_n; i0 += 4) {
           uint2 d[4];
           uint4 kv[4];
-          float4 cf[4];
+          float4 cf[4], cg[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) d[j] = items[(i0 + j < kMaxItems ? i0 + j : 0) * 128 + gt];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            kv[j] = lds128(kt + (d[j].x & 0xffffu));
-            cf[j] = lds128f(s_coef_u + (d[j].x >> 16));
+            const uint32_t ko = d[j].x & 0xffffu;
+            kv[j] = lds128(kt + (hh ? ((ko + 512u) ^ 64u) : ko));
+            if (MODE == MODE_DQ) {
+              const float4* cp =
+                  reinterpret_cast<const float4*>(P.cf + (d[j].x >> 16) + hh * 4 * kMB * 64);
+              cf[j] = __ldg(cp);
+              cg[j] = __ldg(cp + 1);
+            } else {
+              cf[j] = lds128f(s_coef_u + (d[j].x >> 16));
+            }
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            if (i0 + j < my_n) {
+            if (MODE == MODE_DQ && i0 + j < my_n) {
+              // per-offset expansions: the same arithmetic as the panel kernel
+              sts128(bt + (d[j].y & 0xffffu),
+                     make_uint4(tcx::cmul_pack<E>(kv[j].x, cf[j].x, cf[j].y),
+                                tcx::cmul_pack<E>(kv[j].y, cf[j].z, cf[j].w),
+                                tcx::cmul_pack<E>(kv[j].z, cg[j].x, cg[j].y),
+                                tcx::cmul_pack<E>(kv[j].w, cg[j].z, cg[j].w)));
+            } else if (i0 + j < my_n) {
               // (-i)^m: odd terms swap the pair's components (one byte
               // permute), terms 2, 3 mod 4 negate one or both (a sign-bit xor)
               const uint32_t fl = d[j].y >> 16;
@@ -718,11 +752,14 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         mbar_arrive(&bars[B_CE + hh]);
       }
       const int d = gt;
-      // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys)
+      // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys);
+      // column 8 hh + s of C^T is slot s of half hh
       float* row0 = P.dk32 + accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + d;
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (w * kW + j < P.Sk && d < D) atomicAdd(row0 + j * D, dk[j]);
+      for (int j = 0; j < 16; ++j) {
+        const int key = bwd_slot_key(j >> 3, j & 7);
+        if (w * kW + key < P.Sk && d < D) atomicAdd(row0 + key * D, dk[j]);
+      }
       return true;
     };
 
@@ -778,9 +815,16 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     // compensated gate prefix through the current window (advance_prefix)
     float base = 0.f, base_c = 0.f;
     float carry = 0.f;   // gate sum of the keys after the current window
-    float da_run = 0.f;  // gate-gradient prefix before the current half
-    // this group's keys of the window: i -> key 8 (i >> 2) + 4 rg + (i & 3)
+    float da_run = 0.f;  // gate-gradient prefix before the current window
+    // this group's keys of the window: slot 4 rg + (i & 3) of half i >> 2, i.e.
+    // key 4 (i >> 2) + 2 rg + (i & 1) + 8 ((i >> 1) & 1) (tcx::bwd_slot_key)
     float zo[8], uo[8], dpo[8];
+    // d(position) scale of each key: ln 2 / the expansion's half-width
+    float dac[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      dac[i] = POFF ? kLn2 * tcx::offset_inv_halfwidth(16, bwd_slot_key(i >> 2, 4 * rg + (i & 3)))
+                    : kLn2 / kC0;
     uint32_t csc[PW];    // dQ: (cos, sin) as f16 pairs for this group's pairs
     bool ok = wwait(bars[B_Q], 0, err, kErrQ);
 
@@ -789,27 +833,26 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       const int sb = w % NSD;
       if (!wwait(bars[B_SDF + sb], (w / NSD) & 1, err, kErrSd)) return false;
       tc_fence_after();
-      uint32_t sraw[16], d4a[4], d4b[4];
+      uint32_t sraw[16], dp[8];
       tmem_ld16(lane_base + T_SG0 + 16 * sb, sraw);
-      tmem_ld4(lane_base + T_DP0 + 16 * sb + 4 * rg, d4a);
-      tmem_ld4(lane_base + T_DP0 + 16 * sb + 8 + 4 * rg, d4b);
+      // dP of this group's key pairs: half q >> 1, keys 0..7 (q even) or 8..15
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        tmem_ld2(lane_base + T_DP0 + 16 * sb + 4 * (q >> 1) + 2 * rg + 8 * (q & 1), dp[2 * q],
+                 dp[2 * q + 1]);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&bars[B_SDE + sb]);
       const int j0 = w * kW;
       float z[16], uu[16];
-      const float zsum = diag_window(w) ? window_gates<true>(sraw, j0, t, row_ok, z, uu)
-                                        : window_gates<false>(sraw, j0, t, row_ok, z, uu);
+      const float zsum = diag_window(w) ? window_gates<true, POFF>(sraw, j0, t, row_ok, z, uu)
+                                        : window_gates<false, POFF>(sraw, j0, t, row_ok, z, uu);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int kk = 8 * (i >> 2) + (i & 3);
-        zo[i] = rg ? z[kk + 4] : z[kk];
-        uo[i] = rg ? uu[kk + 4] : uu[kk];
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        dpo[i] = __uint_as_float(d4a[i]);
-        dpo[4 + i] = __uint_as_float(d4b[i]);
+        const int k0 = bwd_slot_key(i >> 2, i & 3);  // group 0's key; group 1's is 2 further
+        zo[i] = rg ? z[k0 + 2] : z[k0];
+        uo[i] = rg ? uu[k0 + 2] : uu[k0];
+        dpo[i] = __uint_as_float(dp[i]);
       }
       carry = advance_prefix(zsum, A_t, base, base_c);
       return true;
@@ -889,7 +932,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
     // their derivative in u.  G columns: 16 c + 8 (m & 1) + key, m = 2 c + (m & 1).
     // All 14 loads are issued before the single wait, after which the G
     // region is released to the next half's GEMM.
+    // key pair j runs NPT[j] terms (the chain starts at its first nonzero term)
     auto clenshaw = [&](const float (&uj)[4], float (&f)[4], float (&fd)[4]) {
+      constexpr int NPT[2] = {NPT0, NPT1};
       uint32_t g[kM / 2][2][4];
 #pragma unroll
       for (int c = 0; c < kM / 2; ++c) {
@@ -914,6 +959,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       for (int m = kM - 1; m >= 0; --m) {
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
+          if (m >= NPT[j]) continue;
           const float2 a = make_float2(__uint_as_float(g[m >> 1][m & 1][2 * j]),
                                        __uint_as_float(g[m >> 1][m & 1][2 * j + 1]));
           const float2 t = __ffma2_rn(neg1, b2[j], a);
@@ -940,6 +986,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
             : nullptr;
     auto halves = [&](int w) -> bool {
       const int j0 = w * kW;
+      float da0[4];  // half A's gate gradients, kept for the window's prefix
       uint8_t* const hblk = hblk0 ? hblk0 + (int64_t)w * kHB : nullptr;
       if (MODE == MODE_DK) {
         // the previous window's C GEMMs are done with the A rows and the Y
@@ -973,36 +1020,31 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         float f[4], fd[4];
         clenshaw(uj, f, fd);
         float dl[4], da[4], pr[4];
-        float sum4 = 0.f;
         if (diag_window(w)) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int kj = j0 + 8 * hh + 4 * rg + i;
+            const int kj = j0 + 4 * hh + 2 * rg + (i & 1) + 8 * (i >> 1);
             const bool valid = row_ok && kj <= t;
             float lg = f[i];
             if (HAS_BIAS && valid) lg = fmaf(P.bias[(int64_t)t * P.bias_rs + kj], kLog2e, lg);
             pr[i] = valid ? exp2f(lg - lse2) : 0.f;
             dl[i] = pr[i] * (dpj[i] - delta);
-            da[i] = valid ? dl[i] * (kLn2 / kC0) * fd[i] : 0.f;
-            sum4 += da[i];
+            da[i] = valid ? dl[i] * (hh ? dac[4 + i] : dac[i]) * fd[i] : 0.f;
           }
         } else {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int kj = j0 + 8 * hh + 4 * rg + i;
+            const int kj = j0 + 4 * hh + 2 * rg + (i & 1) + 8 * (i >> 1);
             float lg = f[i];
             if (HAS_BIAS) lg = fmaf(P.bias[(int64_t)t * P.bias_rs + kj], kLog2e, lg);
             pr[i] = exp2f(lg - lse2);
             dl[i] = pr[i] * (dpj[i] - delta);
-            da[i] = dl[i] * (kLn2 / kC0) * fd[i];
-            sum4 += da[i];
+            da[i] = dl[i] * (hh ? dac[4 + i] : dac[i]) * fd[i];
           }
         }
-        // publish this group's sum for the partner group (the dK launch
-        // needs no gate gradient)
-        if (MODE == MODE_DQ) {
-          sts32f(s_xch + ((hh * 2 + rg) * 128 + r) * 4, sum4);
-          mbar_arrive(&bars[B_XCH + hh]);
+        if (hh == 0) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) da0[i] = da[i];  // for the window's prefix after half B
         }
         // Y_m = dl T_m(u), packed per term for the group's 4 keys (dQ launch:
         // times ln 2, the base of the logits, so that X and the dq fold carry it)
@@ -1019,6 +1061,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           y[1][jp] = E::pack(ya1, yb1);
 #pragma unroll
           for (int m = 2; m < kM; ++m) {
+            if (m >= (jp ? NPT1 : NPT0)) break;  // the X GEMM's K^(m) rows there are zero
             const float ya2 = fmaf(ua, ya1, -ya0), yb2 = fmaf(ub, yb1, -yb0);
             ya0 = ya1; ya1 = ya2; yb0 = yb1; yb1 = yb2;
             y[m][jp] = E::pack(ya2, yb2);
@@ -1032,16 +1075,21 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           if (hh == 1 && !wwait(bars[B_YDONE], w & 1, err, kErrX)) return false;
           tc_fence_after();
 #pragma unroll
-          for (int m = 0; m < kM; ++m) tmem_st2(lane_base + tq::YT + 4 * m + 2 * rg, y[m][0], y[m][1]);
+          for (int m = 0; m < NPT0; ++m) {
+            if (m < NPT1)
+              tmem_st2(lane_base + tq::YT + 4 * m + 2 * rg, y[m][0], y[m][1]);
+            else
+              tmem_st1(lane_base + tq::YT + 4 * m + 2 * rg, y[m][0]);
+          }
           if (hh == 0) {
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&bars[B_YA]);
           }
-          // P -> chunk 4 + hh of the P | dS rows (B operand of dV^T); the
-          // previous window's GEMMs are done with them (B_YTFREE above)
-          sts64(sDS + sw128_offset(r, 4 + hh) + 8 * rg, E::pack(pr[0], pr[1]),
-                E::pack(pr[2], pr[3]));
+          // P -> chunks 4, 5 of the P | dS rows (B operand of dV^T; keys in
+          // order); the previous window's GEMMs are done with them (B_YTFREE above)
+          sts32(sDS + sw128_offset(r, 4) + 2 * (4 * hh + 2 * rg), E::pack(pr[0], pr[1]));
+          sts32(sDS + sw128_offset(r, 5) + 2 * (4 * hh + 2 * rg), E::pack(pr[2], pr[3]));
         } else {
           // Y rows into shared memory (B operand of the C GEMMs)
           if (hh == 1 && !wwait(bars[B_YDONE], w & 1, err, kErrY)) return false;
@@ -1052,32 +1100,45 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           mbar_arrive(&bars[hh ? B_YB : B_YA]);
         }
         if (MODE == MODE_DK) continue;
-        // gate-gradient prefix: group 0's keys precede group 1's in the half
-        if (!wwait(bars[B_XCH + hh], w & 1, err, kErrXch)) return false;
-        const float other = lds32f(s_xch + ((hh * 2 + (rg ^ 1)) * 128 + r) * 4);
-        float run = da_run + (rg ? other : 0.f);
-        float ds[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          ds[i] = run * zj[i] * (1.f - zj[i]);
-          run += da[i];
-        }
-        da_run += sum4 + other;
         if (hblk) {
           const int qd = 2 * hh + rg;
           *reinterpret_cast<uint2*>(hblk + (qd * 128 + r) * 8) =
               make_uint2(pack_dl(dl[0], dl[1]), pack_dl(dl[2], dl[3]));
         }
-        // dS -> chunk 6 + hh of the P | dS rows (A operand of dq += dS K,
-        // B operand of dK_gate^T); half B completes the window's rows
-        sts64(sDS + sw128_offset(r, 6 + hh) + 8 * rg, E::pack(ds[0], ds[1]),
-              E::pack(ds[2], ds[3]));
-        if (hh == 1) {
-          fence_async_smem();
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(&bars[B_YB]);
+        if (hh == 0) continue;
+        // Gate-gradient prefix over the window's keys in order.  Key pair p
+        // (keys 2p, 2p + 1) belongs to group p & 1; this group's pairs in
+        // window order are (half 0, keys 0..7), (half 1, 0..7), (half 0,
+        // 8..15), (half 1, 8..15).  Each group publishes its four pair sums.
+        const float ps[4] = {da0[0] + da0[1], da[0] + da[1], da0[2] + da0[3], da[2] + da[3]};
+        sts128f(s_xch + (rg * 128 + r) * 16, make_float4(ps[0], ps[1], ps[2], ps[3]));
+        mbar_arrive(&bars[B_XCH]);
+        if (!wwait(bars[B_XCH], w & 1, err, kErrXch)) return false;
+        const float4 o4 = lds128f(s_xch + ((rg ^ 1) * 128 + r) * 16);
+        const float os[4] = {o4.x, o4.y, o4.z, o4.w};
+        const float dak[4][2] = {{da0[0], da0[1]}, {da[0], da[1]}, {da0[2], da0[3]}, {da[2], da[3]}};
+        const float zk[4][2] = {{zo[0], zo[1]}, {zo[4], zo[5]}, {zo[2], zo[3]}, {zo[6], zo[7]}};
+        float ds[4][2];
+        float run = da_run;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float pre = run + (rg ? os[k] : 0.f);  // group 1's pair follows group 0's
+          ds[k][0] = pre * zk[k][0] * (1.f - zk[k][0]);
+          pre += dak[k][0];
+          ds[k][1] = pre * zk[k][1] * (1.f - zk[k][1]);
+          run += ps[k] + os[k];
         }
+        da_run = run;
+        // dS -> chunks 6, 7 of the P | dS rows (A operand of dq += dS K,
+        // B operand of dK_gate^T); this completes the window's rows
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          sts32(sDS + sw128_offset(r, 6 + (k >> 1)) + 2 * (4 * (k & 1) + 2 * rg),
+                E::pack(ds[k][0], ds[k][1]));
+        fence_async_smem();
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bars[B_YB]);
       }
       return true;
     };
@@ -1116,6 +1177,15 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       return true;
     };
 
+    if (POFF) {
+      // the Y columns of terms a key pair does not run are never written:
+      // they must hold finite values (zeros) for the X GEMM, whose K^(m) rows
+      // there are zero
+      tc_fence_after();
+#pragma unroll
+      for (int m = NPT1; m < NPT0; ++m) tmem_st1(lane_base + tq::YT + 4 * m + 2 * rg + 1, 0u);
+      tmem_wait_st();
+    }
     if (ok) ok = gates(0);
     if (ok) {
       build_a();
@@ -1407,11 +1477,14 @@ __global__ void __launch_bounds__(kThreads, 1) dk3_kernel(const __grid_constant_
       }
       tc_fence_before();
       mbar_arrive(&bars[k3::B_CE + bf]);
-      // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys)
+      // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys);
+      // dk[8 hh + s] belongs to slot s of half hh
       float* row0 = P.dk32 + accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + gt;
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (w * kW + j < P.Sk && gt < D) atomicAdd(row0 + j * D, dk[j]);
+      for (int j = 0; j < 16; ++j) {
+        const int key = bwd_slot_key(j >> 3, j & 7);
+        if (w * kW + key < P.Sk && gt < D) atomicAdd(row0 + key * D, dk[j]);
+      }
     }
     __syncwarp();
     regs_inc<128>();
@@ -1459,9 +1532,9 @@ __global__ void __launch_bounds__(kThreads, 1) dk3_kernel(const __grid_constant_
                                           : window_gates<false>(sraw, w * kW, t, row_ok, z, uu);
         carry = advance_prefix(zsum, A_t, base, base_c);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int kk = 8 * (i >> 2) + (i & 3);
-          uo[i] = rg ? uu[kk + 4] : uu[kk];
+        for (int i = 0; i < 8; ++i) {  // slot 4 rg + (i & 3) of half i >> 2
+          const int k0 = bwd_slot_key(i >> 2, i & 3);
+          uo[i] = rg ? uu[k0 + 2] : uu[k0];
         }
       }
       // ---- A rows of this group's slab into buffer w & 1
@@ -1587,6 +1660,8 @@ static cudaError_t launch_mode(Params& p, bool bias, int S, int nbh, cudaStream_
                                float theta, float sm_scale) {
   constexpr int KM = kMB;
   tcx::fill_coefficients<KM>(p.coef, p.nrow, D, theta, sm_scale);
+  if (MODE == MODE_DQ)  // the per-offset expansions' K extents
+    tcx::fill_offset_rows<KM>(p.nrow, D, theta);
   const int smem = plan<MODE, KM>(p);
   if (smem > kSmemLimit) return cudaErrorInvalidValue;
   dim3 grid((S + kBM - 1) / kBM, nbh);
@@ -1629,24 +1704,26 @@ template <typename T> constexpr int E_dtype() {
   return ElemTraits<T>::kBf16 ? COROPE_DTYPE_BF16 : COROPE_DTYPE_F16;
 }
 
-// Write the dQ launch's K^(m) panels (all Sk keys, 16 terms) into `panels`
-// and point the tensor maps at them.
+// Write the dQ launch's K^(m) panels (all Sk keys, the 16-term backward's
+// per-offset expansions in its key order) into `panels` and point the
+// tensor maps at them.
 template <typename T, int D>
 static cudaError_t make_panels(Params& p, const BwdArgs& a, void* panels, cudaStream_t st) {
-  static tcx::PanelArgs pa;  // guarded by the caller's lock
-  tcx::panel_bytes<kMB>(a.B, a.Hkv, a.Sk, D, a.theta, a.sm_scale, &pa);
+  static tcx::OffsetPanelArgs pa;  // guarded by the caller's lock
+  tcx::offset_panel_bytes<kMB>(a.B, a.Hkv, a.Sk, D, a.theta, a.sm_scale, &pa, true, false);
   const int64_t np = tcx::panel_count(a.B, a.Hkv, a.Sk);
   pa.k = a.k;
   for (int i = 0; i < 3; ++i) pa.ks[i] = a.ks[i];
   pa.out[0] = panels;
   pa.out[1] = static_cast<uint8_t*>(panels) + np * pa.rows[0] * 128;
+  pa.cf = a.coef;  // written by tc_bwd_launch
   for (int s = 0; s < D / 64; ++s)
     if (!tcx::encode_panels(&p.tm_km[s], pa.out[s], E_dtype<T>(), pa.rows[s], np))
       return cudaErrorInvalidValue;
   p.km_nhw = pa.nhw;
   p.km_rows[0] = pa.rows[0];
   p.km_rows[1] = pa.rows[1];
-  tcx::panel_kernel<T, D><<<dim3(pa.nhw, a.B * a.Hkv), 128, 0, st>>>(pa);
+  tcx::offset_panel_kernel<T, D><<<dim3(pa.nhw, a.B * a.Hkv), 128, 0, st>>>(pa);
   return cudaGetLastError();
 }
 
@@ -1710,7 +1787,11 @@ bool tc_bwd_supported(const BwdArgs& a, int dtype) {
 // dQ launch's per-pair results (slice by slice through the region); otherwise
 // it recomputes them.
 size_t tc_bwd_panel_bytes(const BwdArgs& a) {
-  return tcx::panel_bytes<tcb::kMB>(a.B, a.Hkv, a.Sk, a.D, a.theta, a.sm_scale);
+  return tcx::offset_panel_bytes<tcb::kMB>(a.B, a.Hkv, a.Sk, a.D, a.theta, a.sm_scale, nullptr,
+                                           true, false);
+}
+
+size_t tc_bwd_coef_bytes() { return tcx::kOffsetCoefBytes;
 }
 
 cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* handoff,
@@ -1725,6 +1806,14 @@ cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* ha
       !tcx::encode(&p.tm_k, a.k, dtype, a.B, a.Hkv, a.Sk, a.D, a.ks, kKT) ||
       !tcx::encode(&p.tm_v, a.v, dtype, a.B, a.Hkv, a.Sk, a.D, a.vs, kKT))
     return cudaErrorInvalidValue;
+  if (!a.coef) return cudaErrorInvalidValue;  // the dQ kernel's coefficients (minimum workspace)
+  {
+    tcx::OffsetPanelArgs ca;
+    tcx::offset_panel_bytes<kMB>(a.B, a.Hkv, a.Sk, a.D, a.theta, a.sm_scale, &ca, true, false);
+    ca.cf = a.coef;
+    tcx::offset_coef_kernel<<<16, 64, 0, st>>>(ca);
+  }
+  p.cf = a.coef;
   p.r0 = a.r0;
   p.Sk = a.Sk;
   p.dq = a.dq;

@@ -52,6 +52,15 @@ __host__ __device__ constexpr float offset_halfwidth(int km, int o) {
 __host__ __device__ constexpr float offset_inv_halfwidth(int km, int o) {
   return offset_halfwidth(km, o) > 0.f ? 1.0f / offset_halfwidth(km, o) : 0.f;
 }
+// The backward's key slots: slot s of half hh holds window key
+// bwd_slot_key(hh, s) = (s & 1) + 2 (s >> 2) + 4 hh + 8 ((s >> 1) & 1), so row
+// group g takes key pairs (4 hh + 2 g, +1) and (8 + 4 hh + 2 g, +1): both
+// halves of a window see the same offsets' term counts (the pairs of keys
+// 0..7 and of keys 8..15), one instance of the per-pair code serves both.
+__host__ __device__ constexpr int bwd_slot_key(int hh, int s) {
+  return (s & 1) + 2 * (s >> 2) + 4 * hh + 8 * ((s >> 1) & 1);
+}
+
 // Terms a row group runs for position j (0..3) of half hh: the larger count
 // of the two groups' keys there (the smaller one's extra terms are zero).
 __host__ __device__ constexpr int position_terms(int km, int hh, int j) {
@@ -353,6 +362,7 @@ struct OffsetPanelArgs {
   void* out[2];     // slab panels
   float2* cf;       // [16][kPanelTerms][64] complex coefficients
   int km;           // most terms of any offset
+  int bwd_order;    // key slots: tcx::bwd_slot_key (else 8 hh + slot_key)
   float scale;      // sm_scale * log2(e)
   double th[64];    // theta_p
 };
@@ -382,6 +392,15 @@ __device__ inline void bessel_j_all(double x, int n, double* out) {
   for (int m = 0; m < n; ++m) out[m] *= inv;
 }
 
+// The scaled key of one pair: (k_lo + i k_hi) (cr + i ci), rounded once to
+// the 16-bit type; the panel kernel and the dQ kernel's builders share it so
+// that both give the same bits.
+template <typename E>
+__device__ __forceinline__ uint32_t cmul_pack(uint32_t kw, float cr, float ci) {
+  const float kl = E::lo(kw), kh = E::hi(kw);
+  return E::pack(__fmaf_rn(kl, cr, __fmul_rn(-kh, ci)), __fmaf_rn(kl, ci, __fmul_rn(kh, cr)));
+}
+
 // One thread per (offset o = blockIdx.x, pair p = threadIdx.x).
 static __global__ void __launch_bounds__(64) offset_coef_kernel(const __grid_constant__ OffsetPanelArgs A) {
   const int o = blockIdx.x, p = threadIdx.x;
@@ -406,40 +425,34 @@ static __global__ void __launch_bounds__(64) offset_coef_kernel(const __grid_con
 }
 
 // Row r of K step s (16 elements = two 16-byte chunks) of half window hw
-// holds term m = r / 8 of the key in slot r % 8 (key slot_key(r % 8) of the
-// half): its complex coefficient times the key's pair.  Rows a K step does not
-// read (past nrow[s]) and keys past S are zero.
+// holds term m = r / 8 of the key in slot r % 8 (window key 8 (hw & 1) +
+// slot_key(r % 8), or bwd_slot_key(hw & 1, r % 8) in the backward's order):
+// its complex coefficient times the key's pair.  Rows a K step does not read
+// (past nrow[s]) and keys past S are zero.
 template <typename T, int D>
 __global__ void __launch_bounds__(128) offset_panel_kernel(const __grid_constant__ OffsetPanelArgs A) {
   using E = ElemTraits<T>;
   const int hw = blockIdx.x, bh = blockIdx.y;
   const int b = bh / A.Hkv, hk = bh % A.Hkv;
   const T* kb = static_cast<const T*>(A.k) + b * A.ks[0] + hk * A.ks[1];
-  const int o0 = 8 * (hw & 1);  // window offset of the half's first key
+  const int hh = hw & 1;
 #pragma unroll
   for (int s = 0; s < D / 64; ++s) {
     const int rows = A.rows[s];
     uint4* out = static_cast<uint4*>(A.out[s]) + ((int64_t)bh * A.nhw + hw) * rows * 8;
     for (int it = threadIdx.x; it < rows * 8; it += 128) {
       const int r = it >> 3, c = it & 7, m = r >> 3, slot = r & 7;
-      const int kk = slot_key(slot);
-      const int key = 8 * hw + kk;
+      const int kk = A.bwd_order ? bwd_slot_key(hh, slot) : 8 * hh + slot_key(slot);  // window offset
+      const int key = 16 * (hw >> 1) + kk;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (r < A.nrow[4 * s + (c >> 1)] && key < A.S && m < kPanelTerms) {
         const uint4 kv =
             *reinterpret_cast<const uint4*>(kb + (int64_t)key * A.ks[2] + 64 * s + 8 * c);
         const float4* cp = reinterpret_cast<const float4*>(
-            A.cf + ((size_t)(o0 + kk) * kPanelTerms + m) * 64 + 32 * s + 4 * c);
+            A.cf + ((size_t)kk * kPanelTerms + m) * 64 + 32 * s + 4 * c);
         const float4 c01 = __ldg(cp), c23 = __ldg(cp + 1);
-        const float cr[4] = {c01.x, c01.z, c23.x, c23.z}, ci[4] = {c01.y, c01.w, c23.y, c23.w};
-        const uint32_t in[4] = {kv.x, kv.y, kv.z, kv.w};
-        uint32_t ov[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float kl = E::lo(in[e]), kh = E::hi(in[e]);
-          ov[e] = E::pack(kl * cr[e] - kh * ci[e], kl * ci[e] + kh * cr[e]);
-        }
-        v = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+        v = make_uint4(cmul_pack<E>(kv.x, c01.x, c01.y), cmul_pack<E>(kv.y, c01.z, c01.w),
+                       cmul_pack<E>(kv.z, c23.x, c23.y), cmul_pack<E>(kv.w, c23.z, c23.w));
       }
       out[it] = v;
     }
@@ -448,10 +461,11 @@ __global__ void __launch_bounds__(128) offset_panel_kernel(const __grid_constant
 
 // Fill the arguments of the per-offset panels (KM: most terms of any
 // offset) and return the workspace bytes they take: both slabs' panels, then
-// the coefficient table (0 when the head dim has none).
+// (own_table) the coefficient table (0 when the head dim has none).
 template <int KM>
 inline size_t offset_panel_bytes(int B, int Hkv, int S, int D, float theta, float sm_scale,
-                                 OffsetPanelArgs* a = nullptr) {
+                                 OffsetPanelArgs* a = nullptr, bool bwd_order = false,
+                                 bool own_table = true) {
   OffsetPanelArgs local;
   OffsetPanelArgs& p = a ? *a : local;
   std::memset(&p, 0, sizeof(p));
@@ -461,11 +475,12 @@ inline size_t offset_panel_bytes(int B, int Hkv, int S, int D, float theta, floa
   p.B = B; p.Hkv = Hkv; p.S = S;
   p.nhw = 2 * ((S + kW - 1) / kW);
   p.km = KM;
+  p.bwd_order = bwd_order ? 1 : 0;
   p.scale = sm_scale * kLog2e;
   for (int q = 0; q < 64; ++q)
     p.th[q] = q < D / 2 ? 1.0 / std::pow((double)theta, (double)(2 * q) / (double)D) : 0.0;
   const size_t panels = (size_t)panel_count(B, Hkv, S) * (p.rows[0] + p.rows[1]) * 128;
-  return panels > 0 ? panels + kOffsetCoefBytes : 0;
+  return panels > 0 ? panels + (own_table ? kOffsetCoefBytes : 0) : 0;
 }
 
 }  // namespace tcx

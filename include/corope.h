@@ -124,8 +124,10 @@ int corope_mqa_fwd(const corope_fwd_params_t *p, corope_stream_t stream);
  * slice, or not at all). */
 size_t corope_bwd_workspace_bytes(const corope_bwd_params_t *p);
 
-/* Smallest workspace corope_bwd accepts (the dK kernel then recomputes the
- * per-(row, key) results).  No counterpart in the reference. */
+/* Smallest workspace corope_bwd accepts: delta and lse rows, the tensor-core
+ * path's expansion coefficients (128 KiB, written per call) and fp32 dk / dv
+ * accumulators (the dK kernel then recomputes the per-(row, key) results).
+ * No counterpart in the reference. */
 size_t corope_bwd_min_workspace_bytes(const corope_bwd_params_t *p);
 
 /* Part of corope_bwd_workspace_bytes() holding the dQ kernel's scaled-key

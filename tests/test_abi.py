@@ -174,14 +174,15 @@ def test_chunk_argument_checks_without_gpu():
     c.q_row0, c.kv_len = 256, 512
     assert lib.corope_bwd_chunk(ctypes.byref(b), ctypes.byref(c), None) == _lib.ERR_INVALID
     assert b"dk_accum" in lib.corope_last_error()
-    # the chunk workspace holds delta / lse rows, the scaled-key panels of all
-    # kv_len keys and the chunk's hand-off
+    # the chunk workspace holds delta / lse rows and the dQ kernel's expansion
+    # coefficients (16 offsets x 16 terms x 64 pairs, complex fp32), the
+    # scaled-key panels of all kv_len keys and the chunk's hand-off
     lo = lib.corope_bwd_chunk_min_workspace_bytes(ctypes.byref(b), ctypes.byref(c))
     hi = lib.corope_bwd_chunk_workspace_bytes(ctypes.byref(b), ctypes.byref(c))
     keys = _lib.BwdParams.from_buffer_copy(b)
     keys.seq_len = 512
     panels = lib.corope_bwd_panel_bytes(ctypes.byref(keys))
-    assert lo == 2 * 4 * 128 * 4 and panels > 0
+    assert lo == 2 * 4 * 128 * 4 + 16 * 16 * 64 * 8 and panels > 0
     assert hi - lo - panels == 4 * ((256 + 127) // 16 + 1) * 4096
 
 
