@@ -1430,6 +1430,9 @@ __global__ void __launch_bounds__(kThreads, 1) dk3_kernel(const __grid_constant_
           case 2: sgn = -1.f; break;
           default: sgn = e ? -1.f : 1.f; break;
         }
+        // the rows store V_m = s_m Y_m with s_m = -1 for m = 2, 3 mod 4 (their
+        // packed recurrence needs no negation): the sign returns here
+        if ((m & 3) >= 2) sgn = -sgn;
         cm[m] = kLn2 * s_coef[m * NPX + p] * sgn;  // zero for p >= D / 2
       }
     }
@@ -1593,18 +1596,23 @@ __global__ void __launch_bounds__(kThreads, 1) dk3_kernel(const __grid_constant_
         uint32_t y[kM][2];
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
-          // Y_m = dl T_m(u) obeys the Chebyshev recurrence itself:
-          // Y_{m+1} = 2u Y_m - Y_{m-1}, Y_0 = dl, Y_1 = dl u
-          const float ua = 2.f * uj[2 * jp], ub = 2.f * uj[2 * jp + 1];
-          float ya0 = dl[2 * jp], yb0 = dl[2 * jp + 1];
-          float ya1 = ya0 * uj[2 * jp], yb1 = yb0 * uj[2 * jp + 1];
-          y[0][jp] = E::pack(ya0, yb0);
-          y[1][jp] = E::pack(ya1, yb1);
+          // Y_m = dl T_m(u) obeys the Chebyshev recurrence itself,
+          // Y_{m+1} = 2u Y_m - Y_{m-1} (Y_0 = dl, Y_1 = dl u).  Tracked with the
+          // signs s_m = (+, +, -, -, ...), V_m = s_m Y_m obeys
+          // V_m = (-1)^(m+1) 2u V_{m-1} + V_{m-2}: one packed FMA per step for
+          // the pair's two keys, no negated operand (the combine restores s_m)
+          const float2 u2 = make_float2(2.f * uj[2 * jp], 2.f * uj[2 * jp + 1]);
+          const float2 nu2 = make_float2(-2.f * uj[2 * jp], -2.f * uj[2 * jp + 1]);
+          float2 v0 = make_float2(dl[2 * jp], dl[2 * jp + 1]);
+          float2 v1 = make_float2(v0.x * uj[2 * jp], v0.y * uj[2 * jp + 1]);
+          y[0][jp] = E::pack(v0.x, v0.y);
+          y[1][jp] = E::pack(v1.x, v1.y);
 #pragma unroll
           for (int m = 2; m < kM; ++m) {
-            const float ya2 = fmaf(ua, ya1, -ya0), yb2 = fmaf(ub, yb1, -yb0);
-            ya0 = ya1; ya1 = ya2; yb0 = yb1; yb1 = yb2;
-            y[m][jp] = E::pack(ya2, yb2);
+            const float2 v2 = __ffma2_rn((m & 1) ? u2 : nu2, v1, v0);
+            v0 = v1;
+            v1 = v2;
+            y[m][jp] = E::pack(v2.x, v2.y);
           }
         }
 #pragma unroll
