@@ -476,10 +476,6 @@ def run_ours(args):
         saved, o = forward(q, k, v)
         return backward(saved, do) if w["bwd"] else o
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-
     ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     f_ev = [(ev(), ev()) for _ in range(args.steps)]
     b_ev = [(ev(), ev()) for _ in range(args.steps)]
@@ -487,6 +483,12 @@ def run_ours(args):
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
+    # warm-up right before the timed steps: after the sampler's start-up pause
+    # the GPU is idle, and a short timed region (the plain-attention workload
+    # runs 20 steps of ~1 ms) would otherwise include its clock ramp
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     start.record(stream)

@@ -649,6 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           case 2: sgn = -1.f; break;
           default: sgn = e ? -1.f : 1.f; break;
         }
+        if ((m & 3) >= 2) sgn = -sgn;  // the rows store s_m Y_m (see the Y recurrence)
         cm[m] = kLn2 * s_coef[m * NPX + p] * sgn;  // zero for p >= D / 2
       }
     }
@@ -947,7 +948,11 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       // two keys per packed fp32x2 FMA.  Value: b_m = 2u b_{m+1} + (G_m -
       // b_{m+2}); derivative tracked halved, e = d / 2:
       // e_m = 2u e_{m+1} + (b_{m+1} - e_{m+2}) -- two FMAs per step each
+      constexpr bool SGN = MODE == MODE_DQ;
       const float2 neg1 = make_float2(-1.f, -1.f), neg2 = make_float2(-2.f, -2.f);
+      const float2 one = make_float2(1.f, 1.f), two = make_float2(2.f, 2.f);
+      const float2 nu2[2] = {make_float2(-2.f * uj[0], -2.f * uj[1]),
+                             make_float2(-2.f * uj[2], -2.f * uj[3])};
       const float2 u2[2] = {make_float2(2.f * uj[0], 2.f * uj[1]), make_float2(2.f * uj[2], 2.f * uj[3])};
       const float2 u1[2] = {make_float2(uj[0], uj[1]), make_float2(uj[2], uj[3])};
       float2 b1[2], b2[2], e1[2], e2[2];
@@ -962,6 +967,27 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
           if (m >= NPT[j]) continue;
           const float2 a = make_float2(__uint_as_float(g[m >> 1][m & 1][2 * j]),
                                        __uint_as_float(g[m >> 1][m & 1][2 * j + 1]));
+          if (SGN) {
+            // dQ launch: G'_m = s_m G_m (the signs folded into its K^(m)), the
+            // basis V_m = s_m T_m with V_{m+1} = a_m V_m + V_{m-1}, a_m = +-2u
+            // (minus for odd m): b_m = G'_m + a_m b_{m+1} + b_{m+2},
+            // e_m = -+ b_{m+1} + a_m e_{m+1} + e_{m+2} (e = d / 2); then
+            // l = G'_0 + u b_1 + b_2 and l' = b_1 + 2u e_1 + 2 e_2
+            const float2 t = __ffma2_rn(one, b2[j], a);
+            if (m > 0) {
+              const float2 al = (m & 1) ? nu2[j] : u2[j];
+              const float2 en = __ffma2_rn(al, e1[j], __ffma2_rn((m & 1) ? neg1 : one, b1[j], e2[j]));
+              const float2 bn = __ffma2_rn(al, b1[j], t);
+              e2[j] = e1[j]; e1[j] = en;
+              b2[j] = b1[j]; b1[j] = bn;
+            } else {
+              const float2 r = __ffma2_rn(u1[j], b1[j], t);
+              const float2 rd = __ffma2_rn(u2[j], e1[j], __ffma2_rn(two, e2[j], b1[j]));
+              f[2 * j] = r.x; f[2 * j + 1] = r.y;
+              fd[2 * j] = rd.x; fd[2 * j + 1] = rd.y;
+            }
+            continue;
+          }
           const float2 t = __ffma2_rn(neg1, b2[j], a);
           if (m > 0) {
             const float2 en = __ffma2_rn(u2[j], e1[j], __ffma2_rn(neg1, e2[j], b1[j]));
@@ -1051,20 +1077,26 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
         uint32_t y[kM][2];
 #pragma unroll
         for (int jp = 0; jp < 2; ++jp) {
-          // Y_m = dl T_m(u) obeys the Chebyshev recurrence itself:
-          // Y_{m+1} = 2u Y_m - Y_{m-1}, Y_0 = dl, Y_1 = dl u
+          // Y_m = dl T_m(u) obeys the Chebyshev recurrence itself,
+          // Y_{m+1} = 2u Y_m - Y_{m-1} (Y_0 = dl, Y_1 = dl u).  Stored as
+          // V_m = s_m Y_m with s_m = (+, +, -, -, ...): V_m = (-1)^(m+1) 2u
+          // V_{m-1} + V_{m-2}, one packed FMA per step for the pair's two keys
+          // and no negated operand; the signs are in the dQ launch's K^(m)
+          // (its coefficient table) and in the dK launch's combine
           constexpr float ys = MODE == MODE_DQ ? kLn2 : 1.f;
-          const float ua = 2.f * uj[2 * jp], ub = 2.f * uj[2 * jp + 1];
-          float ya0 = ys * dl[2 * jp], yb0 = ys * dl[2 * jp + 1];
-          float ya1 = ya0 * uj[2 * jp], yb1 = yb0 * uj[2 * jp + 1];
-          y[0][jp] = E::pack(ya0, yb0);
-          y[1][jp] = E::pack(ya1, yb1);
+          const float2 u2 = make_float2(2.f * uj[2 * jp], 2.f * uj[2 * jp + 1]);
+          const float2 nu2 = make_float2(-2.f * uj[2 * jp], -2.f * uj[2 * jp + 1]);
+          float2 v0 = make_float2(ys * dl[2 * jp], ys * dl[2 * jp + 1]);
+          float2 v1 = make_float2(v0.x * uj[2 * jp], v0.y * uj[2 * jp + 1]);
+          y[0][jp] = E::pack(v0.x, v0.y);
+          y[1][jp] = E::pack(v1.x, v1.y);
 #pragma unroll
           for (int m = 2; m < kM; ++m) {
             if (m >= (jp ? NPT1 : NPT0)) break;  // the X GEMM's K^(m) rows there are zero
-            const float ya2 = fmaf(ua, ya1, -ya0), yb2 = fmaf(ub, yb1, -yb0);
-            ya0 = ya1; ya1 = ya2; yb0 = yb1; yb1 = yb2;
-            y[m][jp] = E::pack(ya2, yb2);
+            const float2 v2 = __ffma2_rn((m & 1) ? u2 : nu2, v1, v0);
+            v0 = v1;
+            v1 = v2;
+            y[m][jp] = E::pack(v2.x, v2.y);
           }
         }
         if (MODE == MODE_DQ) {
@@ -1819,6 +1851,7 @@ cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* ha
     tcx::OffsetPanelArgs ca;
     tcx::offset_panel_bytes<kMB>(a.B, a.Hkv, a.Sk, a.D, a.theta, a.sm_scale, &ca, true, false);
     ca.cf = a.coef;
+    ca.signs = 1;  // the dQ kernel's rows run the signed basis s_m T_m
     tcx::offset_coef_kernel<<<16, 64, 0, st>>>(ca);
   }
   p.cf = a.coef;

@@ -363,6 +363,7 @@ struct OffsetPanelArgs {
   float2* cf;       // [16][kPanelTerms][64] complex coefficients
   int km;           // most terms of any offset
   int bwd_order;    // key slots: tcx::bwd_slot_key (else 8 hh + slot_key)
+  int signs;        // coefficients times s_m = (+, +, -, -, ...) (the dQ kernel's basis)
   float scale;      // sm_scale * log2(e)
   double th[64];    // theta_p
 };
@@ -411,7 +412,8 @@ static __global__ void __launch_bounds__(64) offset_coef_kernel(const __grid_con
   double sn, cs;
   sincos((kC0 - c) * A.th[p], &sn, &cs);
   for (int m = 0; m < kPanelTerms; ++m) {
-    const double be = m < n ? (m == 0 ? 1.0 : 2.0) * jv[m] * A.scale : 0.0;
+    const double be = (m < n ? (m == 0 ? 1.0 : 2.0) * jv[m] * A.scale : 0.0) *
+                      (A.signs && (m & 3) >= 2 ? -1.0 : 1.0);
     // (-i)^m exp(i phi) = exp(i (phi - m pi / 2))
     double re, im;
     switch (m & 3) {
