@@ -58,11 +58,23 @@ def unshard_sequence(shards, dim: int = 2) -> torch.Tensor:
 
 
 def _all_gather_sequence(x: torch.Tensor, group, world: int) -> torch.Tensor:
-    """[B, H, 2C, D] zig-zag shards of every rank -> [B, H, 2 world C, D]."""
+    """[B, H, 2C, D] zig-zag shards of every rank -> [B, H, 2 world C, D].
+
+    The gathered shards are put in sequence order by one copy per sequence
+    chunk, each moving the chunk's contiguous [C, D] block of every (b, h)
+    (about twice as fast as concatenating the narrowed shards)."""
     x = x.contiguous()
-    out = torch.empty((world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+    B, H, L, D = x.shape
+    C = L // 2
+    out = torch.empty((world * B, H, L, D), dtype=x.dtype, device=x.device)
     dist.all_gather_into_tensor(out, x, group=group)  # ranks concatenated along dim 0
-    return unshard_sequence(list(out.chunk(world, dim=0)))
+    src = out.view(world, B * H, 2, C * D)
+    seq = torch.empty((B, H, world * L, D), dtype=x.dtype, device=x.device)
+    dst = seq.view(B * H, 2 * world, C * D)
+    for r in range(world):
+        for i, c in enumerate(zigzag_chunks(r, world)):
+            dst[:, c].copy_(src[r, :, i])
+    return seq
 
 
 # Most bytes one kv-head group of the backward may hold at once: its

@@ -1763,7 +1763,8 @@ static cudaError_t make_panels(Params& p, const BwdArgs& a, void* panels, cudaSt
   p.km_nhw = pa.nhw;
   p.km_rows[0] = pa.rows[0];
   p.km_rows[1] = pa.rows[1];
-  tcx::offset_panel_kernel<T, D><<<dim3(pa.nhw, a.B * a.Hkv), 128, 0, st>>>(pa);
+  tcx::offset_panel_kernel<T, D>
+      <<<dim3(tcx::panel_halfwindows_read(a.Sk, a.r0, a.S), a.B * a.Hkv), 128, 0, st>>>(pa);
   return cudaGetLastError();
 }
 

@@ -461,6 +461,13 @@ __global__ void __launch_bounds__(128) offset_panel_kernel(const __grid_constant
   }
 }
 
+// Half windows of panels a launch reads: its rows r0 .. r0 + S - 1 see keys
+// below r0 + S only (causal), so a query chunk of a longer key sequence needs
+// the panels of those keys alone; the panel layout keeps the stride of all Sk.
+inline int panel_halfwindows_read(int Sk, int r0, int S) {
+  return 2 * ((std::min(Sk, r0 + S) + kW - 1) / kW);
+}
+
 // Fill the arguments of the per-offset panels (KM: most terms of any
 // offset) and return the workspace bytes they take: both slabs' panels, then
 // (own_table) the coefficient table (0 when the head dim has none).

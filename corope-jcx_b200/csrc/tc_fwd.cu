@@ -846,7 +846,8 @@ static cudaError_t launch_t(Params& p, const FwdArgs& a, cudaStream_t st, void* 
     p.km_rows[0] = pa.rows[0];
     p.km_rows[1] = pa.rows[1];
     tcx::offset_coef_kernel<<<16, 64, 0, st>>>(pa);
-    tcx::offset_panel_kernel<T, D><<<dim3(pa.nhw, a.B * a.Hkv), 128, 0, st>>>(pa);
+    tcx::offset_panel_kernel<T, D>
+        <<<dim3(tcx::panel_halfwindows_read(a.Sk, a.r0, a.S), a.B * a.Hkv), 128, 0, st>>>(pa);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
