@@ -177,7 +177,9 @@ exact_fwd_kernel(FwdArgs args) {
 // Backward
 // ---------------------------------------------------------------------------
 // delta_t = sum_d dO_td * O_td and lse_t = m_t + log(l_t); one warp per row.
-template <typename T>
+// VEC: 16-bit rows with 8-byte aligned starts and D a multiple of 4 -- each
+// lane reads 4 consecutive elements of o and dO per 8-byte load.
+template <typename T, bool VEC>
 __global__ void exact_bwd_pre_kernel(BwdArgs args) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -189,7 +191,18 @@ __global__ void exact_bwd_pre_kernel(BwdArgs args) {
   const T* ob = (const T*)args.o + b * args.os[0] + h * args.os[1] + (int64_t)t * args.os[2];
   const T* db = (const T*)args.dout + b * args.dos[0] + h * args.dos[1] + (int64_t)t * args.dos[2];
   float s = 0.f;
-  for (int d = lane; d < args.D; d += 32) s = fmaf(to_f32<T>(ob[d]), to_f32<T>(db[d]), s);
+  if constexpr (VEC) {
+    for (int d = 4 * lane; d < args.D; d += 128) {
+      const uint2 ov = *reinterpret_cast<const uint2*>(ob + d);
+      const uint2 dv = *reinterpret_cast<const uint2*>(db + d);
+      const T* o4 = reinterpret_cast<const T*>(&ov);
+      const T* d4 = reinterpret_cast<const T*>(&dv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s = fmaf(to_f32<T>(o4[e]), to_f32<T>(d4[e]), s);
+    }
+  } else {
+    for (int d = lane; d < args.D; d += 32) s = fmaf(to_f32<T>(ob[d]), to_f32<T>(db[d]), s);
+  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   if (lane == 0) {
@@ -390,9 +403,48 @@ exact_bwd_kernel(BwdArgs args) {
   }
 }
 
-// fp32 dk/dv accumulators -> output dtype and strides.
-template <typename T>
+// two floats -> one word of 16-bit values, rounded to nearest (as from_f32)
+template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// fp32 dk/dv accumulators -> output dtype and strides.  VEC: 16-bit outputs
+// with 16-byte aligned rows and D a multiple of 8 -- each thread converts 8
+// consecutive elements (two 16-byte loads per accumulator, one 16-byte store
+// per output) and derives the row once for them.
+template <typename T, bool VEC>
 __global__ void exact_bwd_post_kernel(BwdArgs args) {
+  if constexpr (VEC) {
+    const int d8 = args.D / 8;
+    const int64_t n8 = (int64_t)args.B * args.Hkv * args.Sk * d8;
+    for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < n8;
+         g += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t r = g / d8;
+      const int d0 = (int)(g - r * d8) * 8;
+      const int j = (int)(r % args.Sk);
+      const int64_t bh = r / args.Sk;
+      const int hk = (int)(bh % args.Hkv), b = (int)(bh / args.Hkv);
+      const float4* k4 = reinterpret_cast<const float4*>(args.dk32 + g * 8);
+      const float4* v4 = reinterpret_cast<const float4*>(args.dv32 + g * 8);
+      const float4 ka = k4[0], kb = k4[1], va = v4[0], vb = v4[1];
+      uint4 ko, vo;
+      ko.x = pack2<T>(ka.x, ka.y); ko.y = pack2<T>(ka.z, ka.w);
+      ko.z = pack2<T>(kb.x, kb.y); ko.w = pack2<T>(kb.z, kb.w);
+      vo.x = pack2<T>(va.x, va.y); vo.y = pack2<T>(va.z, va.w);
+      vo.z = pack2<T>(vb.x, vb.y); vo.w = pack2<T>(vb.z, vb.w);
+      *reinterpret_cast<uint4*>((T*)args.dk + b * args.dks[0] + hk * args.dks[1] +
+                                (int64_t)j * args.dks[2] + d0) = ko;
+      *reinterpret_cast<uint4*>((T*)args.dv + b * args.dvs[0] + hk * args.dvs[1] +
+                                (int64_t)j * args.dvs[2] + d0) = vo;
+    }
+    return;
+  }
   const int64_t n = (int64_t)args.B * args.Hkv * args.Sk * args.D;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -407,6 +459,49 @@ __global__ void exact_bwd_post_kernel(BwdArgs args) {
     ((T*)args.dv)[b * args.dvs[0] + hk * args.dvs[1] + (int64_t)j * args.dvs[2] + d] =
         from_f32<T>(args.dv32[i]);
   }
+}
+
+// The vectorised conversion applies to 16-bit outputs whose rows start on
+// 16-byte boundaries, with D a multiple of 8.
+template <typename T>
+static bool post_vec_ok(const BwdArgs& a) {
+  if (sizeof(T) != 2 || a.D % 8 != 0) return false;
+  const int64_t* st[2] = {a.dks, a.dvs};
+  const void* p[2] = {a.dk, a.dv};
+  for (int i = 0; i < 2; ++i) {
+    if (reinterpret_cast<uintptr_t>(p[i]) % 16 != 0) return false;
+    for (int k = 0; k < 3; ++k)
+      if ((st[i][k] * 2) % 16 != 0) return false;
+  }
+  return true;
+}
+template <typename T>
+static cudaError_t launch_post(const BwdArgs& a, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2) {
+    if (post_vec_ok<T>(a)) {
+      exact_bwd_post_kernel<T, true><<<148 * 8, 256, 0, st>>>(a);
+      return cudaGetLastError();
+    }
+  }
+  exact_bwd_post_kernel<T, false><<<148 * 8, 256, 0, st>>>(a);
+  return cudaGetLastError();
+}
+// The vectorised delta reads apply to 16-bit rows starting on 8-byte
+// boundaries, with D a multiple of 4.
+template <typename T>
+static void launch_pre(const BwdArgs& a, cudaStream_t st) {
+  const int64_t rows = (int64_t)a.B * a.H * a.S;
+  const unsigned grid = (unsigned)((rows * 32 + 255) / 256);
+  if constexpr (sizeof(T) == 2) {
+    bool vec = a.D % 4 == 0 && reinterpret_cast<uintptr_t>(a.o) % 8 == 0 &&
+               reinterpret_cast<uintptr_t>(a.dout) % 8 == 0;
+    for (int k = 0; k < 3; ++k) vec = vec && (a.os[k] * 2) % 8 == 0 && (a.dos[k] * 2) % 8 == 0;
+    if (vec) {
+      exact_bwd_pre_kernel<T, true><<<grid, 256, 0, st>>>(a);
+      return;
+    }
+  }
+  exact_bwd_pre_kernel<T, false><<<grid, 256, 0, st>>>(a);
 }
 
 // ---------------------------------------------------------------------------
@@ -475,8 +570,7 @@ static cudaError_t launch_bwd_d(const BwdArgs& a, cudaStream_t st) {
 
 template <typename T>
 static cudaError_t launch_bwd_t(const BwdArgs& a, cudaStream_t st) {
-  const int64_t rows = (int64_t)a.B * a.H * a.S;
-  exact_bwd_pre_kernel<T><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(a);
+  launch_pre<T>(a, st);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   switch (a.D) {
@@ -490,20 +584,17 @@ static cudaError_t launch_bwd_t(const BwdArgs& a, cudaStream_t st) {
   }
   if (e != cudaSuccess) return e;
   if (!a.dk || !a.dv) return cudaSuccess;  // query chunk: the caller keeps the fp32 sums
-  exact_bwd_post_kernel<T><<<148 * 8, 256, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_post<T>(a, st);
 }
 
 template <typename T>
 static cudaError_t pre_t(const BwdArgs& a, cudaStream_t st) {
-  const int64_t rows = (int64_t)a.B * a.H * a.S;
-  exact_bwd_pre_kernel<T><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(a);
+  launch_pre<T>(a, st);
   return cudaGetLastError();
 }
 template <typename T>
 static cudaError_t post_t(const BwdArgs& a, cudaStream_t st) {
-  exact_bwd_post_kernel<T><<<148 * 8, 256, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_post<T>(a, st);
 }
 
 // delta = rowsum(dO * O) and lse = m + log(l) into the workspace
