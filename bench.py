@@ -69,7 +69,7 @@ NCU_TRAFFIC_BYTES = {("bench", "exact"): 33.78e6 * 32,
 # The pipe that binds the dominant kernel (ncu, B=1,H=8,S=2048,D=128 of the same
 # kernel): instruction issue of the CUDA-core work around the tensor-core GEMMs
 ROOFLINE_BINDING = {("bench", "tensor"): {"resource": "instruction issue",
-                                          "issue_active_pct": 53.2, "tensor_pipe_pct": 14.9,
+                                          "issue_active_pct": 50.4, "tensor_pipe_pct": 15.0,
                                           "kernel": "dQ kernel (52% of the step)"}}
 
 
