@@ -46,6 +46,42 @@ def _run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo):
     return dq, dk, dv
 
 
+def _table_theta(table, D, theta, algo):
+    """(theta, algo) for a caller-supplied [D/2] frequency table.
+
+    The tensor-core kernels derive their expansion coefficients and term counts
+    from the scalar ``theta`` while the rotation reads the table, so the two
+    must describe the same base.  The reference's callers pass only the table
+    (co_rope_attn.py:35-47 rebuilds it from ``ctx.theta``), so a table that is
+    not ``theta`` 's has its base recovered from its last entry
+    (theta_{D/2-1} = base ** (-(D-2) / D), where fp32 rounding moves the base
+    least) and checked entry by entry.  A table of no
+    base >= 1 runs the exact kernels under "auto" and raises under "tensor".
+    The check reads the table back, which is not allowed while a CUDA graph
+    is being captured: there "auto" runs the exact kernels and "tensor"
+    trusts ``theta``."""
+    if torch.cuda.is_available() and table.is_cuda and torch.cuda.is_current_stream_capturing():
+        return theta, ("exact" if algo == "auto" else algo)
+
+    def matches(base):
+        ref = _lib.theta_table(D, base, table.device)
+        return table.shape == ref.shape and torch.allclose(table, ref, rtol=1e-6, atol=0.0)
+
+    if matches(theta):
+        return theta, algo
+    if table.numel() > 1:
+        t = float(table[-1])
+        if 0.0 < t < 1.0:
+            base = t ** (-D / (D - 2.0))
+            for cand in (float(round(base)), base):
+                if cand >= 1.0 and matches(cand):
+                    return cand, algo
+    if algo == "tensor":
+        raise ValueError("thetas is not base ** (-2p / D) for any base >= 1 (or not for the "
+                         "given theta); the tensor-core kernels cannot run it, use algo='exact'")
+    return theta, "exact"
+
+
 def co_rope_backward(*args, sm_scale=None, theta=10000.0, thetas=None, causal=True,
                      contextual_bias=None, algo="auto", **kwargs):
     if args and isinstance(args[0], (tuple, list)):
@@ -77,6 +113,8 @@ def co_rope_backward(*args, sm_scale=None, theta=10000.0, thetas=None, causal=Tr
         th = th.reshape(-1, th.shape[-1])[0] if th.dim() > 1 else th
         # repeat-interleaved [D] -> one entry per pair
         table = th[0::2].float().contiguous() if th.numel() == vals["q"].shape[-1] else th.float().contiguous()
+        if algo != "exact":
+            theta, algo = _table_theta(table, vals["q"].shape[-1], theta, algo)
     dq, dk, dv = _run(vals["q"], vals["k"], vals["v"], vals["o"], vals["m"], vals["l"], vals["a"],
                       vals["do"], vals["sm_scale"], theta, table, contextual_bias, algo)
     return dq, dk, dv, None

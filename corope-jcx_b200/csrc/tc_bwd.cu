@@ -1809,6 +1809,8 @@ static bool rows16(const void* ptr, const int64_t* st) {
 
 bool tc_bwd_supported(const BwdArgs& a, int dtype) {
   if (dtype != COROPE_DTYPE_BF16 && dtype != COROPE_DTYPE_F16) return false;
+  // the expansions' term counts assume every frequency theta_p <= 1
+  if (!(a.theta >= 1.f)) return false;
   if (a.D != 64 && a.D != 128) return false;
   if (!rows16(a.q, a.qs) || !rows16(a.k, a.ks) || !rows16(a.v, a.vs) ||
       !rows16(a.dout, a.dos) || !rows16(a.dq, a.dqs))

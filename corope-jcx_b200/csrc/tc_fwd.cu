@@ -867,6 +867,8 @@ static bool rows_ok(const void* ptr, const int64_t* st) {
 
 bool tc_fwd_supported(const FwdArgs& a, int dtype) {
   if (dtype != COROPE_DTYPE_BF16 && dtype != COROPE_DTYPE_F16) return false;
+  // the expansions' term counts assume every frequency theta_p <= 1
+  if (!(a.theta >= 1.f)) return false;
   if (a.D != 64 && a.D != 128) return false;
   if (!rows_ok(a.q, a.qs) || !rows_ok(a.k, a.ks) || !rows_ok(a.v, a.vs) || !rows_ok(a.o, a.os))
     return false;

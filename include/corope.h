@@ -67,7 +67,12 @@ typedef struct {
                               logits, sum of exp(logit - m), total gate sum */
   float *lse;              /* optional output [B,H,S] fp32: m + log(l) */
   const float *thetas;     /* optional [D/2] fp32 frequency table; NULL:
-                              theta^(-2p/D) computed from `theta` */
+                              theta^(-2p/D) computed from `theta`.  The
+                              tensor-core kernels derive their expansion
+                              coefficients from `theta` (not read back from
+                              the table), so under AUTO/TENSOR the table must
+                              be theta^(-2p/D) of the same `theta`; theta < 1
+                              always runs the exact kernels */
   const float *bias;       /* optional additive logit bias [S,S] fp32 */
   int64_t bias_row_stride; /* elements between bias rows */
   int64_t q_stride[3], k_stride[3], v_stride[3], o_stride[3];

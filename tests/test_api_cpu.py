@@ -61,6 +61,37 @@ def test_backward_accepts_both_conventions(monkeypatch):
         co_rope_backward(t, t, t, t, t, t, t, t, thetas, False, 0.25)
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_backward_table_base_reaches_tensor_kernels(monkeypatch, D):
+    """The reference's autograd backward passes only the thetas table
+    (co_rope_attn.py:35-47): its base is recovered for the tensor-core
+    kernels; a table of no base runs exact under "auto", raises under
+    "tensor"."""
+    bwd_mod = importlib.import_module("CoROPE.co_rope_backward")
+    seen = []
+
+    def fake_run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo):
+        seen.append((theta, algo))
+        return "dq", "dk", "dv"
+
+    monkeypatch.setattr(bwd_mod, "_run", fake_run)
+    t = torch.zeros(1, 1, 4, D)
+    for base in (10000.0, 500000.0, 1e6, 123.5):
+        th = 1.0 / (base ** (torch.arange(0, D, 2).float() / D))
+        thetas = th.repeat_interleave(2).unsqueeze(0).repeat(2, 1)
+        co_rope_backward(t, t, t, t, t, t, t, t, thetas, True, 0.25)
+        assert seen[-1][1] == "auto"
+        assert seen[-1][0] == pytest.approx(base, rel=1e-6)
+    assert seen[-3][0] == 500000.0  # integer bases come back exact
+    junk = torch.rand(D)
+    co_rope_backward(t, t, t, t, t, t, t, t, junk, True, 0.25)
+    assert seen[-1] == (10000.0, "exact")
+    with pytest.raises(ValueError):
+        co_rope_backward(t, t, t, t, t, t, t, t, junk, True, 0.25, algo="tensor")
+    co_rope_backward(t, t, t, t, t, t, t, t, junk, True, 0.25, algo="exact")
+    assert seen[-1] == (10000.0, "exact")
+
+
 def test_theta_table_matches_reference_expression():
     from CoROPE import _lib
     D, theta = 128, 10000.0

@@ -527,6 +527,51 @@ def test_query_chunk_argument_checks():
                  None, 0.125, 1e4, mqa=True, q_row0=128)
 
 
+def test_theta_below_one_and_reference_tables():
+    """The tensor-core expansions assume every frequency theta_p <= 1 and take
+    their coefficients from a scalar base: theta < 1 under "auto" runs the
+    exact kernels (and "tensor" refuses it); the reference's 11-argument
+    backward, which passes only the thetas table, has the table's base
+    recovered (tensor path, results of that base); a table of no base raises
+    under "tensor".  All against the oracle."""
+    from CoROPE import _lib
+    S, D = 300, 64
+    sm = 1 / math.sqrt(D)
+    (q, k, v, do), cpu = inputs(1, 2, S, D, 41, torch.bfloat16)
+    with pytest.raises(NotImplementedError):
+        co_rope_forward(q, k, v, sm, theta=0.5, algo="tensor")
+    saved, o = co_rope_forward(q, k, v, sm, theta=0.5)
+    dq, dk, dv = co_rope_backward(saved, do, sm, 0.5)
+    torch.cuda.synchronize()
+    assert _lib.take_device_error() == 0
+    ref = O.forward_dense(*cpu[:3], sm, 0.5)
+    assert maxabs(o, ref["o"]) < O_MAXABS
+    for name, mine, r in zip(("dq", "dk", "dv"), (dq, dk, dv),
+                             O.backward_dense(*cpu, sm, 0.5)):
+        assert maxabs(mine, r) < G_MAXABS, name
+
+    # reference call form: repeat-interleaved [H, D] table of base 500, theta
+    # left at its default 1e4
+    saved, o = co_rope_forward(q, k, v, sm, theta=500.0)
+    tab = 1.0 / (500.0 ** (torch.arange(0, D, 2, device=DEV).float() / D))
+    thetas = tab.repeat_interleave(2).expand(2, D).contiguous()
+    args = (*saved, do, thetas, True, sm)
+    dq, dk, dv, dth = co_rope_backward(*args, algo="tensor")
+    torch.cuda.synchronize()
+    assert _lib.take_device_error() == 0 and dth is None
+    for name, mine, r in zip(("dq", "dk", "dv"), (dq, dk, dv),
+                             O.backward_dense(*cpu, sm, 500.0)):
+        assert maxabs(mine, r) < G_MAXABS, name
+        assert rel_l2(mine, r) < REL_L2, name
+    bent = thetas.clone()
+    bent[:, 10:12] *= 1.5
+    with pytest.raises(ValueError):
+        co_rope_backward(*saved, do, bent, True, sm, algo="tensor")
+    dq2, _, _, _ = co_rope_backward(*saved, do, bent, True, sm)
+    torch.cuda.synchronize()
+    assert torch.isfinite(dq2).all()
+
+
 @pytest.mark.parametrize("D,hkv,theta,bias", [(128, None, 1e4, False), (64, None, 5e5, True),
                                               (128, 1, 5e5, False), (128, 2, 1e4, True)])
 def test_forward_panels_equal_in_kernel_builders(D, hkv, theta, bias):
