@@ -20,6 +20,8 @@ LIB_PATH = os.path.join(_HERE, "libcorope_b200.so")
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 ALGO_AUTO, ALGO_EXACT, ALGO_TENSOR = 0, 1, 2
 _ALGOS = {"auto": ALGO_AUTO, "exact": ALGO_EXACT, "tensor": ALGO_TENSOR}
+# corope.h COROPE_BWD_DETERMINISTIC, OR'd into the backward's algo
+BWD_DETERMINISTIC = 0x100
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_DEVICE = range(6)
 
@@ -336,7 +338,7 @@ def fit_workspace(full, least, units, budget, panels=0):
 
 def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="auto",
         thetas=None, workspace="auto", q_row0=None, dk_accum=None, dv_accum=None,
-        accum_chunk_rows=0):
+        accum_chunk_rows=0, deterministic=False):
     """Launch corope_bwd on the current stream of q with a torch-allocated
     workspace: "auto" (auto_workspace_bytes: the full size up to 4 GiB, else
     as many hand-off slices as fit), "full" (corope_bwd_workspace_bytes, the fastest),
@@ -347,7 +349,10 @@ def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="a
     ignored and this chunk's key gradients are added to the contiguous fp32
     ``dk_accum``/``dv_accum``: [B, Hkv, kv_len, D], or with
     ``accum_chunk_rows`` = C the zig-zag owner-major layout
-    [2, N, B, Hkv, C, D] of 2N chunks of C keys (corope_chunk_t)."""
+    [2, N, B, Hkv, C, D] of 2N chunks of C keys (corope_chunk_t).
+
+    ``deterministic`` sets COROPE_BWD_DETERMINISTIC: dk and dv summed in
+    64-bit fixed point, bit-identical from call to call (not with q_row0)."""
     lib = load_library()
     B, H, S, D = q.shape
     p = BwdParams()
@@ -377,6 +382,8 @@ def bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=None, algo="a
     p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, k.shape[1], S, D
     p.sm_scale, p.theta = float(sm_scale), float(theta)
     p.causal, p.dtype, p.algo = 1, _dtype_code(q), algo_code(algo)
+    if deterministic:
+        p.algo |= BWD_DETERMINISTIC
     if workspace == "auto":
         nbytes = auto_workspace_bytes(lib, p, q.device, chunk)
     elif workspace == "full":

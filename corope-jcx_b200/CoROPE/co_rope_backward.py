@@ -16,6 +16,10 @@ check.py:44-103); the reference's own Triton backward does not compute them
 opposite direction), so parity is with the definition, not with that kernel.
 K/V with fewer heads than Q (MQA/GQA, from ``co_rope_mqa_forward``) are
 accepted: their gradients are summed over each head group.
+
+``deterministic=True`` (default: ``torch.are_deterministic_algorithms_enabled()``)
+sums dk and dv in 64-bit fixed point instead of with fp32 atomics, so repeated
+calls give bit-identical gradients (dq is deterministic either way).
 """
 from __future__ import annotations
 
@@ -27,7 +31,7 @@ from .forward import _check_causal
 __all__ = ["co_rope_backward"]
 
 
-def _run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo):
+def _run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo, deterministic=False):
     B, H, S, D = q.shape
     assert q.is_cuda and k.is_cuda and v.is_cuda, "Inputs must be CUDA tensors"
     assert k.shape[0] == B and k.shape[2:] == q.shape[2:] and v.shape == k.shape
@@ -42,7 +46,7 @@ def _run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo):
     for t in (dq, dk, dv):
         assert t.stride(-1) == 1
     _lib.bwd(q, k, v, o, do, m, l, a, dq, dk, dv, sm_scale, theta, bias=bias, algo=algo,
-             thetas=thetas)
+             thetas=thetas, deterministic=deterministic)
     return dq, dk, dv
 
 
@@ -83,7 +87,9 @@ def _table_theta(table, D, theta, algo):
 
 
 def co_rope_backward(*args, sm_scale=None, theta=10000.0, thetas=None, causal=True,
-                     contextual_bias=None, algo="auto", **kwargs):
+                     contextual_bias=None, algo="auto", deterministic=None, **kwargs):
+    if deterministic is None:
+        deterministic = torch.are_deterministic_algorithms_enabled()
     if args and isinstance(args[0], (tuple, list)):
         # (saved, do, sm_scale=None, theta=10000.0)
         saved, do = args[0], args[1] if len(args) > 1 else kwargs.pop("do")
@@ -93,7 +99,8 @@ def co_rope_backward(*args, sm_scale=None, theta=10000.0, thetas=None, causal=Tr
             theta = args[3]
         q, k, v, o, m, l, a = saved
         _check_causal(causal)
-        return _run(q, k, v, o, m, l, a, do, sm_scale, theta, None, contextual_bias, algo)
+        return _run(q, k, v, o, m, l, a, do, sm_scale, theta, None, contextual_bias, algo,
+                    deterministic)
     # (q, k, v, o, m, l, a, do, thetas, causal, sm_scale)
     names = ["q", "k", "v", "o", "m", "l", "a", "do", "thetas", "causal", "sm_scale"]
     vals = dict(zip(names, args))
@@ -116,5 +123,6 @@ def co_rope_backward(*args, sm_scale=None, theta=10000.0, thetas=None, causal=Tr
         if algo != "exact":
             theta, algo = _table_theta(table, vals["q"].shape[-1], theta, algo)
     dq, dk, dv = _run(vals["q"], vals["k"], vals["v"], vals["o"], vals["m"], vals["l"], vals["a"],
-                      vals["do"], vals["sm_scale"], theta, table, contextual_bias, algo)
+                      vals["do"], vals["sm_scale"], theta, table, contextual_bias, algo,
+                      deterministic)
     return dq, dk, dv, None

@@ -137,7 +137,31 @@ struct BwdArgs {
   int acc_chunk; // 0, or the chunk rows C of the owner-major layout
   float2* coef;  // tensor-core path: the dQ kernel's per-offset expansion
                  // coefficients [16][16][64] (complex), written per call
+  int fixed;     // 1: dk32 / dv32 hold 64-bit fixed-point sums (acc_add)
 };
+
+// Deterministic accumulation: each contribution is rounded to a multiple of
+// 2^-36 and added as a 64-bit integer.  Integer addition is associative, so
+// the sums do not depend on the order in which the query tiles' atomics land
+// (fp32 atomics do); sums must stay below 2^27 in magnitude.
+constexpr float kFixScale = 68719476736.f;       // 2^36
+constexpr float kFixUnit = 1.4551915228366852e-11f;  // 2^-36
+
+// Adds v to element i of an accumulator: fp32 atomics, or with `fixed` the
+// fixed-point sum of the same element count viewed as 64-bit words.
+__device__ __forceinline__ void acc_add(float* base, int64_t i, float v, bool fixed) {
+  if (fixed)
+    atomicAdd(reinterpret_cast<unsigned long long*>(base) + i,
+              static_cast<unsigned long long>(__float2ll_rn(v * kFixScale)));
+  else
+    atomicAdd(base + i, v);
+}
+
+// Element i of an accumulator as fp32 (acc_add's two layouts).
+__device__ __forceinline__ float acc_get(const float* base, int64_t i, bool fixed) {
+  if (fixed) return __ll2float_rn(reinterpret_cast<const long long*>(base)[i]) * kFixUnit;
+  return base[i];
+}
 
 // Row (in units of D elements) of key `key` of (b, kv head) `bhk` in the fp32
 // dk / dv accumulators: [B*Hkv][Sk] rows, or, with C = acc_chunk > 0, the

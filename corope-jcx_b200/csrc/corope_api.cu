@@ -164,7 +164,8 @@ static int fwd_common(const corope_fwd_params_t* p, corope_stream_t stream, bool
   const bool tc_ok = tc_fwd_supported(a, p->dtype);
   if (p->algo == COROPE_ALGO_TENSOR && !tc_ok)
     return fail(COROPE_ERR_UNSUPPORTED,
-                "tensor-core forward needs bf16/f16, head_dim 64 or 128 and 16-byte aligned rows");
+                "tensor-core forward needs bf16/f16, head_dim 64 or 128, theta >= 1 and "
+                "16-byte aligned rows");
   if (p->algo != COROPE_ALGO_EXACT && p->algo != COROPE_ALGO_AUTO && p->algo != COROPE_ALGO_TENSOR)
     return fail(COROPE_ERR_INVALID, "unknown algo %d", p->algo);
   if (p->workspace && !aligned(p->workspace, 256))
@@ -178,22 +179,34 @@ static int fwd_common(const corope_fwd_params_t* p, corope_stream_t stream, bool
 
 static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
+// The backward's algorithm without the COROPE_BWD_DETERMINISTIC flag.
+static int bwd_algo(const corope_bwd_params_t* p) { return p->algo & ~COROPE_BWD_DETERMINISTIC; }
+static bool bwd_fixed(const corope_bwd_params_t* p) {
+  return (p->algo & COROPE_BWD_DETERMINISTIC) != 0;
+}
+
+// Whether the tensor-core backward may run for these parameters (the rest of
+// its conditions, on the tensors, are checked at launch).
+static bool bwd_tc_possible(const corope_bwd_params_t* p) {
+  return (p->head_dim == 64 || p->head_dim == 128) && bwd_algo(p) != COROPE_ALGO_EXACT &&
+         (p->dtype == COROPE_DTYPE_BF16 || p->dtype == COROPE_DTYPE_F16) && p->theta >= 1.f;
+}
+
 // The tensor-core backward's expansion coefficients (tc_bwd_coef_bytes) when
 // that path can run for these parameters, else 0.
 static size_t bwd_coef_ws(const corope_bwd_params_t* p) {
-  if ((p->head_dim != 64 && p->head_dim != 128) || p->algo == COROPE_ALGO_EXACT ||
-      (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16))
-    return 0;
-  return align256(tc_bwd_coef_bytes());
+  return bwd_tc_possible(p) ? align256(tc_bwd_coef_bytes()) : 0;
 }
 
 // Minimum workspace: delta and lse rows, the tensor-core path's expansion
-// coefficients, fp32 dk / dv accumulators (a query chunk accumulates into the
-// caller's dk_accum / dv_accum instead).
+// coefficients, dk / dv accumulators -- fp32, or 64-bit fixed point with
+// COROPE_BWD_DETERMINISTIC (a query chunk accumulates into the caller's fp32
+// dk_accum / dv_accum instead).
 static size_t bwd_ws(const corope_bwd_params_t* p, bool chunk = false) {
   const size_t rows = (size_t)p->batch * p->heads * p->seq_len;
   const size_t kv = (size_t)p->batch * p->kv_heads * p->seq_len * p->head_dim;
-  return 2 * align256(rows * 4) + bwd_coef_ws(p) + (chunk ? 0 : 2 * align256(kv * 4));
+  const size_t acc = kv * (bwd_fixed(p) ? 8 : 4);
+  return 2 * align256(rows * 4) + bwd_coef_ws(p) + (chunk ? 0 : 2 * align256(acc));
 }
 
 // Optional hand-off region after it (tensor-core backward only): the dQ
@@ -201,9 +214,7 @@ static size_t bwd_ws(const corope_bwd_params_t* p, bool chunk = false) {
 // rows x 16 keys; with less, the (b, h) slices go through it in chunks, or the
 // dK kernel recomputes them.
 static size_t bwd_handoff_ws(const corope_bwd_params_t* p, int r0 = 0) {
-  if ((p->head_dim != 64 && p->head_dim != 128) || p->algo == COROPE_ALGO_EXACT ||
-      (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16))
-    return 0;
+  if (!bwd_tc_possible(p)) return 0;
   return align256((size_t)p->batch * p->heads *
                   (size_t)tc_bwd_handoff_bytes_per_bh(p->seq_len, r0));
 }
@@ -211,9 +222,7 @@ static size_t bwd_handoff_ws(const corope_bwd_params_t* p, int r0 = 0) {
 // Optional scaled-key panels of the dQ kernel (tensor-core path), placed
 // right after the minimum workspace when the workspace has room for them.
 static size_t bwd_panel_ws(const corope_bwd_params_t* p, int kv_len) {
-  if ((p->head_dim != 64 && p->head_dim != 128) || p->algo == COROPE_ALGO_EXACT ||
-      (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16) || !(p->theta > 0.f))
-    return 0;
+  if (!bwd_tc_possible(p)) return 0;
   BwdArgs a{};
   a.B = p->batch; a.Hkv = p->kv_heads; a.Sk = kv_len; a.D = p->head_dim;
   a.theta = p->theta; a.sm_scale = p->sm_scale;
@@ -237,7 +246,7 @@ int corope_fwd(const corope_fwd_params_t* p, corope_stream_t stream) {
 size_t corope_fwd_workspace_bytes(const corope_fwd_params_t* p) {
   if (!p || p->batch <= 0 || p->heads <= 0 || p->kv_heads <= 0 || p->seq_len <= 0 ||
       (p->head_dim != 64 && p->head_dim != 128) || p->algo == COROPE_ALGO_EXACT ||
-      (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16) || !(p->theta > 0.f))
+      (p->dtype != COROPE_DTYPE_BF16 && p->dtype != COROPE_DTYPE_F16) || !(p->theta >= 1.f))
     return 0;
   FwdArgs a{};
   a.B = p->batch; a.Hkv = p->kv_heads; a.Sk = p->seq_len; a.D = p->head_dim;
@@ -326,8 +335,13 @@ static int bwd_check_args(const corope_bwd_params_t* p, const corope_chunk_t* ch
   if (!p->m || !p->l || !p->a) return fail(COROPE_ERR_INVALID, "m, l and a are required");
   if (p->bias && p->bias_row_stride < r0 + p->seq_len)
     return fail(COROPE_ERR_INVALID, "bias_row_stride must be >= seq_len (q_row0 + seq_len)");
-  if (p->algo != COROPE_ALGO_EXACT && p->algo != COROPE_ALGO_AUTO && p->algo != COROPE_ALGO_TENSOR)
+  const int algo = bwd_algo(p);
+  if (algo != COROPE_ALGO_EXACT && algo != COROPE_ALGO_AUTO && algo != COROPE_ALGO_TENSOR)
     return fail(COROPE_ERR_INVALID, "unknown algo %d", p->algo);
+  if (chunk && bwd_fixed(p))
+    return fail(COROPE_ERR_UNSUPPORTED,
+                "COROPE_BWD_DETERMINISTIC is not available for query chunks (their "
+                "accumulators are the caller's fp32 dk_accum / dv_accum)");
   return COROPE_OK;
 }
 
@@ -378,19 +392,24 @@ static int bwd_common(const corope_bwd_params_t* p, corope_stream_t stream,
     a.dv32 = chunk->dv_accum;
     a.acc_chunk = chunk->accum_chunk_rows;
   } else {
+    // fp32, or 64-bit fixed-point sums (deterministic)
+    a.fixed = bwd_fixed(p) ? 1 : 0;
+    const size_t acc = align256(kv * (a.fixed ? 8 : 4));
     a.dk32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4) + coef);
-    a.dv32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4) + coef + align256(kv * 4));
+    a.dv32 = reinterpret_cast<float*>(ws + 2 * align256(rows * 4) + coef + acc);
   }
 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int algo = bwd_algo(p);
   const bool tc_ok = tc_bwd_supported(a, p->dtype);
-  if (p->algo == COROPE_ALGO_TENSOR && !tc_ok)
+  if (algo == COROPE_ALGO_TENSOR && !tc_ok)
     return fail(COROPE_ERR_UNSUPPORTED,
-                "tensor-core backward needs bf16/f16, head_dim 64 or 128 and 16-byte aligned rows");
+                "tensor-core backward needs bf16/f16, head_dim 64 or 128, theta >= 1 and "
+                "16-byte aligned rows");
   cudaError_t e = cudaSuccess;
-  if (!chunk) e = cudaMemsetAsync(a.dk32, 0, 2 * align256(kv * 4), st);
+  if (!chunk) e = cudaMemsetAsync(a.dk32, 0, 2 * align256(kv * (a.fixed ? 8 : 4)), st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
-  if (p->algo != COROPE_ALGO_EXACT && tc_ok) {
+  if (algo != COROPE_ALGO_EXACT && tc_ok) {
     e = bwd_pre_launch(a, p->dtype, st);
     // [minimum][panels, when they fit][hand-off region: the rest]
     size_t base = need;

@@ -382,10 +382,11 @@ exact_bwd_kernel(BwdArgs args) {
         for (int i = 0; i < NP2; ++i) {
           const int p = i * TPK + sub2;
           if (p < P) {
-            atomicAdd(args.dk32 + row + 2 * p, dkp[i].x);
-            atomicAdd(args.dk32 + row + 2 * p + 1, dkp[i].y);
-            atomicAdd(args.dv32 + row + 2 * p, dvp[i].x);
-            atomicAdd(args.dv32 + row + 2 * p + 1, dvp[i].y);
+            const bool fixed = args.fixed != 0;
+            acc_add(args.dk32, row + 2 * p, dkp[i].x, fixed);
+            acc_add(args.dk32, row + 2 * p + 1, dkp[i].y, fixed);
+            acc_add(args.dv32, row + 2 * p, dvp[i].x, fixed);
+            acc_add(args.dv32, row + 2 * p + 1, dvp[i].y, fixed);
           }
         }
       }
@@ -414,7 +415,16 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) 
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// fp32 dk/dv accumulators -> output dtype and strides.  VEC: 16-bit outputs
+// Four consecutive fixed-point accumulator elements (acc_add) from i, a
+// multiple of 4: two 16-byte loads.
+__device__ __forceinline__ float4 fix4(const float* base, int64_t i) {
+  const longlong2* p = reinterpret_cast<const longlong2*>(base) + i / 2;
+  const longlong2 a = p[0], b = p[1];
+  return make_float4(__ll2float_rn(a.x) * kFixUnit, __ll2float_rn(a.y) * kFixUnit,
+                     __ll2float_rn(b.x) * kFixUnit, __ll2float_rn(b.y) * kFixUnit);
+}
+
+// fp32 (or fixed-point) dk/dv accumulators -> output dtype and strides.  VEC: 16-bit outputs
 // with 16-byte aligned rows and D a multiple of 8 -- each thread converts 8
 // consecutive elements (two 16-byte loads per accumulator, one 16-byte store
 // per output) and derives the row once for them.
@@ -430,9 +440,15 @@ __global__ void exact_bwd_post_kernel(BwdArgs args) {
       const int j = (int)(r % args.Sk);
       const int64_t bh = r / args.Sk;
       const int hk = (int)(bh % args.Hkv), b = (int)(bh / args.Hkv);
-      const float4* k4 = reinterpret_cast<const float4*>(args.dk32 + g * 8);
-      const float4* v4 = reinterpret_cast<const float4*>(args.dv32 + g * 8);
-      const float4 ka = k4[0], kb = k4[1], va = v4[0], vb = v4[1];
+      float4 ka, kb, va, vb;
+      if (args.fixed) {
+        ka = fix4(args.dk32, g * 8); kb = fix4(args.dk32, g * 8 + 4);
+        va = fix4(args.dv32, g * 8); vb = fix4(args.dv32, g * 8 + 4);
+      } else {
+        const float4* k4 = reinterpret_cast<const float4*>(args.dk32 + g * 8);
+        const float4* v4 = reinterpret_cast<const float4*>(args.dv32 + g * 8);
+        ka = k4[0]; kb = k4[1]; va = v4[0]; vb = v4[1];
+      }
       uint4 ko, vo;
       ko.x = pack2<T>(ka.x, ka.y); ko.y = pack2<T>(ka.z, ka.w);
       ko.z = pack2<T>(kb.x, kb.y); ko.w = pack2<T>(kb.z, kb.w);
@@ -454,10 +470,11 @@ __global__ void exact_bwd_post_kernel(BwdArgs args) {
     r /= args.Sk;
     const int hk = r % args.Hkv;
     const int b = r / args.Hkv;
+    const bool fixed = args.fixed != 0;
     ((T*)args.dk)[b * args.dks[0] + hk * args.dks[1] + (int64_t)j * args.dks[2] + d] =
-        from_f32<T>(args.dk32[i]);
+        from_f32<T>(acc_get(args.dk32, i, fixed));
     ((T*)args.dv)[b * args.dvs[0] + hk * args.dvs[1] + (int64_t)j * args.dvs[2] + d] =
-        from_f32<T>(args.dv32[i]);
+        from_f32<T>(acc_get(args.dv32, i, fixed));
   }
 }
 

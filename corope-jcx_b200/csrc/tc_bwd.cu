@@ -105,6 +105,7 @@ struct Params {
   void* dq;              // dQ launch output, element type of q
   float *dk32, *dv32;    // accumulators [B, Hkv, Sk, D] (or the owner-major chunk layout)
   int acc_chunk;         // 0, or the chunk rows of the owner-major layout (accum_row)
+  int fixed;             // accumulators hold 64-bit fixed-point sums (acc_add)
   const float *lse, *delta, *a;  // [B, H, S]
   const float* thetas;
   const float* bias;
@@ -755,11 +756,12 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       const int d = gt;
       // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys);
       // column 8 hh + s of C^T is slot s of half hh
-      float* row0 = P.dk32 + accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + d;
+      const int64_t row0 = accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + d;
+      const bool fixed = P.fixed != 0;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = bwd_slot_key(j >> 3, j & 7);
-        if (w * kW + key < P.Sk && d < D) atomicAdd(row0 + key * D, dk[j]);
+        if (w * kW + key < P.Sk && d < D) acc_add(P.dk32, row0 + key * D, dk[j], fixed);
       }
       return true;
     };
@@ -778,11 +780,12 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       const int d = gt;
       // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys)
       const int64_t row0 = accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + d;
+      const bool fixed = P.fixed != 0;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         if (w * kW + j < P.Sk && d < D) {
-          atomicAdd(P.dv32 + row0 + j * D, __uint_as_float(g[0][j]));
-          atomicAdd(P.dk32 + row0 + j * D, __uint_as_float(g[1][j]));
+          acc_add(P.dv32, row0 + j * D, __uint_as_float(g[0][j]), fixed);
+          acc_add(P.dk32, row0 + j * D, __uint_as_float(g[1][j]), fixed);
         }
       }
       return true;
@@ -1514,11 +1517,12 @@ __global__ void __launch_bounds__(kThreads, 1) dk3_kernel(const __grid_constant_
       mbar_arrive(&bars[k3::B_CE + bf]);
       // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys);
       // dk[8 hh + s] belongs to slot s of half hh
-      float* row0 = P.dk32 + accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + gt;
+      const int64_t row0 = accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + gt;
+      const bool fixed = P.fixed != 0;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = bwd_slot_key(j >> 3, j & 7);
-        if (w * kW + key < P.Sk && gt < D) atomicAdd(row0 + key * D, dk[j]);
+        if (w * kW + key < P.Sk && gt < D) acc_add(P.dk32, row0 + key * D, dk[j], fixed);
       }
     }
     __syncwarp();
@@ -1863,6 +1867,7 @@ cudaError_t tc_bwd_launch(const BwdArgs& a, int dtype, cudaStream_t st, void* ha
   p.dq = a.dq;
   p.dk32 = a.dk32;
   p.dv32 = a.dv32;
+  p.fixed = a.fixed;
   p.acc_chunk = a.acc_chunk;
   p.lse = a.lse;
   p.delta = a.delta;

@@ -51,6 +51,16 @@ typedef enum {
   COROPE_ALGO_TENSOR = 2
 } corope_algo_t;
 
+/* Backward only: OR'd into corope_bwd_params_t.algo, dk and dv are summed in
+ * 64-bit fixed point (each contribution rounded to a multiple of 2^-36, sums
+ * below 2^27 in magnitude) instead of with fp32 atomics, so that the same
+ * inputs give bit-identical dk / dv from call to call (dq is deterministic
+ * either way).  The dk / dv accumulators of the minimum workspace double in
+ * size; the chunk entry points answer COROPE_ERR_UNSUPPORTED.  The reference
+ * has no such mode: its backward adds dk / dv with fp32 atomics as well
+ * (CoROPE/co_rope_backward.py:104-110). */
+#define COROPE_BWD_DETERMINISTIC 0x100
+
 typedef enum {
   COROPE_OK = 0,
   COROPE_ERR_INVALID = 1,     /* bad argument (shape, stride, pointer) */

@@ -186,6 +186,42 @@ def test_chunk_argument_checks_without_gpu():
     assert hi - lo - panels == 4 * ((256 + 127) // 16 + 1) * 4096
 
 
+def test_deterministic_flag_without_gpu():
+    """COROPE_BWD_DETERMINISTIC (OR'd into algo): 64-bit dk / dv accumulators
+    in the minimum workspace (twice the fp32 size), any base algo, refused
+    for query chunks before any device work; theta < 1 (exact kernels only)
+    asks for no tensor-core workspace."""
+    lib = _lib.load_library()
+    hdr = open(HEADER).read()
+    assert "#define COROPE_BWD_DETERMINISTIC 0x100" in hdr
+    assert _lib.BWD_DETERMINISTIC == 0x100
+    kv = 1 * 2 * 128 * 64
+    for algo in (_lib.ALGO_AUTO, _lib.ALGO_EXACT, _lib.ALGO_TENSOR):
+        p = _bwd_params(algo=algo)
+        d = _bwd_params(algo=algo | _lib.BWD_DETERMINISTIC)
+        lo, lo_det = (lib.corope_bwd_min_workspace_bytes(ctypes.byref(x)) for x in (p, d))
+        assert lo_det - lo == 2 * kv * 4
+        hi, hi_det = (lib.corope_bwd_workspace_bytes(ctypes.byref(x)) for x in (p, d))
+        assert hi_det - hi == 2 * kv * 4
+        # the workspace check still answers first (no device touched)
+        assert lib.corope_bwd(ctypes.byref(d), None) == _lib.ERR_WORKSPACE
+    bad = _bwd_params(algo=9 | _lib.BWD_DETERMINISTIC)
+    assert lib.corope_bwd(ctypes.byref(bad), None) == _lib.ERR_INVALID
+    c = _lib.ChunkParams()
+    c.q_row0, c.kv_len = 0, 128
+    d = _bwd_params(algo=_lib.BWD_DETERMINISTIC)
+    acc = _lib.ChunkParams.from_buffer_copy(c)
+    acc.dk_accum = acc.dv_accum = 1 << 20
+    assert lib.corope_bwd_chunk(ctypes.byref(d), ctypes.byref(acc), None) == _lib.ERR_UNSUPPORTED
+    assert b"DETERMINISTIC" in lib.corope_last_error()
+    # theta < 1: no coefficient table, panels or hand-off region
+    p = _bwd_params()
+    p.theta = 0.5
+    assert lib.corope_bwd_panel_bytes(ctypes.byref(p)) == 0
+    assert lib.corope_bwd_min_workspace_bytes(ctypes.byref(p)) == \
+        lib.corope_bwd_workspace_bytes(ctypes.byref(p)) == 2 * 2 * 128 * 4 + 2 * kv * 4
+
+
 def test_size_queries_accept_null():
     """Every size query answers 0 for a NULL params / chunk instead of
     dereferencing it."""

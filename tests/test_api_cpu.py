@@ -43,7 +43,7 @@ def test_backward_accepts_both_conventions(monkeypatch):
     bwd_mod = importlib.import_module("CoROPE.co_rope_backward")
     seen = []
 
-    def fake_run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo):
+    def fake_run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo, det=False):
         seen.append((sm_scale, theta, None if thetas is None else thetas.tolist()))
         return "dq", "dk", "dv"
 
@@ -61,6 +61,32 @@ def test_backward_accepts_both_conventions(monkeypatch):
         co_rope_backward(t, t, t, t, t, t, t, t, thetas, False, 0.25)
 
 
+def test_backward_deterministic_follows_torch_setting(monkeypatch):
+    """deterministic=None takes torch.are_deterministic_algorithms_enabled();
+    an explicit value wins, in both calling conventions."""
+    bwd_mod = importlib.import_module("CoROPE.co_rope_backward")
+    seen = []
+
+    def fake_run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo, det=False):
+        seen.append(det)
+        return "dq", "dk", "dv"
+
+    monkeypatch.setattr(bwd_mod, "_run", fake_run)
+    t = torch.zeros(1, 1, 4, 4)
+    was = torch.are_deterministic_algorithms_enabled()
+    try:
+        torch.use_deterministic_algorithms(False)
+        co_rope_backward((t,) * 7, t, 0.3, 500.0)
+        co_rope_backward((t,) * 7, t, 0.3, 500.0, deterministic=True)
+        torch.use_deterministic_algorithms(True)
+        co_rope_backward((t,) * 7, t, 0.3, 500.0)
+        co_rope_backward(t, t, t, t, t, t, t, t, None, True, 0.25)
+        co_rope_backward((t,) * 7, t, 0.3, 500.0, deterministic=False)
+    finally:
+        torch.use_deterministic_algorithms(was)
+    assert seen == [False, True, True, True, False]
+
+
 @pytest.mark.parametrize("D", [64, 128])
 def test_backward_table_base_reaches_tensor_kernels(monkeypatch, D):
     """The reference's autograd backward passes only the thetas table
@@ -70,7 +96,7 @@ def test_backward_table_base_reaches_tensor_kernels(monkeypatch, D):
     bwd_mod = importlib.import_module("CoROPE.co_rope_backward")
     seen = []
 
-    def fake_run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo):
+    def fake_run(q, k, v, o, m, l, a, do, sm_scale, theta, thetas, bias, algo, det=False):
         seen.append((theta, algo))
         return "dq", "dk", "dv"
 

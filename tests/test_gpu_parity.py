@@ -527,6 +527,51 @@ def test_query_chunk_argument_checks():
                  None, 0.125, 1e4, mqa=True, q_row0=128)
 
 
+@pytest.mark.parametrize("algo,ws,hkv,dtype", [
+    ("tensor", "auto", 4, torch.bfloat16),   # dQ kernel + dK kernel via the hand-off
+    ("tensor", "min", 4, torch.bfloat16),    # the dK side recomputed (no hand-off)
+    ("tensor", "auto", 1, torch.float16),    # 4 query heads add to each key row
+    ("exact", "auto", 4, torch.float32),
+])
+def test_deterministic_backward_is_bit_identical(algo, ws, hkv, dtype):
+    """COROPE_BWD_DETERMINISTIC: two calls give bit-identical dq, dk, dv (the
+    fp32-atomic default need not), equal to the default within rounding and
+    to the oracle within the gradient bounds."""
+    from CoROPE import _lib
+    B, H, S, D = 2, 4, 640, 64
+    (q, k, v, do), cpu = inputs(B, H, S, D, 61, dtype, hkv=hkv)
+    sm = 1 / math.sqrt(D)
+    fwd = co_rope_forward if hkv == H else co_rope_mqa_forward
+    saved, o = fwd(q, k, v, sm, algo=algo)
+    q_, k_, v_, o_, m_, l_, a_ = saved
+
+    def run(det):
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        _lib.bwd(q_, k_, v_, o_, do, m_, l_, a_, dq, dk, dv, sm, 1e4, algo=algo, workspace=ws,
+                 deterministic=det)
+        return dq, dk, dv
+
+    first = run(True)
+    second = run(True)
+    plain = run(False)
+    torch.cuda.synchronize()
+    assert _lib.take_device_error() == 0
+    for x, y in zip(first, second):
+        assert torch.equal(x, y)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    for x, y in zip(first, plain):
+        assert maxabs(x, y) < tol * max(1.0, y.abs().max().item())
+    rq, rk, rv = O.backward_dense(*cpu, sm, 1e4)
+    g_tol = 1e-3 if dtype == torch.float32 else G_MAXABS
+    for name, mine, r in zip(("dq", "dk", "dv"), first, (rq, rk, rv)):
+        assert maxabs(mine, r) < g_tol * max(1.0, r.abs().max().item()), name
+        assert rel_l2(mine, r) < REL_L2, name
+    # the public call takes the same path
+    dq, dk, dv = co_rope_backward(saved, do, sm, algo=algo, deterministic=True)
+    if ws == "auto":
+        assert torch.equal(dk, first[1]) and torch.equal(dv, first[2])
+
+
 def test_theta_below_one_and_reference_tables():
     """The tensor-core expansions assume every frequency theta_p <= 1 and take
     their coefficients from a scalar base: theta < 1 under "auto" runs the
