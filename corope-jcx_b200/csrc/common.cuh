@@ -67,27 +67,6 @@ __device__ __forceinline__ float reduce_2pi(float x) {
   return fmaf(-k, 1.9353071795864769e-3f, r);
 }
 
-// sin/cos of r in [-pi, pi] on the FMA pipe (no MUFU): Taylor series of
-// sin and cos of h = r/2 (through h^7 and h^8; |h| <= pi/2, truncation
-// below 2e-4), then the double-angle formulas sin r = 2 sin h cos h and
-// cos r = 1 - 2 sin^2 h.  Absolute error below 4e-4 -- used only where the
-// result is rounded to 16-bit floats anyway.
-__device__ __forceinline__ void sincos_poly(float r, float* s, float* c) {
-  const float h = 0.5f * r;
-  const float h2 = h * h;
-  float sp = fmaf(h2, -1.0f / 5040.0f, 1.0f / 120.0f);
-  sp = fmaf(h2, sp, -1.0f / 6.0f);
-  sp = fmaf(h2, sp, 1.0f);
-  const float sh = h * sp;
-  float cp = fmaf(h2, 1.0f / 40320.0f, -1.0f / 720.0f);
-  cp = fmaf(h2, cp, 1.0f / 24.0f);
-  cp = fmaf(h2, cp, -0.5f);
-  const float ch = fmaf(h2, cp, 1.0f);
-  const float t = sh + sh;
-  *s = t * ch;
-  *c = fmaf(-t, sh, 1.0f);
-}
-
 __device__ __forceinline__ float sigmoidf_fast(float x) {
   return 1.0f / (1.0f + __expf(-x));
 }
