@@ -422,6 +422,7 @@ def test_long_context_s32768(mode):
     p = _lib.BwdParams()
     p.batch, p.heads, p.kv_heads, p.seq_len, p.head_dim = B, H, H, S, D
     p.dtype, p.algo = _lib._dtype_code(q), _lib.algo_code("tensor")
+    p.theta, p.sm_scale = theta, sm  # the sizes depend on them (theta < 1: exact kernels)
     lib = _lib.load_library()
     lo = lib.corope_bwd_min_workspace_bytes(ctypes.byref(p))
     hi = lib.corope_bwd_workspace_bytes(ctypes.byref(p))
