@@ -265,7 +265,9 @@ __device__ __forceinline__ float2 unpack_cs(uint32_t v) {
 
 // KMT (dQ launch only): the K^(m) operands come from precomputed panels in
 // global memory (tcx::panel_kernel) by TMA instead of warps 12-15.
-template <typename T, int D, int MODE, bool HAS_BIAS, int KM, bool KMT>
+// FIX: the dk / dv accumulators hold 64-bit fixed-point sums (acc_add); a
+// template parameter so that the default fp32-atomic path carries no branch
+template <typename T, int D, int MODE, bool HAS_BIAS, int KM, bool KMT, bool FIX>
 __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant__ Params P) {
   static_assert(!KMT || MODE == MODE_DQ, "panels feed the dQ launch only");
   using E = ElemTraits<T>;
@@ -757,7 +759,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys);
       // column 8 hh + s of C^T is slot s of half hh
       const int64_t row0 = accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + d;
-      const bool fixed = P.fixed != 0;
+      constexpr bool fixed = FIX;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = bwd_slot_key(j >> 3, j & 7);
@@ -780,7 +782,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(const __grid_constant_
       const int d = gt;
       // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys)
       const int64_t row0 = accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + d;
-      const bool fixed = P.fixed != 0;
+      constexpr bool fixed = FIX;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         if (w * kW + j < P.Sk && d < D) {
@@ -1305,7 +1307,7 @@ constexpr uint32_t C0 = 0, C1 = 256, SG = 384;
 static_assert(SG + 32 <= 512, "tmem");
 }  // namespace k3
 
-template <typename T, int D>
+template <typename T, int D, bool FIX>
 __global__ void __launch_bounds__(kThreads, 1) dk3_kernel(const __grid_constant__ Params P) {
   using E = ElemTraits<T>;
   using namespace sm100;
@@ -1518,7 +1520,7 @@ __global__ void __launch_bounds__(kThreads, 1) dk3_kernel(const __grid_constant_
       // a window's 16 keys lie in one accumulator chunk (chunks are multiples of 16 keys);
       // dk[8 hh + s] belongs to slot s of half hh
       const int64_t row0 = accum_row(w * kW, bhk, BHkv, P.Sk, P.acc_chunk) * D + gt;
-      const bool fixed = P.fixed != 0;
+      constexpr bool fixed = FIX;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int key = bwd_slot_key(j >> 3, j & 7);
@@ -1691,7 +1693,8 @@ static int plan(Params& p) {
 
 template <typename T, int D, int MODE, bool HAS_BIAS, int KM, bool KMT>
 static cudaError_t launch_k(const Params& p, int smem, dim3 grid, cudaStream_t st) {
-  auto kern = bwd_kernel<T, D, MODE, HAS_BIAS, KM, KMT>;
+  auto kern = p.fixed ? bwd_kernel<T, D, MODE, HAS_BIAS, KM, KMT, true>
+                      : bwd_kernel<T, D, MODE, HAS_BIAS, KM, KMT, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kSmemLimit);
   if (e != cudaSuccess) return e;
@@ -1722,7 +1725,7 @@ static cudaError_t launch_dk3(Params& p, int S, int nbh, cudaStream_t st, float 
   tcx::fill_coefficients<kMB>(p.coef, p.nrow, D, theta, sm_scale);
   const int smem = k3::TOTAL + 1024;
   dim3 grid((S + kBM - 1) / kBM, nbh);
-  auto kern = dk3_kernel<T, D>;
+  auto kern = p.fixed ? dk3_kernel<T, D, true> : dk3_kernel<T, D, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   kern<<<grid, kThreads, smem, st>>>(p);
