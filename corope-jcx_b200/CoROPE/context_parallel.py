@@ -25,6 +25,8 @@ cuts a full tensor the same way); m, l, a are ``[B, H, 2C]``.
 """
 from __future__ import annotations
 
+import warnings
+
 import torch
 import torch.distributed as dist
 
@@ -160,7 +162,20 @@ def co_rope_backward_cp(saved, do, sm_scale=None, theta=10000.0, group=None, alg
     K and V all-gathered, every local query chunk adds its key gradients to
     fp32 accumulators over the whole sequence in the owner-major layout, and
     one reduce-scatter per half of that layout hands each rank the sums of its
-    own two chunks -- no reordering copy of the accumulators."""
+    own two chunks -- no reordering copy of the accumulators.
+
+    The chunk kernels add key gradients with fp32 atomics, so there is no
+    deterministic variant: with ``torch.use_deterministic_algorithms(True)``
+    this raises (or warns, with ``warn_only=True``), as torch's own
+    nondeterministic operations do."""
+    if torch.are_deterministic_algorithms_enabled():
+        msg = ("co_rope_backward_cp has no deterministic implementation (its key gradients are "
+               "summed with fp32 atomics); use co_rope_backward(deterministic=True) on whole "
+               "sequences")
+        if torch.is_deterministic_algorithms_warn_only_enabled():
+            warnings.warn(msg)
+        else:
+            raise RuntimeError(msg)
     kern = kernels or _Kernels
     q, k, v, o, m, l, a = saved
     rank, world = dist.get_rank(group), dist.get_world_size(group)

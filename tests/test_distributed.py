@@ -171,3 +171,22 @@ def test_sequence_sharded_forward_backward_gloo():
         assert out["roundtrip"] and out["groups"] == 2
         assert out["o"] < 1e-12 and out["a"] < 1e-6 and out["dq"] < 1e-12
         assert out["dk"] < 1e-6 and out["dv"] < 1e-6
+
+
+def test_sequence_sharded_backward_refuses_deterministic_mode():
+    """co_rope_backward_cp sums key gradients with fp32 atomics: under
+    torch.use_deterministic_algorithms(True) it raises before any collective,
+    and with warn_only=True it warns and goes on."""
+    from CoROPE import context_parallel as cp
+    was, only = (torch.are_deterministic_algorithms_enabled(),
+                 torch.is_deterministic_algorithms_warn_only_enabled())
+    try:
+        torch.use_deterministic_algorithms(True)
+        with pytest.raises(RuntimeError, match="deterministic"):
+            cp.co_rope_backward_cp((None,) * 7, None)
+        torch.use_deterministic_algorithms(True, warn_only=True)
+        with pytest.warns(UserWarning, match="deterministic"):
+            with pytest.raises(Exception):  # no process group: fails after the warning
+                cp.co_rope_backward_cp((None,) * 7, None)
+    finally:
+        torch.use_deterministic_algorithms(was, warn_only=only)
