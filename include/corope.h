@@ -141,7 +141,8 @@ size_t corope_bwd_workspace_bytes(const corope_bwd_params_t *p);
 
 /* Smallest workspace corope_bwd accepts: delta and lse rows, the tensor-core
  * path's expansion coefficients (128 KiB, written per call) and fp32 dk / dv
- * accumulators (the dK kernel then recomputes the per-(row, key) results).
+ * accumulators, 64-bit with COROPE_BWD_DETERMINISTIC (the dK kernel then
+ * recomputes the per-(row, key) results).
  * No counterpart in the reference. */
 size_t corope_bwd_min_workspace_bytes(const corope_bwd_params_t *p);
 
