@@ -74,6 +74,8 @@ template <> struct ElemTraits<__nv_bfloat16> {
   static constexpr bool kBf16 = true;
   __device__ static float lo(uint32_t x) { return __uint_as_float(x << 16); }
   __device__ static float hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
+  // -hi(x): the sign flip folded into the same logic operation
+  __device__ static float nhi(uint32_t x) { return __uint_as_float((x & 0xffff0000u) ^ 0x80000000u); }
   __device__ static uint32_t pack(float a, float b) { return sm100::pack_bf16(a, b); }
 };
 template <> struct ElemTraits<__half> {
@@ -84,8 +86,48 @@ template <> struct ElemTraits<__half> {
   __device__ static float hi(uint32_t x) {
     return __half2float(__ushort_as_half((unsigned short)(x >> 16)));
   }
+  __device__ static float nhi(uint32_t x) {
+    return __half2float(__ushort_as_half((unsigned short)((x >> 16) ^ 0x8000u)));
+  }
   __device__ static uint32_t pack(float a, float b) { return sm100::pack_f16(a, b); }
 };
+
+// Angles a * th[i] of 16 rotation pairs, two per packed fp32x2 multiply (the
+// same single rounding as a scalar product).
+__device__ __forceinline__ void angles16(float a, const float (&th)[16], float (&rr)[16]) {
+  const float2 a2 = make_float2(a, a);
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    const float2 x = __fmul2_rn(a2, make_float2(th[i], th[i + 1]));
+    rr[i] = x.x;
+    rr[i + 1] = x.y;
+  }
+}
+
+// The A operand's rotation of 16 pairs: pair i of the row, the 16-bit word
+// (q_e, q_o) at word i of qv, becomes (q_e c - q_o s, q_e s + q_o c) with
+// s, c = sn[i], cs[i], rounded to 16 bits.  Two pairs per packed fp32x2
+// multiply and FMA (each component one product then one FMA, as the scalar
+// form rounds); -q_o comes from its own unpack, so no operand is negated.
+template <typename E>
+__device__ __forceinline__ void rotate16(const uint4 (&qv)[4], const float (&sn)[16],
+                                         const float (&cs)[16], uint32_t (&o)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    const uint4& v = qv[i >> 2];
+    const uint32_t w0 = (i & 3) == 0 ? v.x : v.z;
+    const uint32_t w1 = (i & 3) == 0 ? v.y : v.w;
+    const float2 qe = make_float2(E::lo(w0), E::lo(w1));
+    const float2 qo = make_float2(E::hi(w0), E::hi(w1));
+    const float2 nqo = make_float2(E::nhi(w0), E::nhi(w1));
+    const float2 c = make_float2(cs[i], cs[i + 1]);
+    const float2 sv = make_float2(sn[i], sn[i + 1]);
+    const float2 x = __ffma2_rn(nqo, sv, __fmul2_rn(qe, c));
+    const float2 y = __ffma2_rn(qo, c, __fmul2_rn(qe, sv));
+    o[i] = E::pack(x.x, y.x);
+    o[i + 1] = E::pack(x.y, y.y);
+  }
+}
 
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + __expf(-x)); }
 

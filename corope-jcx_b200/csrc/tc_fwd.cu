@@ -156,6 +156,8 @@ enum {
 using tcx::ElemTraits;
 using tcx::sigmoid_f;
 using tcx::slot_key;
+using tcx::angles16;
+using tcx::rotate16;
 
 // Gates of one window for row t (keys j0 .. j0 + 15, descending): the
 // in-window positions uu[jj] = (gate sum of the window's keys after jj) / c0
@@ -547,23 +549,15 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(const __grid_constant_
           th[4 * cc] = t4.x; th[4 * cc + 1] = t4.y; th[4 * cc + 2] = t4.z; th[4 * cc + 3] = t4.w;
         }
         float rr[16], sn[16], cs[16];
-        if (mufu_reduce) {
+        angles16(base, th, rr);
+        if (!mufu_reduce) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) rr[i] = base * th[i];
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) rr[i] = reduce_2pi(base * th[i]);
+          for (int i = 0; i < 16; ++i) rr[i] = reduce_2pi(rr[i]);
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) __sincosf(rr[i], &sn[i], &cs[i]);
         uint32_t regs[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint32_t w32 = (i & 3) == 0 ? qv[i >> 2].x : (i & 3) == 1 ? qv[i >> 2].y
-                             : (i & 3) == 2 ? qv[i >> 2].z : qv[i >> 2].w;
-          const float qe = E::lo(w32), qo = E::hi(w32);
-          regs[i] = E::pack(qe * cs[i] - qo * sn[i], qe * sn[i] + qo * cs[i]);
-        }
+        rotate16<E>(qv, sn, cs, regs);
         tmem_st16(lane_base + av_col + p0, regs);
       }
       tmem_wait_st();
